@@ -1,0 +1,232 @@
+// tf_device.cuh -- device building blocks shared by the quantized-expert kernels.
+//
+// Weight format (TurboFieldfare MLX-affine, Quantization.swift:35-45,300-349):
+//   int4 row of K values = K/2 bytes, element k in byte k/2, low nibble = even k;
+//   int8 row = K bytes; per group of 64 along K one scale and one bias
+//   (BF16 in the reference format, fp16 optionally).
+//   w[k] = q[k] * scale[k/64] + bias[k/64].
+//
+// Compute scheme (all kernels): a warp owns a 16-row tile of weights that a
+// bulk asynchronous copy (cp.async.bulk, the TMA engine) has placed in shared
+// memory.  Codes are turned into exact fp16 integers (q in 0..255 is exact in
+// fp16) and multiplied with fp16 activations on the tensor cores with
+// mma.sync m16n8k16 (fp32 accumulate).  Each 64-wide group is reduced into a
+// fresh accumulator and then folded in fp32 as
+//   acc += scale_g * sum_k(q_k x_k) + bias_g * sum_k(x_k),
+// the same affine factoring as dequant_int4.metal:126-173.  The N=8 columns
+// of the MMA carry up to 8 tokens, so one code path serves batch-1 decode and
+// small grouped batches.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+namespace tf {
+
+constexpr int kGroup = 64;
+constexpr int kWarps = 8;             // consumer warps per CTA
+constexpr int kRowsPerTile = 16;      // MMA M
+constexpr int kMaxTok = 8;            // MMA N
+// Padded shared-memory row strides (bytes).  int4 tiles are read with 8-byte
+// loads in half-warps of 4 rows x 4 lanes: a stride of 8 (mod 32) words puts
+// those 4 rows on disjoint banks.  int8 tiles are read with 16-byte loads in
+// quarter-warps of 2 rows: 16 (mod 32) words.
+constexpr int kStageStride4 = 416;
+constexpr int kStageStride8 = 448;
+constexpr int kStageBytes = kRowsPerTile * kStageStride8;
+constexpr int kChunkGroups4 = 11;     // groups per unit, int4 (352 B per row)
+constexpr int kChunkGroups8 = 6;      // groups per unit, int8 (384 B per row)
+constexpr uint32_t kSpinLimit = 1u << 26;  // bounded mbarrier wait (error flag after)
+
+// Error bits written to the context's device status word.
+enum : uint32_t { kErrMbarTimeout = 1u, kErrBadExpert = 2u };
+
+__device__ __forceinline__ float scale_to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float scale_to_float(__half v) { return __half2float(v); }
+
+template <typename ST>
+__device__ __forceinline__ float ldg_scale(const ST* p) {
+    return scale_to_float(__ldg(p));
+}
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: returns false (and records the error) if the phase never
+// completes; the caller then skips the work instead of hanging the GPU.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t* err) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    if (err) atomicOr(err, kErrMbarTimeout);
+    return false;
+}
+
+// 1-D bulk copy global -> shared, completion counted on an mbarrier.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t magic) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(magic));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t hsub2_u(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+__device__ __forceinline__ void mma16816(float c[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ---------------------------------------------------------------------------
+// Exact code -> fp16 conversion.
+// Activations are staged in "octet pair" order: for every 8 consecutive k
+// (an octet) the words are  P_i = half2(x[8q+i], x[8q+i+4]), i = 0..3.
+// dq4 produces the same pairing from one 32-bit word of 8 nibbles, so the MMA
+// sees A and B in the same (permuted) k order and the products are exact.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void dq4(uint32_t w, uint32_t p[4]) {
+    constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024.0 in both halves
+    constexpr uint32_t k1024 = 0x64006400u;
+    constexpr uint32_t kSixteenth = 0x2C002C00u;  // 1/16
+    constexpr uint32_t kNeg64 = 0xD400D400u;      // -64
+    const uint32_t w8 = w >> 8;
+    p[0] = hsub2_u(lop3_and_or(w, 0x000F000Fu, kMagic), k1024);                // k0,k4
+    p[1] = hfma2_u(lop3_and_or(w, 0x00F000F0u, kMagic), kSixteenth, kNeg64);   // k1,k5
+    p[2] = hsub2_u(lop3_and_or(w8, 0x000F000Fu, kMagic), k1024);               // k2,k6
+    p[3] = hfma2_u(lop3_and_or(w8, 0x00F000F0u, kMagic), kSixteenth, kNeg64);  // k3,k7
+}
+
+// One octet of int8 codes (w0 = k0..3, w1 = k4..7) -> P0..P3.
+__device__ __forceinline__ void dq8(uint32_t w0, uint32_t w1, uint32_t p[4]) {
+    constexpr uint32_t kMagic = 0x64006400u;
+    constexpr uint32_t k1024 = 0x64006400u;
+    // prmt selector nibbles: byte i of w0 -> out byte 0, byte i of w1 -> out byte 2.
+    p[0] = hsub2_u(lop3_and_or(__byte_perm(w0, w1, 0x0400u), 0x00FF00FFu, kMagic), k1024);
+    p[1] = hsub2_u(lop3_and_or(__byte_perm(w0, w1, 0x0501u), 0x00FF00FFu, kMagic), k1024);
+    p[2] = hsub2_u(lop3_and_or(__byte_perm(w0, w1, 0x0602u), 0x00FF00FFu, kMagic), k1024);
+    p[3] = hsub2_u(lop3_and_or(__byte_perm(w0, w1, 0x0703u), 0x00FF00FFu, kMagic), k1024);
+}
+
+// ---------------------------------------------------------------------------
+// Activation staging: x (fp16, K values) -> octet-pair layout in shared
+// memory (K/2 words per token, token stride padded) + per-group sums (fp32).
+// ---------------------------------------------------------------------------
+__host__ __device__ constexpr int x_words_stride(int K) {
+    // K/2 words per token, padded to 4 (mod 32) words: a quarter-warp reads
+    // two tokens x 4 lanes x 16 B, which then land on disjoint banks.
+    return ((K / 2 + 31) / 32) * 32 + 4;
+}
+
+// Cooperative staging by `nthreads` threads starting at `tid`.
+// xs: [ntok][x_words_stride] words; xsum: [ntok][K/64] floats.
+// Token rows >= ntok are not touched (callers mask by token count).
+__device__ __forceinline__ void stage_x(const __half* __restrict__ x, int x_row_stride, int ntok, int K,
+                                        uint32_t* xs, float* xsum, int tid, int nthreads) {
+    const int octets = K / 8;
+    const int ws = x_words_stride(K);
+    for (int i = tid; i < ntok * octets; i += nthreads) {
+        const int t = i / octets, q = i % octets;
+        const __half* src = x + (size_t)t * x_row_stride + q * 8;
+        uint4 raw = *reinterpret_cast<const uint4*>(src);  // 16 B aligned: x rows are 16 B aligned
+        const __half* h = reinterpret_cast<const __half*>(&raw);
+        uint32_t* dst = xs + t * ws + q * 4;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            __half2 p = __halves2half2(h[j], h[j + 4]);
+            dst[j] = *reinterpret_cast<uint32_t*>(&p);
+        }
+    }
+    const int ng = K / kGroup;
+    for (int i = tid; i < ntok * ng; i += nthreads) {
+        const int t = i / ng, g = i % ng;
+        const __half* src = x + (size_t)t * x_row_stride + g * kGroup;
+        float s = 0.f;
+        for (int k = 0; k < kGroup; ++k) s += __half2float(src[k]);
+        xsum[t * ng + g] = s;
+    }
+}
+
+// Scalar variant for activations that are not 16-byte aligned.
+__device__ __forceinline__ void stage_x_scalar(const __half* __restrict__ x, int x_row_stride, int ntok, int K,
+                                               uint32_t* xs, float* xsum, int tid, int nthreads) {
+    const int octets = K / 8;
+    const int ws = x_words_stride(K);
+    for (int i = tid; i < ntok * octets; i += nthreads) {
+        const int t = i / octets, q = i % octets;
+        const __half* src = x + (size_t)t * x_row_stride + q * 8;
+        uint32_t* dst = xs + t * ws + q * 4;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            __half2 p = __halves2half2(src[j], src[j + 4]);
+            dst[j] = *reinterpret_cast<uint32_t*>(&p);
+        }
+    }
+    const int ng = K / kGroup;
+    for (int i = tid; i < ntok * ng; i += nthreads) {
+        const int t = i / ng, g = i % ng;
+        const __half* src = x + (size_t)t * x_row_stride + g * kGroup;
+        float s = 0.f;
+        for (int k = 0; k < kGroup; ++k) s += __half2float(src[k]);
+        xsum[t * ng + g] = s;
+    }
+}
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+    // gelu_pytorch_tanh with the inner clamp of moe.metal:53-60.
+    const float x3 = x * x * x;
+    float inner = 0.7978845608028654f * (x + 0.044715f * x3);
+    inner = fminf(fmaxf(inner, -20.0f), 20.0f);
+    return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+}  // namespace tf

@@ -1,0 +1,188 @@
+/*
+ * tfcuda.h -- C ABI of the B200 (sm_100a) quantized-expert hot path for
+ * TurboFieldfare (Gemma 4 26B-A4B MoE).
+ *
+ * Every entry point ENQUEUES work on the caller's CUDA stream (passed as
+ * `void* stream`, a cudaStream_t; NULL = legacy default stream) and returns
+ * immediately; none synchronises, none allocates device memory, so every call
+ * is usable inside CUDA-graph capture once the context exists.  This mirrors
+ * the reference's encoder style, where each `encode(commandBuffer:...)`
+ * appends to a caller-owned MTLCommandBuffer
+ * (Sources/TurboFieldfare/Kernels/Quant/DequantInt4GEMV.swift:84-127).
+ *
+ * Buffers are device pointers owned by the caller (byte offsets folded in).
+ * Dimensions are uint32_t.  Weight layout is the reference's MLX-affine
+ * format: codes packed LSB-first (int4: element k in byte k/2, low nibble =
+ * even k), one scale and one bias per 64 elements along a row, stored as BF16
+ * (TF_SCALE_BF16, the reference format) or fp16 (TF_SCALE_F16).  Activations
+ * and outputs are fp16.
+ *
+ * Errors: a non-zero tf_status, never an abort.  The reference traps on
+ * contract violations (precondition) and throws Swift errors for shape
+ * mismatches; here both become status codes with a message readable through
+ * tf_context_last_error().
+ */
+#ifndef TFCUDA_H
+#define TFCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define TF_API __attribute__((visibility("default")))
+#else
+#define TF_API
+#endif
+
+#define TFCUDA_VERSION_MAJOR 0
+#define TFCUDA_VERSION_MINOR 1
+
+typedef enum {
+    TF_OK = 0,
+    TF_ERR_INVALID_ARG = 1,       /* null pointer, zero or inconsistent dims */
+    TF_ERR_MISALIGNED = 2,        /* pointer alignment the kernel cannot accept */
+    TF_ERR_UNSUPPORTED_SHAPE = 3, /* N % 64 != 0, top_k / num_experts limits, ... */
+    TF_ERR_CUDA = 4,              /* CUDA runtime error (launch, attribute, copy) */
+    TF_ERR_NCCL = 5,              /* NCCL error in the expert-parallel layer */
+    TF_ERR_TIMEOUT = 6,           /* a bounded device-side wait gave up */
+    TF_ERR_NO_DEVICE = 7,         /* no usable sm_100 device */
+    TF_ERR_GROUPING = 8           /* route metadata rejected (see tf_grouping_error) */
+} tf_status;
+
+typedef enum { TF_SCALE_BF16 = 0, TF_SCALE_F16 = 1 } tf_scale_type;
+
+typedef struct tf_context tf_context;
+
+/* ---- library / context ------------------------------------------------- */
+TF_API const char* tf_status_string(tf_status s);
+TF_API void tf_version(int* major, int* minor);
+
+/* Replaces MetalContext (Sources/TurboFieldfare/Infrastructure/Metal/MetalContext.swift:98-210):
+ * binds `device`, sizes the small device workspace (router logits, selection
+ * ticket, device error word, decode activations) once. */
+TF_API tf_status tf_context_create(int device, tf_context** out);
+TF_API void tf_context_destroy(tf_context* ctx);
+TF_API const char* tf_context_last_error(const tf_context* ctx);
+/* Synchronises `stream`, returns the device error bits raised by bounded
+ * waits or out-of-range expert ids since the last call (and clears them).
+ * TF_ERR_TIMEOUT when a wait gave up. */
+TF_API tf_status tf_context_check_device(tf_context* ctx, void* stream, uint32_t* flags_out);
+
+/* ---- dense affine GEMV --------------------------------------------------- */
+/* DequantInt4GEMV.encode / encodeTgx (Sources/TurboFieldfare/Kernels/Quant/DequantInt4GEMV.swift:84-180):
+ * y[m] = sum_n (q*s+b)[m][n] * x[n] with fp32 accumulation, fp16 out.
+ * W: m rows of n/2 bytes; scales/biases: m rows of n/64.  n % 64 == 0.
+ * W must be at least 2-byte aligned (16-byte aligned takes the bulk-copy path). */
+TF_API tf_status tf_int4_gemv(tf_context* ctx, const void* W, const void* scales, const void* biases,
+                       const void* x, void* y, uint32_t m, uint32_t n, tf_scale_type st,
+                       void* stream);
+
+/* DequantInt8GEMV.encode (Sources/TurboFieldfare/Kernels/Quant/DequantInt8GEMV.swift:50-81). */
+TF_API tf_status tf_int8_gemv(tf_context* ctx, const void* W, const void* scales, const void* biases,
+                       const void* x, void* y, uint32_t m, uint32_t n, tf_scale_type st,
+                       void* stream);
+
+/* Batched form of the two above: `batch` matrices at W + i*w_stride_bytes
+ * (scales/biases at + i*sb_stride_elems elements), a shared activation block
+ * of `ntok` (1..8) tokens x[t*x_row_stride + k], outputs
+ * y[i*y_batch_stride + t*y_row_stride + row].  bits in {4, 8}.
+ * (No single reference counterpart: it is the GemvBench loop,
+ * Tests/TurboFieldfare/Core/Kernels/Quant/GemvBench.swift:20-107, and the
+ * T-token repeated-GEMV path, PrefillSharedExpert.swift:43-58, in one launch.) */
+TF_API tf_status tf_affine_gemv_batched(tf_context* ctx, uint32_t bits, const void* W, const void* scales,
+                                 const void* biases, uint64_t w_stride_bytes, uint64_t sb_stride_elems,
+                                 uint32_t batch, const void* x, uint32_t ntok, uint32_t x_row_stride,
+                                 void* y, uint32_t y_row_stride, uint64_t y_batch_stride, uint32_t m,
+                                 uint32_t n, tf_scale_type st, void* stream);
+
+/* ---- router ------------------------------------------------------------- */
+/* MoE.encodeRouterGemma4 (Sources/TurboFieldfare/Kernels/MoE/MoE.swift:147-197), both
+ * encoders fused into one launch:
+ *   logits[e] = sum_g s*sum(q*x~) + b*sum(x~),  x~_i = float(hidden_i)*float(eff_scale_i)
+ *   top_k by logit (ties -> lower id), softmax over the k, w = half(p * per_expert_scale[e]).
+ * W: int8 [num_experts][d]; eff_scale [d], per_expert_scale [num_experts] are BF16.
+ * out_indices uint32[top_k], out_weights fp16[top_k] (device).
+ * Limits: num_experts <= 256, 1 <= top_k <= 32, d % 64 == 0. */
+TF_API tf_status tf_router_topk(tf_context* ctx, const void* W, const void* scales, const void* biases,
+                         const void* hidden, const void* eff_scale, const void* per_expert_scale,
+                         void* out_indices, void* out_weights, uint32_t num_experts, uint32_t d,
+                         uint32_t top_k, tf_scale_type st, void* stream);
+
+/* ---- decode MoE ---------------------------------------------------------- */
+/* MoEExpertOffsets (Sources/TurboFieldfare/Kernels/MoE/MoE.swift:4-29): byte offsets of
+ * the nine sub-tensors inside one expert blob, identical for all experts. */
+typedef struct {
+    uint32_t gate_w, gate_s, gate_b, up_w, up_s, up_b, down_w, down_s, down_b;
+} tf_expert_offsets;
+
+/* Routed experts are addressed either as an HBM-resident pool
+ * (expert e at pool + e*expert_stride, ids read on the device from
+ * `expert_ids`, uint32[top_k]) or, when expert_ids == NULL, through `blobs`,
+ * a HOST array of top_k device pointers (the reference's RoutedBlobs).
+ * top_k <= 8. */
+
+/* MoE.encodeRoutedPersistentPhase1U16Load (MoE.swift:234-266; moe.metal:248-369):
+ * acts[slot*f + j] = half(gelu_tanh(gate_slot[j].x) * (up_slot[j].x)), d % 64 == 0, f % 64 == 0. */
+TF_API tf_status tf_moe_phase1(tf_context* ctx, const void* pool, uint64_t expert_stride, uint32_t num_experts,
+                        const void* expert_ids, const void* const* blobs, const tf_expert_offsets* offsets,
+                        const void* x, void* acts, uint32_t d, uint32_t f, uint32_t top_k,
+                        tf_scale_type st, void* stream);
+
+/* MoE.encodeRoutedPersistentPhase2Reduce (MoE.swift:312-362; moe.metal:475-511):
+ * y[i] = half(residual[i] + sum_slot float(w_slot) * down_slot[i].acts_slot).
+ * residual may be NULL (zero). */
+TF_API tf_status tf_moe_phase2(tf_context* ctx, const void* pool, uint64_t expert_stride, uint32_t num_experts,
+                        const void* expert_ids, const void* const* blobs, const tf_expert_offsets* offsets,
+                        const void* acts, const void* routing_weights, const void* residual, void* y,
+                        uint32_t d, uint32_t f, uint32_t top_k, tf_scale_type st, void* stream);
+
+/* SharedExpertProjection (Sources/TurboFieldfare/Kernels/MoE/SharedExpertInt8.swift:9-31). */
+typedef struct {
+    const void* weights;
+    const void* scales;
+    const void* biases;
+    uint32_t rows, cols;
+    uint32_t bits; /* 4 or 8 */
+} tf_affine_matrix;
+
+/* SharedExpertRuntime.encode (Sources/TurboFieldfare/Kernels/MoE/SharedExpertInt4.swift:97-137):
+ * g = half(gate.x), u = half(up.x), act = half(gelu(g)*u), y = half(down.act).
+ * scratch_act: caller-owned fp16[gate.rows] (the reference's scratchAct). */
+TF_API tf_status tf_shared_expert(tf_context* ctx, const void* x, const tf_affine_matrix* gate,
+                           const tf_affine_matrix* up, const tf_affine_matrix* down, void* y,
+                           void* scratch_act, tf_scale_type st, void* stream);
+
+/* One MoE FFN decode layer for one token (RealForwardRunner.produceToken's MoE
+ * section, Sources/TurboFieldfare/Runtime/Inference/RealForwardRunner.swift:2480-2860,
+ * without the SSD fetch: experts are HBM resident):
+ *   router(router_x) -> top_k ids/weights (kept on the device)
+ *   y = half(residual + sum_slot w_slot*routed_slot(x) + shared(x))
+ * shared_* with rows == 0 disables the shared expert; residual may be NULL.
+ * out_indices / out_weights (device, optional) receive the routing. */
+typedef struct {
+    const void* router_w;
+    const void* router_s;
+    const void* router_b;
+    const void* eff_scale;        /* BF16 [d] */
+    const void* per_expert_scale; /* BF16 [num_experts] */
+    const void* expert_pool;
+    uint64_t expert_stride;
+    uint32_t num_experts;
+    tf_expert_offsets offsets;
+    tf_affine_matrix shared_gate, shared_up, shared_down;
+    uint32_t d, f, top_k;
+    tf_scale_type scale_type;
+} tf_moe_layer;
+
+TF_API tf_status tf_moe_decode_layer(tf_context* ctx, const tf_moe_layer* layer, const void* router_x,
+                              const void* x, const void* residual, void* y, void* out_indices,
+                              void* out_weights, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TFCUDA_H */
