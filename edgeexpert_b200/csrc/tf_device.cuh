@@ -36,7 +36,7 @@ constexpr int kStageStride8 = 448;
 constexpr int kStageBytes = kRowsPerTile * kStageStride8;
 constexpr int kChunkGroups4 = 11;     // groups per unit, int4 (352 B per row)
 constexpr int kChunkGroups8 = 6;      // groups per unit, int8 (384 B per row)
-constexpr uint32_t kSpinLimit = 1u << 26;  // bounded mbarrier wait (error flag after)
+constexpr uint32_t kSpinLimit = 1u << 22;  // bounded mbarrier wait (error flag after)
 
 // Error bits written to the context's device status word.
 enum : uint32_t { kErrMbarTimeout = 1u, kErrBadExpert = 2u };

@@ -307,6 +307,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) engine_kernel(const typename P
 
     int seq = 0;
     int parity_buf = 0;
+    bool dead = false;
     for (int sjx = blockIdx.x; sjx < S; sjx += gridDim.x) {
         const SuperJob sj = decode_superjob<Pol>(p, sjx);
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -321,7 +322,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1) engine_kernel(const typename P
             const bool found = find_unit<Pol>(p, sj.j0 + v / sj.U, v % sj.U, &sd, &chunk);
             bool ready = true;
             if (p.aligned) {
-                ready = mbar_wait_bounded(&my_bars[slot], ph, p.err);
+                // once a wait has given up, later waits of this warp are skipped
+                ready = !dead && mbar_wait_bounded(&my_bars[slot], ph, p.err);
+                dead = dead || !ready;
             } else if (found) {
                 unit_copy_sync(st, sd, chunk, lane);
                 __syncwarp();
