@@ -139,14 +139,14 @@ tf_status tf_context_create(int device, tf_context** out) {
     ctx->num_sms = prop.multiProcessorCount;
     ctx->max_smem_optin = prop.sharedMemPerBlockOptin;
     cudaError_t e = cudaSuccess;
-    e = e ? e : cudaMalloc(&ctx->d_err, sizeof(uint32_t));
+    e = e ? e : cudaMalloc(&ctx->d_err, 4 * sizeof(uint32_t));
     e = e ? e : cudaMalloc(&ctx->d_logits, sizeof(float) * kMaxRouterExperts * 64);
     e = e ? e : cudaMalloc(&ctx->d_ticket, sizeof(unsigned int) * 64);
     e = e ? e : cudaMalloc(&ctx->d_idx, sizeof(uint32_t) * kMaxTopKDecode);
     e = e ? e : cudaMalloc(&ctx->d_w, sizeof(__half) * kMaxTopKDecode);
     e = e ? e : cudaMalloc(&ctx->d_acts, sizeof(__half) * kMaxTopKDecode * kMaxF);
     e = e ? e : cudaMalloc(&ctx->d_shared_act, sizeof(__half) * kMaxFs);
-    e = e ? e : cudaMemset(ctx->d_err, 0, sizeof(uint32_t));
+    e = e ? e : cudaMemset(ctx->d_err, 0, 4 * sizeof(uint32_t));
     e = e ? e : cudaMemset(ctx->d_ticket, 0, sizeof(unsigned int) * 64);
     e = e ? e : cudaDeviceSynchronize();
     if (e != cudaSuccess) {
@@ -176,15 +176,19 @@ tf_status tf_context_check_device(tf_context* ctx, void* stream, uint32_t* flags
     tf_status s = check_ctx(ctx);
     if (s) return s;
     cudaStream_t cs = static_cast<cudaStream_t>(stream);
-    uint32_t flags = 0;
-    cudaError_t e = cudaMemcpyAsync(&flags, ctx->d_err, sizeof(flags), cudaMemcpyDeviceToHost, cs);
+    uint32_t words[4] = {0, 0, 0, 0};
+    cudaError_t e = cudaMemcpyAsync(words, ctx->d_err, sizeof(words), cudaMemcpyDeviceToHost, cs);
     if (e == cudaSuccess) e = cudaStreamSynchronize(cs);
-    if (e == cudaSuccess) e = cudaMemsetAsync(ctx->d_err, 0, sizeof(uint32_t), cs);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ctx->d_err, 0, sizeof(words), cs);
+    const uint32_t flags = words[0];
     if (e == cudaSuccess) e = cudaStreamSynchronize(cs);
     if (e != cudaSuccess) return cuda_check(ctx, e, "tf_context_check_device");
     if (flags_out) *flags_out = flags;
     if (flags & kErrMbarTimeout) return fail(ctx, TF_ERR_TIMEOUT, "a bounded device wait gave up (flags=0x%x)", flags);
     if (flags & kErrBadExpert) return fail(ctx, TF_ERR_INVALID_ARG, "an expert id was out of range (flags=0x%x)", flags);
+    if (flags & kErrAlign)
+        return fail(ctx, TF_ERR_MISALIGNED, "misaligned access skipped at site %u, address 0x%08x%08x", words[1],
+                    words[3], words[2]);
     return TF_OK;
 }
 

@@ -39,7 +39,25 @@ constexpr int kChunkGroups8 = 6;      // groups per unit, int8 (384 B per row)
 constexpr uint32_t kSpinLimit = 1u << 22;  // bounded mbarrier wait (error flag after)
 
 // Error bits written to the context's device status word.
-enum : uint32_t { kErrMbarTimeout = 1u, kErrBadExpert = 2u };
+enum : uint32_t { kErrMbarTimeout = 1u, kErrBadExpert = 2u, kErrAlign = 4u };
+
+// Debug builds (-DTF_CHECKS) verify the alignment of every vector and bulk
+// access before issuing it; a violation records the site and address in the
+// device status words (err[1] = site, err[2..3] = address) and skips the access.
+#ifdef TF_CHECKS
+__device__ __forceinline__ bool tf_check_align(const void* p, unsigned a, uint32_t* err, uint32_t site) {
+    if ((reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0) return true;
+    if (err && atomicOr(err, kErrAlign) == 0) {
+        err[1] = site;
+        err[2] = (uint32_t)reinterpret_cast<uintptr_t>(p);
+        err[3] = (uint32_t)(reinterpret_cast<uintptr_t>(p) >> 32);
+    }
+    return false;
+}
+#define TF_ALIGNED(p, a, err, site) tf_check_align((p), (a), (err), (site))
+#else
+#define TF_ALIGNED(p, a, err, site) true
+#endif
 
 __device__ __forceinline__ float scale_to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ float scale_to_float(__half v) { return __half2float(v); }

@@ -59,7 +59,8 @@ __host__ __device__ inline int superjob_J(int U) { return (U <= kWarps && kWarps
 // ---------------------------------------------------------------------------
 template <typename ST, int BITS>
 __device__ __forceinline__ void compute_unit(const uint8_t* __restrict__ stage, const SegDesc& sd, int chunk,
-                                             float out[4], int lane) {
+                                             float out[4], int lane, uint32_t* err) {
+    (void)err;
     const int g = lane >> 2, t = lane & 3;
     const int ngK = sd.K / kGroup;
     const int cg = chunk_groups(BITS);
@@ -86,11 +87,15 @@ __device__ __forceinline__ void compute_unit(const uint8_t* __restrict__ stage, 
         uint4 x0 = make_uint4(0, 0, 0, 0), x1 = make_uint4(0, 0, 0, 0);
         if (tokv) {
             const uint4* xp = reinterpret_cast<const uint4*>(xrow + (G * 8 + 2 * t) * 4);
-            x0 = xp[0];
-            x1 = xp[1];
+            if (TF_ALIGNED(xp, 16, err, 1)) {
+                x0 = xp[0];
+                x1 = xp[1];
+            }
         }
         uint32_t pa0[4], pa1[4], pb0[4], pb1[4];
         if (BITS == 4) {
+            if (!TF_ALIGNED(rowa + gl * 32 + t * 8, 8, err, 2) || !TF_ALIGNED(rowb + gl * 32 + t * 8, 8, err, 3))
+                continue;
             const uint2 wa = *reinterpret_cast<const uint2*>(rowa + gl * 32 + t * 8);
             const uint2 wb = *reinterpret_cast<const uint2*>(rowb + gl * 32 + t * 8);
             dq4(wa.x, pa0);
@@ -98,6 +103,8 @@ __device__ __forceinline__ void compute_unit(const uint8_t* __restrict__ stage, 
             dq4(wb.x, pb0);
             dq4(wb.y, pb1);
         } else {
+            if (!TF_ALIGNED(rowa + gl * 64 + t * 16, 16, err, 4) || !TF_ALIGNED(rowb + gl * 64 + t * 16, 16, err, 5))
+                continue;
             const uint4 wa = *reinterpret_cast<const uint4*>(rowa + gl * 64 + t * 16);
             const uint4 wb = *reinterpret_cast<const uint4*>(rowb + gl * 64 + t * 16);
             dq8(wa.x, wa.y, pa0);
@@ -165,7 +172,8 @@ __device__ __forceinline__ void unit_copy_sync(uint8_t* stage, const SegDesc& sd
 }
 
 __device__ __forceinline__ void unit_issue(uint8_t* stage, uint64_t* bar, const SegDesc& sd, int chunk,
-                                           int lane) {
+                                           int lane, uint32_t* err) {
+    (void)err;
     const int stride = stage_stride(sd.bits);
     uint32_t total = 0;
     for (int r = 0; r < 16; ++r) {
@@ -182,7 +190,9 @@ __device__ __forceinline__ void unit_issue(uint8_t* stage, uint64_t* bar, const 
         int bytes;
         bool valid;
         unit_row(sd, chunk, lane, &src, &bytes, &valid);
-        if (valid) bulk_g2s(stage + lane * stride, src, (uint32_t)bytes, bar);
+        if (valid && TF_ALIGNED(src, 16, err, 6) && TF_ALIGNED(stage + lane * stride, 16, err, 7) &&
+            TF_ALIGNED((const void*)(uintptr_t)bytes, 16, err, 8))
+            bulk_g2s(stage + lane * stride, src, (uint32_t)bytes, bar);
     }
 }
 
@@ -294,7 +304,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) engine_kernel(const typename P
             SegDesc sd;
             int chunk;
             if (find_unit<Pol>(p, sj.j0 + v / sj.U, v % sj.U, &sd, &chunk)) {
-                unit_issue(my_stages + (size_t)slot * kStageBytes, &my_bars[slot], sd, chunk, lane);
+                unit_issue(my_stages + (size_t)slot * kStageBytes, &my_bars[slot], sd, chunk, lane, p.err);
             } else if (lane == 0) {
                 mbar_arrive_expect_tx(&my_bars[slot], 0);  // keep the phase sequence intact
             }
@@ -332,9 +342,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1) engine_kernel(const typename P
             if (found && ready) {
                 float u[4];
                 if (sd.bits == 4)
-                    compute_unit<ST, 4>(st, sd, chunk, u, lane);
+                    compute_unit<ST, 4>(st, sd, chunk, u, lane, p.err);
                 else
-                    compute_unit<ST, 8>(st, sd, chunk, u, lane);
+                    compute_unit<ST, 8>(st, sd, chunk, u, lane, p.err);
 #pragma unroll
                 for (int k = 0; k < 4; ++k) acc[k] = fmaf(sd.mult, u[k], acc[k]);
             }

@@ -246,11 +246,14 @@ struct Phase2Policy {
         *U = p.top_k * units_for_K(p.F, 4) + (p.has_shared ? units_for_K(p.Fs, p.shared_bits) : 0);
     }
     // x area: top_k routed act slots (F) then the shared act slot (Fs).
-    static size_t x_bytes(int top_k, int F, int Fs) {
-        return (size_t)top_k * (x_words_stride(F) * 4 + (F / kGroup) * 4) +
-               (size_t)(Fs > 0 ? x_words_stride(Fs) * 4 + (Fs / kGroup) * 4 : 0);
+    // Each slot (staged activation + per-group sums) is rounded up to 16 bytes
+    // so the next slot's staged words stay 16-byte aligned for vector loads.
+    __host__ __device__ static size_t slot_bytes(int K) {
+        return ((size_t)x_words_stride(K) * 4 + (size_t)(K / kGroup) * 4 + 15) / 16 * 16;
     }
-    __device__ static size_t slot_bytes(int K) { return (size_t)x_words_stride(K) * 4 + (K / kGroup) * 4; }
+    static size_t x_bytes(int top_k, int F, int Fs) {
+        return (size_t)top_k * slot_bytes(F) + (size_t)(Fs > 0 ? slot_bytes(Fs) : 0);
+    }
     __device__ static void stage_x(const Params& p, uint8_t* xa, int tid, int nt) {
         for (int s = 0; s < p.top_k; ++s) {
             uint32_t* xs = reinterpret_cast<uint32_t*>(xa + s * slot_bytes(p.F));

@@ -266,9 +266,14 @@ def test_routed_phase1_phase2(cuda, use_pool, D, F):
 def test_shared_expert(cuda, bits, D, Fs):
     from edgeexpert_b200.moe import SharedExpertProjection, SharedExpertRuntime
     rng = O.seed_tree(9, f"shared-{bits}-{D}")
-    g = rng.synthetic_affine(Fs, D, bits, 0)
-    u = rng.synthetic_affine(Fs, D, bits, 0)
-    d = rng.synthetic_affine(D, Fs, bits, 0)
+    if bits == 4:  # BASELINE config distributions
+        g = rng.synthetic_affine(Fs, D, bits, 0)
+        u = rng.synthetic_affine(Fs, D, bits, 0)
+        d = rng.synthetic_affine(D, Fs, bits, 0)
+    else:  # SharedExpertInt8Tests style: quantizeInt8Affine of small uniform rows
+        g = O.quantize_affine(rng.uniform(-0.04, 0.04, Fs * D).reshape(Fs, D), 8)
+        u = O.quantize_affine(rng.uniform(-0.04, 0.04, Fs * D).reshape(Fs, D), 8)
+        d = O.quantize_affine(rng.uniform(-0.04, 0.04, D * Fs).reshape(D, Fs), 8)
     x16 = rng.normal_f16(D)
     act_ref, y16_ref, y32_ref = O.shared_expert(g, u, d, x16, D, Fs, bits)
 
