@@ -88,6 +88,7 @@ _PROTOS = {
     "tf_shared_expert": ([_P, _P, C.POINTER(AffineMatrix), C.POINTER(AffineMatrix), C.POINTER(AffineMatrix),
                           _P, _P, _I, _P], _I),
     "tf_moe_decode_layer": ([_P, C.POINTER(MoELayer), _P, _P, _P, _P, _P, _P, _P], _I),
+    "tf_router_topk_noalloc": ([_P, _P, _P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _I, _P], _I),
 }
 
 # Symbols of include/tfcuda.h added by later milestones register here too.

@@ -112,6 +112,22 @@ TF_API tf_status tf_router_topk(tf_context* ctx, const void* W, const void* scal
                          void* out_indices, void* out_weights, uint32_t num_experts, uint32_t d,
                          uint32_t top_k, tf_scale_type st, void* stream);
 
+/* Same computation as tf_router_topk, for callers that cannot allocate
+ * device memory (a host application whose allocator owns every device byte,
+ * or code that must not allocate after start-up).  No counterpart in the
+ * reference.  Needs no tf_context and allocates nothing: its scratch (router
+ * logits, selection ticket, error words; about 1 KB) is a fixed array in the
+ * library that every GPU loading the library keeps until process exit.
+ * Limit: num_experts <= 256 (TF_ERR_UNSUPPORTED_SHAPE beyond), other limits
+ * as tf_router_topk.  The first call on a device, with that device current,
+ * looks up the array's device address and zeroes it (synchronously); make
+ * that first call before any stream capture.  All calls on a device share the
+ * array, so calls that overlap on the GPU race: serialise them on one stream. */
+TF_API tf_status tf_router_topk_noalloc(const void* W, const void* scales, const void* biases,
+                                        const void* hidden, const void* eff_scale, const void* per_expert_scale,
+                                        void* out_indices, void* out_weights, uint32_t num_experts, uint32_t d,
+                                        uint32_t top_k, tf_scale_type st, void* stream);
+
 /* ---- decode MoE ---------------------------------------------------------- */
 /* MoEExpertOffsets (Sources/TurboFieldfare/Kernels/MoE/MoE.swift:4-29): byte offsets of
  * the nine sub-tensors inside one expert blob, identical for all experts. */
