@@ -10,7 +10,10 @@ import threading
 from pathlib import Path
 
 _PKG = Path(__file__).resolve().parent
-LIB_PATH = _PKG / "libtfcuda.so"
+import os
+
+# TFCUDA_LIB selects another build of the same library (e.g. a debug build).
+LIB_PATH = Path(os.environ.get("TFCUDA_LIB", str(_PKG / "libtfcuda.so")))
 
 # tf_status codes (tfcuda.h)
 TF_OK = 0

@@ -37,6 +37,9 @@ bool source_aligned(const ExpertSource& s, uint32_t top_k, bool phase1) {
     const uint32_t a = phase1 ? s.off[0] : s.off[6];
     const uint32_t b = phase1 ? s.off[3] : s.off[6];
     if ((a & 15u) || (b & 15u)) return false;
+    const int sb[4] = {phase1 ? 1 : 7, phase1 ? 2 : 8, phase1 ? 4 : 7, phase1 ? 5 : 8};
+    for (int i = 0; i < 4; ++i)
+        if (s.off[sb[i]] & 3u) return false;
     if (s.ids) return aligned16(s.pool) && (s.stride & 15u) == 0;
     for (uint32_t i = 0; i < top_k; ++i)
         if (!aligned16(s.blobs[i])) return false;
@@ -89,11 +92,16 @@ tf_status gemv_common(tf_context* ctx, uint32_t bits, const void* W, const void*
     p.y = static_cast<__half*>(y);
     p.y_row_stride = (int)yrs;
     p.y_bstride = (long long)ybs;
-    p.aligned = aligned16(W) && (batch == 1 || (wbs & 15u) == 0);
+    // Bulk-copy path: 16-byte aligned weights; scale/bias rows copied as
+    // 4-byte words, so 4-byte aligned bases and an even element count.
+    p.aligned = aligned16(W) && (batch == 1 || (wbs & 15u) == 0) && aligned4(S) && aligned4(B) &&
+                (((uint64_t)m * (n / 64)) % 2 == 0) && (batch == 1 || sbs % 2 == 0);
     p.x_aligned = aligned16(x) && (ntok == 1 || (xrs % 8) == 0);
     p.err = ctx->d_err;
     const int U = units_for_K((int)n, (int)bits);
-    const int sj = host_superjobs((int)batch * (((int)m + 15) / 16), U);
+    p.tiles = ((int)m + 15) / 16;
+    p.sched = make_sched((int)batch * p.tiles, U);
+    const int sj = p.sched.S_total;
     cudaStream_t cs = static_cast<cudaStream_t>(stream);
     return dispatch_scale(st, [&](auto tag) {
         using ST = decltype(tag);
@@ -237,9 +245,10 @@ static tf_status router_launch(tf_context* ctx, const void* W, const void* S, co
     p.ticket = ctx->d_ticket;
     p.out_idx = static_cast<uint32_t*>(out_idx);
     p.out_w = static_cast<__half*>(out_w);
-    p.aligned = aligned16(W);
+    p.aligned = aligned16(W) && aligned4(S) && aligned4(B) && (((uint64_t)E * (d / 64)) % 2 == 0);
     p.err = ctx->d_err;
-    const int sj = host_superjobs(((int)E + 15) / 16, units_for_K((int)d, 8));
+    p.sched = make_sched(((int)E + 15) / 16, units_for_K((int)d, 8));
+    const int sj = p.sched.S_total;
     return dispatch_scale(st, [&](auto tag) {
         using ST = decltype(tag);
         return launch_engine<RouterPolicy<ST>, ST>(ctx, p, RouterPolicy<ST>::x_bytes((int)d), sj, cs, name);
@@ -277,13 +286,16 @@ static tf_status phase1_launch(tf_context* ctx, const ExpertSource& src, const v
         p.sg = AffineMat{static_cast<const uint8_t*>(sg->weights), sg->scales, sg->biases};
         p.su = AffineMat{static_cast<const uint8_t*>(su->weights), su->scales, su->biases};
         p.shared_act = static_cast<__half*>(shared_act);
-        aligned = aligned && aligned16(sg->weights) && aligned16(su->weights);
+        aligned = aligned && aligned16(sg->weights) && aligned16(su->weights) && aligned4(sg->scales) &&
+                  aligned4(sg->biases) && aligned4(su->scales) && aligned4(su->biases);
     }
     p.aligned = aligned;
     p.x_aligned = aligned16(x);
     p.err = ctx->d_err;
-    int sj = top_k ? host_superjobs((int)top_k * ((int)f / 8), units_for_K((int)d, 4)) : 0;
-    if (sg) sj += host_superjobs((int)sg->rows / 8, units_for_K((int)d, (int)sg->bits));
+    p.fjobs = (int)f / 8;
+    p.sched = make_sched((int)top_k * p.fjobs, units_for_K((int)d, 4), sg ? (int)sg->rows / 8 : 0,
+                         sg ? units_for_K((int)d, (int)sg->bits) : 1);
+    const int sj = p.sched.S_total;
     return dispatch_scale(st, [&](auto tag) {
         using ST = decltype(tag);
         return launch_engine<Phase1Policy<ST>, ST>(ctx, p, Phase1Policy<ST>::x_bytes((int)d), sj, cs, name);
@@ -316,13 +328,15 @@ static tf_status phase2_launch(tf_context* ctx, const ExpertSource& src, const v
         p.Fs = (int)sdn->cols;
         p.sd = AffineMat{static_cast<const uint8_t*>(sdn->weights), sdn->scales, sdn->biases};
         p.shared_act = static_cast<const __half*>(shared_act);
-        aligned = aligned && aligned16(sdn->weights);
+        aligned = aligned && aligned16(sdn->weights) && aligned4(sdn->scales) && aligned4(sdn->biases);
         if (!aligned16(shared_act)) return fail(ctx, TF_ERR_MISALIGNED, "%s: shared act must be 16-byte aligned", name);
     }
     p.aligned = aligned;
     p.err = ctx->d_err;
     const int U = (int)top_k * units_for_K((int)f, 4) + (sdn ? units_for_K((int)sdn->cols, (int)sdn->bits) : 0);
-    const int sj = host_superjobs(((int)d + 15) / 16, U);
+    p.upf = units_for_K((int)f, 4);
+    p.sched = make_sched(((int)d + 15) / 16, U);
+    const int sj = p.sched.S_total;
     return dispatch_scale(st, [&](auto tag) {
         using ST = decltype(tag);
         xb = Phase2Policy<ST>::x_bytes((int)top_k, (int)f, sdn ? (int)sdn->cols : 0);
@@ -422,3 +436,9 @@ tf_status tf_moe_decode_layer(tf_context* ctx, const tf_moe_layer* L, const void
 }
 
 }  // extern "C"
+
+#ifdef TF_TRACE
+extern "C" TF_API int tf_debug_trace(unsigned long long* out, int n) {
+    return (int)cudaMemcpyFromSymbol(out, tf::g_tf_trace, sizeof(unsigned long long) * 8 * n);
+}
+#endif

@@ -51,12 +51,7 @@ inline tf_status cuda_check(tf_context* ctx, cudaError_t e, const char* what) {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline bool aligned2(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 1u) == 0; }
-
-// Number of engine super-jobs for one range (host mirror of superjob_J).
-inline int host_superjobs(int njobs, int U) {
-    const int J = superjob_J(U);
-    return (njobs + J - 1) / J;
-}
+inline bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
 
 // Launch one engine instantiation: picks the ring depth that fits, sets the
 // dynamic shared-memory attribute once per instantiation, sizes the grid to
@@ -65,7 +60,15 @@ template <class Pol, typename ST>
 tf_status launch_engine(tf_context* ctx, typename Pol::Params p, size_t x_bytes, int superjobs,
                         cudaStream_t stream, const char* name) {
     if (superjobs <= 0) return TF_OK;
-    const size_t limit = ctx->max_smem_optin;
+    // Dynamic shared memory may use what the kernel's static shared memory leaves.
+    static size_t static_smem = (size_t)-1;
+    if (static_smem == (size_t)-1) {
+        cudaFuncAttributes fa;
+        cudaError_t e = cudaFuncGetAttributes(&fa, engine_kernel<Pol, ST>);
+        if (e != cudaSuccess) return cuda_check(ctx, e, name);
+        static_smem = fa.sharedSizeBytes;
+    }
+    const size_t limit = ctx->max_smem_optin - static_smem;
     int ns = 3;
     size_t smem = engine_fixed_smem(ns) + x_bytes;
     if (smem > limit) {

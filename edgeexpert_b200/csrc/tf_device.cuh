@@ -33,7 +33,12 @@ constexpr int kMaxTok = 8;            // MMA N
 // quarter-warps of 2 rows: 16 (mod 32) words.
 constexpr int kStageStride4 = 416;
 constexpr int kStageStride8 = 448;
-constexpr int kStageBytes = kRowsPerTile * kStageStride8;
+// Stage = 16 padded weight rows, then 32 slots of 32 bytes holding each row's
+// scales and biases for the unit's groups (4-byte-aligned superset copy).
+constexpr int kScaleOff = kRowsPerTile * kStageStride8;
+constexpr int kScaleSlot = 32;
+constexpr int kStageBytes = kScaleOff + 2 * kRowsPerTile * kScaleSlot;
+constexpr uint32_t kStageArrivals = 33;  // 1 expect_tx arrive + 32 cp.async arrives
 constexpr int kChunkGroups4 = 11;     // groups per unit, int4 (352 B per row)
 constexpr int kChunkGroups8 = 6;      // groups per unit, int8 (384 B per row)
 constexpr uint32_t kSpinLimit = 1u << 22;  // bounded mbarrier wait (error flag after)
@@ -118,6 +123,17 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// 4-byte asynchronous global -> shared copy (LDGSTS).
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+// Arrive on `bar` once this thread's earlier cp.async copies have landed
+// (counts as one of the barrier's initialised arrivals).
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t magic) {
     uint32_t r;
     asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(magic));
@@ -185,57 +201,48 @@ __host__ __device__ constexpr int x_words_stride(int K) {
     return ((K / 2 + 31) / 32) * 32 + 4;
 }
 
-// Cooperative staging by `nthreads` threads starting at `tid`.
-// xs: [ntok][x_words_stride] words; xsum: [ntok][K/64] floats.
-// Token rows >= ntok are not touched (callers mask by token count).
-__device__ __forceinline__ void stage_x(const __half* __restrict__ x, int x_row_stride, int ntok, int K,
-                                        uint32_t* xs, float* xsum, int tid, int nthreads) {
+// Per-group sums from the staged octet-pair words: one warp per (token,
+// group); the 32 words of a group hold its 64 values, one word per lane.
+// Callers synchronise the CTA between writing `xs` and calling this.
+__device__ __forceinline__ void stage_xsum_smem(const uint32_t* xs, int ws, int ntok, int K, float* xsum, int tid,
+                                                int nthreads) {
+    const int ng = K / kGroup;
+    const int warp = tid >> 5, lane = tid & 31, nw = nthreads >> 5;
+    for (int i = warp; i < ntok * ng; i += nw) {
+        const int t = i / ng, g = i - t * ng;
+        const uint32_t w = xs[t * ws + g * 32 + lane];
+        const __half2 h = *reinterpret_cast<const __half2*>(&w);
+        float s = __low2float(h) + __high2float(h);
+        for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+        if (lane == 0) xsum[t * ng + g] = s;
+    }
+}
+
+// Cooperative staging of `ntok` activation rows (x[t*x_row_stride + k]) into
+// the octet-pair layout xs[t*x_words_stride(K) + ...] by `nthreads` threads.
+// 16-byte loads when `vec` (row starts 16-byte aligned), else 2-byte loads.
+// No barrier inside: callers synchronise before stage_xsum_smem.
+__device__ __forceinline__ void stage_words(const __half* __restrict__ x, int x_row_stride, int ntok, int K,
+                                            uint32_t* xs, bool vec, int tid, int nthreads) {
     const int octets = K / 8;
     const int ws = x_words_stride(K);
     for (int i = tid; i < ntok * octets; i += nthreads) {
-        const int t = i / octets, q = i % octets;
+        const int t = i / octets, q = i - t * octets;
         const __half* src = x + (size_t)t * x_row_stride + q * 8;
-        uint4 raw = *reinterpret_cast<const uint4*>(src);  // 16 B aligned: x rows are 16 B aligned
-        const __half* h = reinterpret_cast<const __half*>(&raw);
+        __half h[8];
+        if (vec) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(src);
+            memcpy(h, &raw, 16);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) h[j] = src[j];
+        }
         uint32_t* dst = xs + t * ws + q * 4;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             __half2 p = __halves2half2(h[j], h[j + 4]);
             dst[j] = *reinterpret_cast<uint32_t*>(&p);
         }
-    }
-    const int ng = K / kGroup;
-    for (int i = tid; i < ntok * ng; i += nthreads) {
-        const int t = i / ng, g = i % ng;
-        const __half* src = x + (size_t)t * x_row_stride + g * kGroup;
-        float s = 0.f;
-        for (int k = 0; k < kGroup; ++k) s += __half2float(src[k]);
-        xsum[t * ng + g] = s;
-    }
-}
-
-// Scalar variant for activations that are not 16-byte aligned.
-__device__ __forceinline__ void stage_x_scalar(const __half* __restrict__ x, int x_row_stride, int ntok, int K,
-                                               uint32_t* xs, float* xsum, int tid, int nthreads) {
-    const int octets = K / 8;
-    const int ws = x_words_stride(K);
-    for (int i = tid; i < ntok * octets; i += nthreads) {
-        const int t = i / octets, q = i % octets;
-        const __half* src = x + (size_t)t * x_row_stride + q * 8;
-        uint32_t* dst = xs + t * ws + q * 4;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            __half2 p = __halves2half2(src[j], src[j + 4]);
-            dst[j] = *reinterpret_cast<uint32_t*>(&p);
-        }
-    }
-    const int ng = K / kGroup;
-    for (int i = tid; i < ntok * ng; i += nthreads) {
-        const int t = i / ng, g = i % ng;
-        const __half* src = x + (size_t)t * x_row_stride + g * kGroup;
-        float s = 0.f;
-        for (int k = 0; k < kGroup; ++k) s += __half2float(src[k]);
-        xsum[t * ng + g] = s;
     }
 }
 

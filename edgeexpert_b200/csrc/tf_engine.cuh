@@ -25,6 +25,19 @@
 
 namespace tf {
 
+#ifdef TF_TRACE
+// Debug-only phase timestamps (%globaltimer, ns) of thread 0 of each CTA.
+__device__ unsigned long long g_tf_trace[1024][8];
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+#define TF_T(i) do { if (threadIdx.x == 0 && blockIdx.x < 1024) g_tf_trace[blockIdx.x][i] = gtimer(); } while (0)
+#else
+#define TF_T(i) do {} while (0)
+#endif
+
 struct SegDesc {
     const uint8_t* WA;
     const void* SA;
@@ -52,6 +65,14 @@ __host__ __device__ inline int units_for_K(int K, int bits) {
 __host__ __device__ inline int stage_stride(int bits) { return bits == 4 ? kStageStride4 : kStageStride8; }
 __host__ __device__ inline int superjob_J(int U) { return (U <= kWarps && kWarps % U == 0) ? kWarps / U : 1; }
 
+// Global address of the unit's first scale (a=0) or bias (a=1) of stage row r.
+__device__ __forceinline__ const uint8_t* scale_src(const SegDesc& sd, int r, int a, int G0) {
+    const int ngK = sd.K / kGroup;
+    const void* base = r < 8 ? (a ? sd.BA : sd.SA) : (a ? sd.BB : sd.SB);
+    const int row = r < 8 ? sd.rowA + r : sd.rowB + r - 8;
+    return static_cast<const uint8_t*>(base) + ((size_t)row * ngK + G0) * 2;
+}
+
 // ---------------------------------------------------------------------------
 // Unit compute: fresh accumulator over the unit's groups.
 //   c[0] row g   token 2t      c[1] row g   token 2t+1
@@ -68,10 +89,16 @@ __device__ __forceinline__ void compute_unit(const uint8_t* __restrict__ stage, 
     const int G1 = min(ngK, G0 + cg);
     const int stride = stage_stride(BITS);
     const bool va = g < sd.nA, vb = g < sd.nB;
-    const ST* sA = reinterpret_cast<const ST*>(sd.SA) + (size_t)(sd.rowA + g) * ngK;
-    const ST* bA = reinterpret_cast<const ST*>(sd.BA) + (size_t)(sd.rowA + g) * ngK;
-    const ST* sB = reinterpret_cast<const ST*>(sd.SB) + (size_t)(sd.rowB + g) * ngK;
-    const ST* bB = reinterpret_cast<const ST*>(sd.BB) + (size_t)(sd.rowB + g) * ngK;
+    // scale/bias slots of rows g and g+8 (byte offset = the copy's misalignment)
+    auto slot = [&](int r, int a) {
+        const uint8_t* src = scale_src(sd, r, a, G0);
+        return reinterpret_cast<const ST*>(stage + kScaleOff + (r * 2 + a) * kScaleSlot +
+                                           (reinterpret_cast<uintptr_t>(src) & 3u));
+    };
+    const ST* sA = slot(g, 0);
+    const ST* bA = slot(g, 1);
+    const ST* sB = slot(g + 8, 0);
+    const ST* bB = slot(g + 8, 1);
     const bool tokv = g < sd.ntok;
     const bool xv0 = 2 * t < sd.ntok, xv1 = 2 * t + 1 < sd.ntok;
     const uint32_t* xrow = sd.xs + g * sd.xws;
@@ -81,9 +108,13 @@ __device__ __forceinline__ void compute_unit(const uint8_t* __restrict__ stage, 
     const uint8_t* rowb = stage + (g + 8) * stride;
 
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 2
-    for (int G = G0; G < G1; ++G) {
-        const int gl = G - G0;
+    constexpr int kCG = BITS == 4 ? kChunkGroups4 : kChunkGroups8;
+    // Fully unrolled over the unit's groups so the scale/bias loads of every
+    // group are issued before the first MMA instead of one group at a time.
+#pragma unroll
+    for (int gl = 0; gl < kCG; ++gl) {
+        const int G = G0 + gl;
+        if (G >= G1) break;
         uint4 x0 = make_uint4(0, 0, 0, 0), x1 = make_uint4(0, 0, 0, 0);
         if (tokv) {
             const uint4* xp = reinterpret_cast<const uint4*>(xrow + (G * 8 + 2 * t) * 4);
@@ -117,10 +148,10 @@ __device__ __forceinline__ void compute_unit(const uint8_t* __restrict__ stage, 
         mma16816(c, pa0[2], pb0[2], pa0[3], pb0[3], x0.z, x0.w);
         mma16816(c, pa1[0], pb1[0], pa1[1], pb1[1], x1.x, x1.y);
         mma16816(c, pa1[2], pb1[2], pa1[3], pb1[3], x1.z, x1.w);
-        const float sa = va ? ldg_scale(sA + G) : 0.f;
-        const float ba = va ? ldg_scale(bA + G) : 0.f;
-        const float sb = vb ? ldg_scale(sB + G) : 0.f;
-        const float bb = vb ? ldg_scale(bB + G) : 0.f;
+        const float sa = va ? scale_to_float(sA[gl]) : 0.f;
+        const float ba = va ? scale_to_float(bA[gl]) : 0.f;
+        const float sb = vb ? scale_to_float(sB[gl]) : 0.f;
+        const float bb = vb ? scale_to_float(bB[gl]) : 0.f;
         const float s0 = xv0 ? xs0[G] : 0.f;
         const float s1 = xv1 ? xs1[G] : 0.f;
         acc[0] = fmaf(sa, c[0], acc[0]);
@@ -169,88 +200,89 @@ __device__ __forceinline__ void unit_copy_sync(uint8_t* stage, const SegDesc& sd
         uint16_t* d16 = reinterpret_cast<uint16_t*>(stage + r * stride);
         for (int i = lane; i < bytes / 2; i += 32) d16[i] = s16[i];
     }
+    const int ngK = sd.K / kGroup;
+    const int G0 = chunk * chunk_groups(sd.bits);
+    const int n = min(ngK, G0 + chunk_groups(sd.bits)) - G0;
+    const int r = lane >> 1, a = lane & 1;
+    if (r < 8 ? r < sd.nA : (r - 8) < sd.nB) {
+        const uint8_t* src = scale_src(sd, r, a, G0);
+        uint8_t* dst = stage + kScaleOff + lane * kScaleSlot + (reinterpret_cast<uintptr_t>(src) & 3u);
+        const uint16_t* s16 = reinterpret_cast<const uint16_t*>(src);
+        uint16_t* d16 = reinterpret_cast<uint16_t*>(dst);
+        for (int i = 0; i < n; ++i) d16[i] = s16[i];
+    }
 }
 
 __device__ __forceinline__ void unit_issue(uint8_t* stage, uint64_t* bar, const SegDesc& sd, int chunk,
                                            int lane, uint32_t* err) {
     (void)err;
     const int stride = stage_stride(sd.bits);
-    uint32_t total = 0;
-    for (int r = 0; r < 16; ++r) {
-        const uint8_t* src;
-        int bytes;
-        bool valid;
-        unit_row(sd, chunk, r, &src, &bytes, &valid);
-        if (valid) total += bytes;
-    }
-    if (lane == 0) mbar_arrive_expect_tx(bar, total);
+    const int ngK = sd.K / kGroup;
+    const int cg = chunk_groups(sd.bits);
+    const int G0 = chunk * cg;
+    const int gb = group_bytes(sd.bits);
+    const int bytes = (min(ngK, G0 + cg) - G0) * gb;
+    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(bytes * (sd.nA + sd.nB)));
     __syncwarp();
     if (lane < 16) {
-        const uint8_t* src;
-        int bytes;
-        bool valid;
-        unit_row(sd, chunk, lane, &src, &bytes, &valid);
+        const int rb = row_bytes(sd.K, sd.bits);
+        const bool lo = lane < 8;
+        const int r = lo ? lane : lane - 8;
+        const bool valid = r < (lo ? sd.nA : sd.nB);
+        const uint8_t* src = (lo ? sd.WA + (size_t)(sd.rowA + r) * rb : sd.WB + (size_t)(sd.rowB + r) * rb) +
+                             (size_t)G0 * gb;
         if (valid && TF_ALIGNED(src, 16, err, 6) && TF_ALIGNED(stage + lane * stride, 16, err, 7) &&
             TF_ALIGNED((const void*)(uintptr_t)bytes, 16, err, 8))
             bulk_g2s(stage + lane * stride, src, (uint32_t)bytes, bar);
     }
+    {   // scales/biases: lane = 2*row + {0: scale, 1: bias}, 4-byte async copies
+        const int r = lane >> 1, a = lane & 1;
+        const bool valid = r < 8 ? r < sd.nA : (r - 8) < sd.nB;
+        if (valid) {
+            const uint8_t* src = scale_src(sd, r, a, G0);
+            const uint8_t* al = reinterpret_cast<const uint8_t*>(reinterpret_cast<uintptr_t>(src) & ~uintptr_t(3));
+            const int nbytes = (min(ngK, G0 + cg) - G0) * 2 + (int)(src - al);
+            uint8_t* dst = stage + kScaleOff + lane * kScaleSlot;
+            for (int i = 0; i < (nbytes + 3) / 4; ++i) cp_async4(dst + 4 * i, al + 4 * i);
+        }
+        cp_async_mbar_arrive(bar);
+    }
 }
 
-// Locate unit `u` of job `job`: returns the seg index and chunk.
-template <class Pol>
-__device__ __forceinline__ bool find_unit(const typename Pol::Params& p, int job, int u, SegDesc* sd,
-                                          int* chunk) {
-    const int ns = Pol::nseg(p, job);
-    for (int s = 0; s < ns; ++s) {
-        SegDesc d;
-        Pol::seg(p, job, s, &d);
-        const int nu = units_for_K(d.K, d.bits);
-        if (u < nu) {
-            *sd = d;
-            *chunk = u;
-            return true;
-        }
-        u -= nu;
-    }
-    return false;
+// Host-computed schedule: up to two job ranges (e.g. routed and shared
+// experts) with U units per job, J jobs per super-job and S super-jobs each.
+struct Sched {
+    int nj[2], U[2], J[2], S[2];
+    int S_total;
+};
+
+inline Sched make_sched(int nj0, int U0, int nj1 = 0, int U1 = 1) {
+    Sched s;
+    s.nj[0] = nj0;
+    s.U[0] = U0;
+    s.J[0] = superjob_J(U0);
+    s.S[0] = nj0 > 0 ? (nj0 + s.J[0] - 1) / s.J[0] : 0;
+    s.nj[1] = nj1;
+    s.U[1] = U1;
+    s.J[1] = superjob_J(U1);
+    s.S[1] = nj1 > 0 ? (nj1 + s.J[1] - 1) / s.J[1] : 0;
+    s.S_total = s.S[0] + s.S[1];
+    return s;
 }
 
 struct SuperJob {
-    int range, j0, j1, J, U;  // jobs [j0, j1) of `range`, U units per job
+    int j0, j1, J, U;  // jobs [j0, j1), U units per job, J jobs per super-job
 };
 
-template <class Pol>
-__device__ __forceinline__ int total_superjobs(const typename Pol::Params& p) {
-    int S = 0;
-    for (int r = 0; r < Pol::nranges(p); ++r) {
-        int nj, U;
-        Pol::range(p, r, &nj, &U);
-        const int J = superjob_J(U);
-        S += (nj + J - 1) / J;
-    }
-    return S;
-}
-
-template <class Pol>
-__device__ __forceinline__ SuperJob decode_superjob(const typename Pol::Params& p, int sj) {
-    SuperJob s{0, 0, 0, 1, 1};
-    int base = 0;
-    for (int r = 0; r < Pol::nranges(p); ++r) {
-        int nj, U;
-        Pol::range(p, r, &nj, &U);
-        const int J = superjob_J(U);
-        const int S = (nj + J - 1) / J;
-        if (sj < S) {
-            s.range = r;
-            s.j0 = base + sj * J;
-            s.j1 = base + min(nj, (sj + 1) * J);
-            s.J = J;
-            s.U = U;
-            return s;
-        }
-        sj -= S;
-        base += nj;
-    }
+__device__ __forceinline__ SuperJob decode_superjob(const Sched& sc, int sj) {
+    const int r = sj >= sc.S[0] ? 1 : 0;
+    const int local = sj - (r ? sc.S[0] : 0);
+    const int base = r ? sc.nj[0] : 0;
+    SuperJob s;
+    s.J = sc.J[r];
+    s.U = sc.U[r];
+    s.j0 = base + local * s.J;
+    s.j1 = base + min(sc.nj[r], (local + 1) * s.J);
     return s;
 }
 
@@ -281,19 +313,21 @@ __global__ void __launch_bounds__(kWarps * 32, 1) engine_kernel(const typename P
     uint8_t* my_stages = stages + (size_t)warp * ns * kStageBytes;
     uint64_t* my_bars = bars + warp * ns;
 
+    TF_T(0);
     if (lane == 0)
-        for (int s = 0; s < ns; ++s) mbar_init(&my_bars[s], 1);
+        for (int s = 0; s < ns; ++s) mbar_init(&my_bars[s], kStageArrivals);
     fence_mbar_init();
-    Pol::stage_x(p, xarea, threadIdx.x, kWarps * 32);
+    Pol::stage_pre(p, threadIdx.x);
     __syncthreads();
+    TF_T(1);
 
-    const int S = total_superjobs<Pol>(p);
+    const int S = p.sched.S_total;
 
     // Load cursor: same unit sequence as the compute loop below.
     int l_sj = blockIdx.x, l_i = 0;
     auto load_next = [&](int slot) -> void {
         while (l_sj < S) {
-            const SuperJob sj = decode_superjob<Pol>(p, l_sj);
+            const SuperJob sj = decode_superjob(p.sched, l_sj);
             const int v = warp_unit(sj, warp, l_i);
             if (v < 0) {
                 l_sj += gridDim.x;
@@ -303,23 +337,30 @@ __global__ void __launch_bounds__(kWarps * 32, 1) engine_kernel(const typename P
             ++l_i;
             SegDesc sd;
             int chunk;
-            if (find_unit<Pol>(p, sj.j0 + v / sj.U, v % sj.U, &sd, &chunk)) {
+            if (Pol::unit(p, sj.j0 + v / sj.U, v % sj.U, &sd, &chunk)) {
                 unit_issue(my_stages + (size_t)slot * kStageBytes, &my_bars[slot], sd, chunk, lane, p.err);
-            } else if (lane == 0) {
-                mbar_arrive_expect_tx(&my_bars[slot], 0);  // keep the phase sequence intact
+            } else {  // keep the phase sequence intact
+                if (lane == 0) mbar_arrive_expect_tx(&my_bars[slot], 0);
+                cp_async_mbar_arrive(&my_bars[slot]);
             }
             return;
         }
     };
 
+    // Weight tiles do not depend on the activations: put the first NS units of
+    // every warp in flight before staging the activations.
     if (p.aligned)
         for (int s = 0; s < ns; ++s) load_next(s);
+    TF_T(2);
+    Pol::stage_x(p, xarea, threadIdx.x, kWarps * 32);
+    __syncthreads();
+    TF_T(3);
 
     int seq = 0;
     int parity_buf = 0;
     bool dead = false;
     for (int sjx = blockIdx.x; sjx < S; sjx += gridDim.x) {
-        const SuperJob sj = decode_superjob<Pol>(p, sjx);
+        const SuperJob sj = decode_superjob(p.sched, sjx);
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         for (int i = 0;; ++i) {
             const int v = warp_unit(sj, warp, i);
@@ -329,12 +370,13 @@ __global__ void __launch_bounds__(kWarps * 32, 1) engine_kernel(const typename P
             uint8_t* st = my_stages + (size_t)slot * kStageBytes;
             SegDesc sd;
             int chunk;
-            const bool found = find_unit<Pol>(p, sj.j0 + v / sj.U, v % sj.U, &sd, &chunk);
+            const bool found = Pol::unit(p, sj.j0 + v / sj.U, v % sj.U, &sd, &chunk);
             bool ready = true;
             if (p.aligned) {
                 // once a wait has given up, later waits of this warp are skipped
                 ready = !dead && mbar_wait_bounded(&my_bars[slot], ph, p.err);
                 dead = dead || !ready;
+                if (seq == 0) TF_T(4);
             } else if (found) {
                 unit_copy_sync(st, sd, chunk, lane);
                 __syncwarp();
@@ -374,7 +416,9 @@ __global__ void __launch_bounds__(kWarps * 32, 1) engine_kernel(const typename P
             Pol::epilogue(p, sj.j0 + jj, f, lane);
         }
         parity_buf ^= 1;
+        TF_T(5);
     }
+    TF_T(6);
 }
 
 }  // namespace tf

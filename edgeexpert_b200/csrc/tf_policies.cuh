@@ -1,9 +1,22 @@
-// tf_policies.cuh -- job/segment/epilogue policies for the streaming engine.
+// tf_policies.cuh -- job/unit/epilogue policies for the streaming engine.
 // Each policy maps the reference operator's output rows onto 16-row jobs.
+//
+// Policy interface:
+//   Params                      kernel parameters; carry `Sched sched`, `ns`,
+//                               `aligned`, `err`
+//   stage_pre(p, tid)           tiny per-CTA set-up needed to issue copies
+//   stage_x(p, xa, tid, nt)     stage activations (all threads; may barrier)
+//   unit(p, job, u, &sd, &c)    describe unit u of job (weights, rows, x)
+//   epilogue(p, job, f, lane)   one warp writes the job's reduced outputs
 #pragma once
 #include "tf_engine.cuh"
 
 namespace tf {
+
+__device__ __forceinline__ const uint8_t* engine_xarea(int ns) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    return smem + engine_fixed_smem(ns);
+}
 
 // ===========================================================================
 // Plain affine GEMV, Y[tok][row] = sum_k W[row][k] * X[tok][k]
@@ -16,7 +29,7 @@ struct GemvParams {
     const void* B;
     long long w_bstride;   // bytes between matrices
     long long sb_bstride;  // elements between scale blocks
-    int M, K, batch, bits;
+    int M, K, batch, bits, tiles;
     const __half* x;
     int x_row_stride;  // elements between tokens
     int ntok;
@@ -25,32 +38,25 @@ struct GemvParams {
     long long y_bstride;  // elements between matrices of y
     int aligned, x_aligned, ns;
     uint32_t* err;
+    Sched sched;
 };
 
 template <typename ST>
 struct GemvPolicy {
     using Params = GemvParams;
-    __device__ static int nranges(const Params&) { return 1; }
-    __device__ static void range(const Params& p, int, int* nj, int* U) {
-        *nj = p.batch * ((p.M + 15) / 16);
-        *U = units_for_K(p.K, p.bits);
-    }
-    __device__ static void stage_x(const Params& p, uint8_t* xa, int tid, int nt) {
-        uint32_t* xs = reinterpret_cast<uint32_t*>(xa);
-        float* xsum = reinterpret_cast<float*>(xs + kMaxTok * x_words_stride(p.K));
-        if (p.x_aligned)
-            tf::stage_x(p.x, p.x_row_stride, p.ntok, p.K, xs, xsum, tid, nt);
-        else
-            stage_x_scalar(p.x, p.x_row_stride, p.ntok, p.K, xs, xsum, tid, nt);
-    }
     static size_t x_bytes(int K) {
         return (size_t)kMaxTok * x_words_stride(K) * 4 + (size_t)kMaxTok * (K / kGroup) * 4;
     }
-    __device__ static int nseg(const Params&, int) { return 1; }
-    __device__ static void seg(const Params& p, int job, int, SegDesc* d) {
-        extern __shared__ __align__(128) uint8_t smem[];
-        const int tiles = (p.M + 15) / 16;
-        const int b = job / tiles, tile = job % tiles;
+    __device__ static void stage_pre(const Params&, int) {}
+    __device__ static void stage_x(const Params& p, uint8_t* xa, int tid, int nt) {
+        uint32_t* xs = reinterpret_cast<uint32_t*>(xa);
+        float* xsum = reinterpret_cast<float*>(xs + kMaxTok * x_words_stride(p.K));
+        stage_words(p.x, p.x_row_stride, p.ntok, p.K, xs, p.x_aligned, tid, nt);
+        __syncthreads();
+        stage_xsum_smem(xs, x_words_stride(p.K), p.ntok, p.K, xsum, tid, nt);
+    }
+    __device__ static bool unit(const Params& p, int job, int u, SegDesc* d, int* chunk) {
+        const int b = job / p.tiles, tile = job - b * p.tiles;
         const uint8_t* W = p.W + (size_t)b * p.w_bstride;
         const ST* S = reinterpret_cast<const ST*>(p.S) + (size_t)b * p.sb_bstride;
         const ST* B = reinterpret_cast<const ST*>(p.B) + (size_t)b * p.sb_bstride;
@@ -63,17 +69,17 @@ struct GemvPolicy {
         d->nB = max(0, min(8, p.M - d->rowB));
         d->K = p.K;
         d->bits = p.bits;
-        const uint32_t* xs = reinterpret_cast<const uint32_t*>(
-            smem + engine_fixed_smem(p.ns));
+        const uint32_t* xs = reinterpret_cast<const uint32_t*>(engine_xarea(p.ns));
         d->xs = xs;
         d->xsum = reinterpret_cast<const float*>(xs + kMaxTok * x_words_stride(p.K));
         d->xws = x_words_stride(p.K);
         d->ntok = p.ntok;
         d->mult = 1.0f;
+        *chunk = u;
+        return true;
     }
     __device__ static void epilogue(const Params& p, int job, const float f[4], int lane) {
-        const int tiles = (p.M + 15) / 16;
-        const int b = job / tiles, tile = job % tiles;
+        const int b = job / p.tiles, tile = job - b * p.tiles;
         const int g = lane >> 2, t = lane & 3;
         __half* y = p.y + (size_t)b * p.y_bstride;
         const int r0 = tile * 16 + g, r1 = r0 + 8;
@@ -101,9 +107,20 @@ struct ExpertSource {
     uint32_t off[9];  // gate_w gate_s gate_b up_w up_s up_b down_w down_s down_b
 };
 
+// Device expert ids are copied into shared memory once per CTA (stage_ids)
+// so no bulk copy waits on a global load of its expert id.
+__device__ __forceinline__ uint32_t* ids_smem() {
+    __shared__ uint32_t ids[8];
+    return ids;
+}
+
+__device__ __forceinline__ void stage_ids(const ExpertSource& es, int top_k, int tid) {
+    if (es.ids != nullptr && tid < top_k) ids_smem()[tid] = __ldg(es.ids + tid);
+}
+
 __device__ __forceinline__ const uint8_t* expert_blob(const ExpertSource& es, int slot, uint32_t* err) {
     if (es.ids == nullptr) return es.blobs[slot];
-    const uint32_t e = __ldg(es.ids + slot);
+    const uint32_t e = ids_smem()[slot];
     if (e >= (uint32_t)es.num_experts) {
         if (err) atomicOr(err, kErrBadExpert);
         return nullptr;
@@ -129,7 +146,7 @@ struct AffineMat {
 // ===========================================================================
 struct Phase1Params {
     ExpertSource src;
-    int D, F, top_k;
+    int D, F, top_k, fjobs;  // fjobs = F / 8
     const __half* x;
     __half* acts;  // [top_k][F]
     int has_shared, shared_bits, Fs;
@@ -137,43 +154,32 @@ struct Phase1Params {
     __half* shared_act;  // [Fs]
     int aligned, x_aligned, ns;
     uint32_t* err;
+    Sched sched;
 };
 
 template <typename ST>
 struct Phase1Policy {
     using Params = Phase1Params;
-    __device__ static int nranges(const Params& p) { return p.has_shared ? 2 : 1; }
-    __device__ static void range(const Params& p, int r, int* nj, int* U) {
-        if (r == 0) {
-            *nj = p.top_k * (p.F / 8);
-            *U = units_for_K(p.D, 4);
-        } else {
-            *nj = p.Fs / 8;
-            *U = units_for_K(p.D, p.shared_bits);
-        }
-    }
     static size_t x_bytes(int D) { return (size_t)x_words_stride(D) * 4 + (size_t)(D / kGroup) * 4; }
+    __device__ static void stage_pre(const Params& p, int tid) { stage_ids(p.src, p.top_k, tid); }
     __device__ static void stage_x(const Params& p, uint8_t* xa, int tid, int nt) {
         uint32_t* xs = reinterpret_cast<uint32_t*>(xa);
         float* xsum = reinterpret_cast<float*>(xs + x_words_stride(p.D));
-        if (p.x_aligned)
-            tf::stage_x(p.x, p.D, 1, p.D, xs, xsum, tid, nt);
-        else
-            stage_x_scalar(p.x, p.D, 1, p.D, xs, xsum, tid, nt);
+        stage_words(p.x, p.D, 1, p.D, xs, p.x_aligned, tid, nt);
+        __syncthreads();
+        stage_xsum_smem(xs, x_words_stride(p.D), 1, p.D, xsum, tid, nt);
     }
-    __device__ static int nseg(const Params&, int) { return 1; }
-    __device__ static void seg(const Params& p, int job, int, SegDesc* d) {
-        extern __shared__ __align__(128) uint8_t smem[];
-        const uint32_t* xs = reinterpret_cast<const uint32_t*>(smem + engine_fixed_smem(p.ns));
+    __device__ static bool unit(const Params& p, int job, int u, SegDesc* d, int* chunk) {
+        const uint32_t* xs = reinterpret_cast<const uint32_t*>(engine_xarea(p.ns));
         d->xs = xs;
         d->xsum = reinterpret_cast<const float*>(xs + x_words_stride(p.D));
         d->xws = x_words_stride(p.D);
         d->ntok = 1;
         d->mult = 1.0f;
         d->K = p.D;
-        const int rjobs = p.top_k * (p.F / 8);
+        const int rjobs = p.top_k * p.fjobs;
         if (job < rjobs) {
-            const int slot = job / (p.F / 8), f0 = (job % (p.F / 8)) * 8;
+            const int slot = job / p.fjobs, f0 = (job - slot * p.fjobs) * 8;
             const uint8_t* b = expert_blob(p.src, slot, p.err);
             d->bits = 4;
             d->rowA = d->rowB = f0;
@@ -197,13 +203,15 @@ struct Phase1Policy {
             d->SB = p.su.S;
             d->BB = p.su.B;
         }
+        *chunk = u;
+        return true;
     }
     __device__ static void epilogue(const Params& p, int job, const float f[4], int lane) {
         const int g = lane >> 2, t = lane & 3;
         if (t != 0) return;  // token 0 lives in column 0: lanes with t == 0
-        const int rjobs = p.top_k * (p.F / 8);
+        const int rjobs = p.top_k * p.fjobs;
         if (job < rjobs) {
-            const int slot = job / (p.F / 8), f0 = (job % (p.F / 8)) * 8;
+            const int slot = job / p.fjobs, f0 = (job - slot * p.fjobs) * 8;
             // routed: g and u stay fp32 (moe.metal:368)
             p.acts[(size_t)slot * p.F + f0 + g] = __float2half_rn(gelu_tanh(f[0]) * f[2]);
         } else {
@@ -222,10 +230,12 @@ struct Phase1Policy {
 //                                 [+ shared_down[d].shared_act])
 // (moe_phase2_down_reduce_k8, moe.metal:475-511; shared down GEMV,
 // SharedExpertInt4.swift:87-93).  Job = 16 consecutive d rows.
+// x area: routed acts as a token block [top_k][ws(F)] words, their sums
+// [top_k][F/64], then the shared act words [ws(Fs)] and sums [Fs/64].
 // ===========================================================================
 struct Phase2Params {
     ExpertSource src;
-    int D, F, top_k;
+    int D, F, top_k, upf;     // upf = units per routed down row (F)
     const __half* acts;       // [top_k][F]
     const __half* routing_w;  // [top_k] fp16
     const __half* residual;   // [D] or nullptr
@@ -235,46 +245,41 @@ struct Phase2Params {
     const __half* shared_act;  // [Fs]
     int aligned, ns;
     uint32_t* err;
+    Sched sched;
 };
 
 template <typename ST>
 struct Phase2Policy {
     using Params = Phase2Params;
-    __device__ static int nranges(const Params&) { return 1; }
-    __device__ static void range(const Params& p, int, int* nj, int* U) {
-        *nj = (p.D + 15) / 16;
-        *U = p.top_k * units_for_K(p.F, 4) + (p.has_shared ? units_for_K(p.Fs, p.shared_bits) : 0);
-    }
-    // x area: top_k routed act slots (F) then the shared act slot (Fs).
-    // Each slot (staged activation + per-group sums) is rounded up to 16 bytes
-    // so the next slot's staged words stay 16-byte aligned for vector loads.
-    __host__ __device__ static size_t slot_bytes(int K) {
-        return ((size_t)x_words_stride(K) * 4 + (size_t)(K / kGroup) * 4 + 15) / 16 * 16;
+    __host__ __device__ static size_t routed_words(int top_k, int F) { return (size_t)top_k * x_words_stride(F); }
+    __host__ __device__ static size_t shared_off(int top_k, int F) {
+        return ((routed_words(top_k, F) * 4 + (size_t)top_k * (F / kGroup) * 4) + 15) / 16 * 16;
     }
     static size_t x_bytes(int top_k, int F, int Fs) {
-        return (size_t)top_k * slot_bytes(F) + (size_t)(Fs > 0 ? slot_bytes(Fs) : 0);
+        return shared_off(top_k, F) + (Fs > 0 ? (size_t)x_words_stride(Fs) * 4 + (size_t)(Fs / kGroup) * 4 : 0);
     }
+    __device__ static void stage_pre(const Params& p, int tid) { stage_ids(p.src, p.top_k, tid); }
     __device__ static void stage_x(const Params& p, uint8_t* xa, int tid, int nt) {
-        for (int s = 0; s < p.top_k; ++s) {
-            uint32_t* xs = reinterpret_cast<uint32_t*>(xa + s * slot_bytes(p.F));
-            float* xsum = reinterpret_cast<float*>(xs + x_words_stride(p.F));
-            tf::stage_x(p.acts + (size_t)s * p.F, p.F, 1, p.F, xs, xsum, tid, nt);
-        }
-        if (p.has_shared) {
-            uint32_t* xs = reinterpret_cast<uint32_t*>(xa + p.top_k * slot_bytes(p.F));
-            float* xsum = reinterpret_cast<float*>(xs + x_words_stride(p.Fs));
-            tf::stage_x(p.shared_act, p.Fs, 1, p.Fs, xs, xsum, tid, nt);
-        }
+        uint32_t* xs = reinterpret_cast<uint32_t*>(xa);
+        float* xsum = reinterpret_cast<float*>(xs + routed_words(p.top_k, p.F));
+        uint32_t* xss = reinterpret_cast<uint32_t*>(xa + shared_off(p.top_k, p.F));
+        float* xsums = reinterpret_cast<float*>(xss + x_words_stride(p.Fs));
+        if (p.top_k) stage_words(p.acts, p.F, p.top_k, p.F, xs, true, tid, nt);
+        if (p.has_shared) stage_words(p.shared_act, p.Fs, 1, p.Fs, xss, true, tid, nt);
+        __syncthreads();
+        if (p.top_k) stage_xsum_smem(xs, x_words_stride(p.F), p.top_k, p.F, xsum, tid, nt);
+        if (p.has_shared) stage_xsum_smem(xss, x_words_stride(p.Fs), 1, p.Fs, xsums, tid, nt);
     }
-    __device__ static int nseg(const Params& p, int) { return p.top_k + (p.has_shared ? 1 : 0); }
-    __device__ static void seg(const Params& p, int job, int s, SegDesc* d) {
-        extern __shared__ __align__(128) uint8_t smem[];
-        uint8_t* xa = smem + engine_fixed_smem(p.ns);
+    __device__ static bool unit(const Params& p, int job, int u, SegDesc* d, int* chunk) {
+        const uint8_t* xa = engine_xarea(p.ns);
         const int d0 = job * 16;
         d->rowA = d0;
         d->rowB = d0 + 8;
         d->ntok = 1;
-        if (s < p.top_k) {
+        const int nr = p.top_k * p.upf;
+        if (u < nr) {
+            const int s = p.upf == 1 ? u : u / p.upf;
+            *chunk = u - s * p.upf;
             const uint8_t* b = expert_blob(p.src, s, p.err);
             const bool ok = b != nullptr;
             if (!b) b = p.src.pool ? p.src.pool : p.src.blobs[0];
@@ -285,12 +290,13 @@ struct Phase2Policy {
             d->BA = d->BB = b + p.src.off[8];
             d->K = p.F;
             d->bits = 4;
-            const uint32_t* xs = reinterpret_cast<const uint32_t*>(xa + s * slot_bytes(p.F));
-            d->xs = xs;
-            d->xsum = reinterpret_cast<const float*>(xs + x_words_stride(p.F));
+            const uint32_t* xs = reinterpret_cast<const uint32_t*>(xa);
+            d->xs = xs + (size_t)s * x_words_stride(p.F);
+            d->xsum = reinterpret_cast<const float*>(xs + routed_words(p.top_k, p.F)) + s * (p.F / kGroup);
             d->xws = x_words_stride(p.F);
             d->mult = __half2float(p.routing_w[s]);
         } else {
+            *chunk = u - nr;
             d->nA = max(0, min(8, p.D - d0));
             d->nB = max(0, min(8, p.D - d0 - 8));
             d->WA = d->WB = p.sd.W;
@@ -298,12 +304,13 @@ struct Phase2Policy {
             d->BA = d->BB = p.sd.B;
             d->K = p.Fs;
             d->bits = p.shared_bits;
-            const uint32_t* xs = reinterpret_cast<const uint32_t*>(xa + p.top_k * slot_bytes(p.F));
-            d->xs = xs;
-            d->xsum = reinterpret_cast<const float*>(xs + x_words_stride(p.Fs));
+            const uint32_t* xss = reinterpret_cast<const uint32_t*>(xa + shared_off(p.top_k, p.F));
+            d->xs = xss;
+            d->xsum = reinterpret_cast<const float*>(xss + x_words_stride(p.Fs));
             d->xws = x_words_stride(p.Fs);
             d->mult = 1.0f;
         }
+        return true;
     }
     __device__ static void epilogue(const Params& p, int job, const float f[4], int lane) {
         const int g = lane >> 2, t = lane & 3;
@@ -342,6 +349,7 @@ struct RouterParams {
     __half* out_w;
     int aligned, ns;
     uint32_t* err;
+    Sched sched;
 };
 
 __device__ __forceinline__ void warp_topk_softmax(const float* logits, int E, int k,
@@ -355,15 +363,11 @@ __device__ __forceinline__ void warp_topk_softmax(const float* logits, int E, in
         const int e = lane + 32 * i;
         v[i] = e < E ? __ldcg(logits + e) : -INFINITY;
     }
-    float sel_v[64 / 32 + 1];
-    (void)sel_v;
-    float top_val = -INFINITY;
     float my_exp = 0.f;
     int my_e = -1;
     float vmax = 0.f;
     float sum = 0.f;
     for (int r = 0; r < k; ++r) {
-        // local best
         float bv = -INFINITY;
         int be = 0x7fffffff;
         for (int i = 0; i < kPer; ++i) {
@@ -387,12 +391,10 @@ __device__ __forceinline__ void warp_topk_softmax(const float* logits, int E, in
         if (lane == r) {
             my_e = be;
             my_exp = ex;
-            top_val = bv;
         }
         if (be < E && (be & 31) == lane) v[be >> 5] = -INFINITY;
         if (be >= E) break;
     }
-    (void)top_val;
     if (lane < k && my_e >= 0) {
         out_idx[lane] = (uint32_t)my_e;
         out_w[lane] = __float2half_rn(my_exp / sum * __bfloat162float(pes[my_e]));
@@ -402,12 +404,8 @@ __device__ __forceinline__ void warp_topk_softmax(const float* logits, int E, in
 template <typename ST>
 struct RouterPolicy {
     using Params = RouterParams;
-    __device__ static int nranges(const Params&) { return 1; }
-    __device__ static void range(const Params& p, int, int* nj, int* U) {
-        *nj = (p.E + 15) / 16;
-        *U = units_for_K(p.D, 8);
-    }
     static size_t x_bytes(int D) { return (size_t)2 * x_words_stride(D) * 4 + (size_t)2 * (D / kGroup) * 4; }
+    __device__ static void stage_pre(const Params&, int) {}
     __device__ static void stage_x(const Params& p, uint8_t* xa, int tid, int nt) {
         uint32_t* xs = reinterpret_cast<uint32_t*>(xa);
         const int ws = x_words_stride(p.D);
@@ -428,20 +426,23 @@ struct RouterPolicy {
                 xs[ws + i * 4 + j] = *reinterpret_cast<uint32_t*>(&b);
             }
         }
-        for (int g = tid; g < ng; g += nt) {
-            float s = 0.f;
-            for (int k = 0; k < kGroup; ++k) {
-                const int i = g * kGroup + k;
-                s += __half2float(p.hidden[i]) * __bfloat162float(p.eff_scale[i]);
+        __syncthreads();
+        const int warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
+        for (int g = warp; g < ng; g += nw) {
+            // x~ = hi + lo: sum both staged halves of the group's 64 values
+            const uint32_t a = xs[g * 32 + lane], b = xs[ws + g * 32 + lane];
+            const __half2 ha = *reinterpret_cast<const __half2*>(&a);
+            const __half2 hb = *reinterpret_cast<const __half2*>(&b);
+            float s = (__low2float(ha) + __low2float(hb)) + (__high2float(ha) + __high2float(hb));
+            for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+            if (lane == 0) {
+                xsum[g] = s;  // bias term rides on column 0 only
+                xsum[ng + g] = 0.f;
             }
-            xsum[g] = s;       // bias term rides on column 0 only
-            xsum[ng + g] = 0.f;
         }
     }
-    __device__ static int nseg(const Params&, int) { return 1; }
-    __device__ static void seg(const Params& p, int job, int, SegDesc* d) {
-        extern __shared__ __align__(128) uint8_t smem[];
-        const uint32_t* xs = reinterpret_cast<const uint32_t*>(smem + engine_fixed_smem(p.ns));
+    __device__ static bool unit(const Params& p, int job, int u, SegDesc* d, int* chunk) {
+        const uint32_t* xs = reinterpret_cast<const uint32_t*>(engine_xarea(p.ns));
         d->WA = d->WB = p.W;
         d->SA = d->SB = p.S;
         d->BA = d->BB = p.B;
@@ -456,6 +457,8 @@ struct RouterPolicy {
         d->xws = x_words_stride(p.D);
         d->ntok = 2;
         d->mult = 1.0f;
+        *chunk = u;
+        return true;
     }
     __device__ static void epilogue(const Params& p, int job, const float f[4], int lane) {
         const int g = lane >> 2, t = lane & 3;
