@@ -1,5 +1,10 @@
 // tf_api_decode.cu -- C ABI: context, GEMVs, router, decode MoE layer.
+#include <stdlib.h>
+
+#include <algorithm>
+
 #include "tf_context.cuh"
+#include "tf_fused.cuh"
 
 using namespace tf;
 
@@ -32,18 +37,14 @@ ExpertSource make_source(const void* pool, uint64_t stride, uint32_t E, const vo
     return s;
 }
 
-// True when every weight sub-tensor the bulk-copy path touches is 16-byte aligned.
-bool source_aligned(const ExpertSource& s, uint32_t top_k, bool phase1) {
-    const uint32_t a = phase1 ? s.off[0] : s.off[6];
-    const uint32_t b = phase1 ? s.off[3] : s.off[6];
-    if ((a & 15u) || (b & 15u)) return false;
-    const int sb[4] = {phase1 ? 1 : 7, phase1 ? 2 : 8, phase1 ? 4 : 7, phase1 ? 5 : 8};
-    for (int i = 0; i < 4; ++i)
-        if (s.off[sb[i]] & 3u) return false;
-    if (s.ids) return aligned16(s.pool) && (s.stride & 15u) == 0;
-    for (uint32_t i = 0; i < top_k; ++i)
-        if (!aligned16(s.blobs[i])) return false;
-    return true;
+// TMA descriptors for one weight sub-tensor (byte offset `off` inside each
+// expert blob) of all routed experts: one 3-D map over the pool, or one map
+// per slot for explicit blobs.  False when any cannot be described.
+bool source_maps(const ExpertSource& s, uint32_t top_k, uint32_t off, uint64_t rb, uint64_t rows, CUtensorMap* maps) {
+    if (s.ids) return make_weight_map(&maps[0], s.pool + off, rb, rows, (uint64_t)s.num_experts, s.stride);
+    bool ok = true;
+    for (uint32_t i = 0; i < top_k; ++i) ok = make_weight_map(&maps[i], s.blobs[i] + off, rb, rows, 1, 0) && ok;
+    return ok;
 }
 
 tf_status check_source(tf_context* ctx, const void* pool, const void* ids, const void* const* blobs,
@@ -92,20 +93,32 @@ tf_status gemv_common(tf_context* ctx, uint32_t bits, const void* W, const void*
     p.y = static_cast<__half*>(y);
     p.y_row_stride = (int)yrs;
     p.y_bstride = (long long)ybs;
-    // Bulk-copy path: 16-byte aligned weights; scale/bias rows copied as
-    // 4-byte words, so 4-byte aligned bases and an even element count.
-    p.aligned = aligned16(W) && (batch == 1 || (wbs & 15u) == 0) && aligned4(S) && aligned4(B) &&
-                (((uint64_t)m * (n / 64)) % 2 == 0) && (batch == 1 || sbs % 2 == 0);
+    // TMA path when the weights can be described (16-byte aligned base and
+    // batch stride); otherwise the synchronous 16-bit copy path.
+    p.aligned = make_weight_map(&p.map, W, row_bytes((int)n, (int)bits), m, batch, wbs);
     p.x_aligned = aligned16(x) && (ntok == 1 || (xrs % 8) == 0);
     p.err = ctx->d_err;
     const int U = units_for_K((int)n, (int)bits);
     p.tiles = ((int)m + 15) / 16;
-    p.sched = make_sched((int)batch * p.tiles, U);
+    p.sched = make_sched((int)batch * p.tiles, U, 0, 1, ctx->num_sms);
     const int sj = p.sched.S_total;
     cudaStream_t cs = static_cast<cudaStream_t>(stream);
     return dispatch_scale(st, [&](auto tag) {
         using ST = decltype(tag);
-        return launch_engine<GemvPolicy<ST>, ST>(ctx, p, GemvPolicy<ST>::x_bytes((int)n), sj, cs, name);
+        using Pol = GemvPolicy<ST>;
+        // Tokens per launch: as many as the staged activations fit in shared memory.
+        int tpl = (int)ntok;
+        const size_t limit = engine_smem_limit<Pol, ST>(ctx);
+        while (tpl > 1 && engine_fixed_smem() + Pol::x_bytes((int)n, tpl) + 1024 > limit) --tpl;
+        for (int t0 = 0; t0 < (int)ntok; t0 += tpl) {
+            GemvParams q = p;
+            q.ntok = min(tpl, (int)ntok - t0);
+            q.x = p.x + (size_t)t0 * xrs;
+            q.y = p.y + (size_t)t0 * yrs;
+            tf_status rc = launch_engine<Pol, ST>(ctx, q, Pol::x_bytes((int)n, q.ntok), sj, cs, name);
+            if (rc) return rc;
+        }
+        return TF_OK;
     });
 }
 
@@ -150,12 +163,14 @@ tf_status tf_context_create(int device, tf_context** out) {
     e = e ? e : cudaMalloc(&ctx->d_err, 4 * sizeof(uint32_t));
     e = e ? e : cudaMalloc(&ctx->d_logits, sizeof(float) * kMaxRouterExperts * 64);
     e = e ? e : cudaMalloc(&ctx->d_ticket, sizeof(unsigned int) * 64);
+    e = e ? e : cudaMalloc(&ctx->d_flags, sizeof(unsigned int) * 32 * 1024);
     e = e ? e : cudaMalloc(&ctx->d_idx, sizeof(uint32_t) * kMaxTopKDecode);
     e = e ? e : cudaMalloc(&ctx->d_w, sizeof(__half) * kMaxTopKDecode);
     e = e ? e : cudaMalloc(&ctx->d_acts, sizeof(__half) * kMaxTopKDecode * kMaxF);
     e = e ? e : cudaMalloc(&ctx->d_shared_act, sizeof(__half) * kMaxFs);
     e = e ? e : cudaMemset(ctx->d_err, 0, 4 * sizeof(uint32_t));
     e = e ? e : cudaMemset(ctx->d_ticket, 0, sizeof(unsigned int) * 64);
+    e = e ? e : cudaMemset(ctx->d_flags, 0, sizeof(unsigned int) * 32 * 1024);
     e = e ? e : cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         tf_context_destroy(ctx);
@@ -171,6 +186,7 @@ void tf_context_destroy(tf_context* ctx) {
     cudaFree(ctx->d_err);
     cudaFree(ctx->d_logits);
     cudaFree(ctx->d_ticket);
+    cudaFree(ctx->d_flags);
     cudaFree(ctx->d_idx);
     cudaFree(ctx->d_w);
     cudaFree(ctx->d_acts);
@@ -221,7 +237,8 @@ tf_status tf_affine_gemv_batched(tf_context* ctx, uint32_t bits, const void* W, 
 // Router launch shared by tf_router_topk and the fused layer.
 static tf_status router_launch(tf_context* ctx, const void* W, const void* S, const void* B, const void* hidden,
                                const void* es, const void* pes, void* out_idx, void* out_w, uint32_t E, uint32_t d,
-                               uint32_t top_k, tf_scale_type st, cudaStream_t cs) {
+                               uint32_t top_k, tf_scale_type st, cudaStream_t cs,
+                               RouterParams* build_only = nullptr) {
     const char* name = "tf_router_topk";
     if (!W || !S || !B || !hidden || !es || !pes || !out_idx || !out_w) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
     if (d == 0 || d % 64) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: d must be a positive multiple of 64", name);
@@ -245,10 +262,14 @@ static tf_status router_launch(tf_context* ctx, const void* W, const void* S, co
     p.ticket = ctx->d_ticket;
     p.out_idx = static_cast<uint32_t*>(out_idx);
     p.out_w = static_cast<__half*>(out_w);
-    p.aligned = aligned16(W) && aligned4(S) && aligned4(B) && (((uint64_t)E * (d / 64)) % 2 == 0);
+    p.aligned = make_weight_map(&p.map, W, d, E, 1, 0);
     p.err = ctx->d_err;
-    p.sched = make_sched(((int)E + 15) / 16, units_for_K((int)d, 8));
+    p.sched = make_sched(((int)E + 15) / 16, units_for_K((int)d, 8), 0, 1, ctx->num_sms);
     const int sj = p.sched.S_total;
+    if (build_only) {
+        *build_only = p;
+        return TF_OK;
+    }
     return dispatch_scale(st, [&](auto tag) {
         using ST = decltype(tag);
         return launch_engine<RouterPolicy<ST>, ST>(ctx, p, RouterPolicy<ST>::x_bytes((int)d), sj, cs, name);
@@ -266,7 +287,8 @@ tf_status tf_router_topk(tf_context* ctx, const void* W, const void* S, const vo
 
 static tf_status phase1_launch(tf_context* ctx, const ExpertSource& src, const void* x, void* acts, uint32_t d,
                                uint32_t f, uint32_t top_k, const tf_affine_matrix* sg, const tf_affine_matrix* su,
-                               void* shared_act, tf_scale_type st, cudaStream_t cs, const char* name) {
+                               void* shared_act, tf_scale_type st, cudaStream_t cs, const char* name,
+                               Phase1Params* build_only = nullptr) {
     if (!x || (!acts && top_k)) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null activation pointer", name);
     if (d == 0 || d % 64 || f == 0 || f % 64) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: d and f must be positive multiples of 64", name);
     if (f > (uint32_t)kMaxF * 4) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: f too large", name);
@@ -278,7 +300,11 @@ static tf_status phase1_launch(tf_context* ctx, const ExpertSource& src, const v
     p.top_k = (int)top_k;
     p.x = static_cast<const __half*>(x);
     p.acts = static_cast<__half*>(acts);
-    bool aligned = top_k ? source_aligned(src, top_k, true) : true;
+    bool aligned = true;
+    if (top_k) {
+        aligned = source_maps(src, top_k, src.off[0], d / 2, f, &p.map[0]) &&
+                  source_maps(src, top_k, src.off[3], d / 2, f, &p.map[8]);
+    }
     if (sg) {
         p.has_shared = 1;
         p.shared_bits = (int)sg->bits;
@@ -286,16 +312,21 @@ static tf_status phase1_launch(tf_context* ctx, const ExpertSource& src, const v
         p.sg = AffineMat{static_cast<const uint8_t*>(sg->weights), sg->scales, sg->biases};
         p.su = AffineMat{static_cast<const uint8_t*>(su->weights), su->scales, su->biases};
         p.shared_act = static_cast<__half*>(shared_act);
-        aligned = aligned && aligned16(sg->weights) && aligned16(su->weights) && aligned4(sg->scales) &&
-                  aligned4(sg->biases) && aligned4(su->scales) && aligned4(su->biases);
+        const uint64_t rb = row_bytes((int)d, (int)sg->bits);
+        aligned = make_weight_map(&p.map[16], sg->weights, rb, sg->rows, 1, 0) &&
+                  make_weight_map(&p.map[17], su->weights, rb, su->rows, 1, 0) && aligned;
     }
     p.aligned = aligned;
     p.x_aligned = aligned16(x);
     p.err = ctx->d_err;
     p.fjobs = (int)f / 8;
     p.sched = make_sched((int)top_k * p.fjobs, units_for_K((int)d, 4), sg ? (int)sg->rows / 8 : 0,
-                         sg ? units_for_K((int)d, (int)sg->bits) : 1);
+                         sg ? units_for_K((int)d, (int)sg->bits) : 1, ctx->num_sms);
     const int sj = p.sched.S_total;
+    if (build_only) {
+        *build_only = p;
+        return TF_OK;
+    }
     return dispatch_scale(st, [&](auto tag) {
         using ST = decltype(tag);
         return launch_engine<Phase1Policy<ST>, ST>(ctx, p, Phase1Policy<ST>::x_bytes((int)d), sj, cs, name);
@@ -305,7 +336,7 @@ static tf_status phase1_launch(tf_context* ctx, const ExpertSource& src, const v
 static tf_status phase2_launch(tf_context* ctx, const ExpertSource& src, const void* acts, const void* rw,
                                const void* residual, void* y, uint32_t d, uint32_t f, uint32_t top_k,
                                const tf_affine_matrix* sdn, const void* shared_act, tf_scale_type st, cudaStream_t cs,
-                               const char* name) {
+                               const char* name, Phase2Params* build_only = nullptr) {
     if (!y || (top_k && (!acts || !rw))) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
     if (d == 0 || d % 64 || f == 0 || f % 64) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: d and f must be positive multiples of 64", name);
     if (acts && !aligned16(acts)) return fail(ctx, TF_ERR_MISALIGNED, "%s: acts must be 16-byte aligned", name);
@@ -320,7 +351,7 @@ static tf_status phase2_launch(tf_context* ctx, const ExpertSource& src, const v
     p.routing_w = static_cast<const __half*>(rw);
     p.residual = static_cast<const __half*>(residual);
     p.y = static_cast<__half*>(y);
-    bool aligned = top_k ? source_aligned(src, top_k, false) : true;
+    bool aligned = top_k ? source_maps(src, top_k, src.off[6], f / 2, d, &p.map[0]) : true;
     size_t xb;
     if (sdn) {
         p.has_shared = 1;
@@ -328,15 +359,20 @@ static tf_status phase2_launch(tf_context* ctx, const ExpertSource& src, const v
         p.Fs = (int)sdn->cols;
         p.sd = AffineMat{static_cast<const uint8_t*>(sdn->weights), sdn->scales, sdn->biases};
         p.shared_act = static_cast<const __half*>(shared_act);
-        aligned = aligned && aligned16(sdn->weights) && aligned4(sdn->scales) && aligned4(sdn->biases);
+        aligned = make_weight_map(&p.map[8], sdn->weights, row_bytes((int)sdn->cols, (int)sdn->bits), sdn->rows, 1, 0) &&
+                  aligned;
         if (!aligned16(shared_act)) return fail(ctx, TF_ERR_MISALIGNED, "%s: shared act must be 16-byte aligned", name);
     }
     p.aligned = aligned;
     p.err = ctx->d_err;
     const int U = (int)top_k * units_for_K((int)f, 4) + (sdn ? units_for_K((int)sdn->cols, (int)sdn->bits) : 0);
     p.upf = units_for_K((int)f, 4);
-    p.sched = make_sched(((int)d + 15) / 16, U);
+    p.sched = make_sched(((int)d + 15) / 16, U, 0, 1, ctx->num_sms);
     const int sj = p.sched.S_total;
+    if (build_only) {
+        *build_only = p;
+        return TF_OK;
+    }
     return dispatch_scale(st, [&](auto tag) {
         using ST = decltype(tag);
         xb = Phase2Policy<ST>::x_bytes((int)top_k, (int)f, sdn ? (int)sdn->cols : 0);
@@ -404,6 +440,77 @@ tf_status tf_shared_expert(tf_context* ctx, const void* x, const tf_affine_matri
                          "tf_shared_expert");
 }
 
+// Fused single-launch layer (tf_fused.cuh).  Builds the four phase
+// parameter blocks with the same builders as the separate entry points.
+static tf_status decode_layer_fused(tf_context* ctx, const tf_moe_layer* L, const void* router_x, const void* x,
+                                    const void* residual, void* y, uint32_t* idx, __half* w, cudaStream_t cs) {
+    const char* name = "tf_moe_decode_layer";
+    const bool shared = L->shared_gate.rows != 0;
+    LayerParams lp;
+    memset(&lp, 0, sizeof(lp));
+    tf_status s = router_launch(ctx, L->router_w, L->router_s, L->router_b, router_x, L->eff_scale,
+                                L->per_expert_scale, idx, w, L->num_experts, L->d, L->top_k, L->scale_type, cs, &lp.r);
+    if (s) return s;
+    lp.r.fused = 1;
+    lp.r.replicas = 16;  // d_logits holds 64 x 256 floats
+    ExpertSource none;
+    memset(&none, 0, sizeof(none));
+    if (shared) {
+        s = phase1_launch(ctx, none, x, nullptr, L->d, 64, 0, &L->shared_gate, &L->shared_up, ctx->d_shared_act,
+                          L->scale_type, cs, name, &lp.sh);
+        if (s) return s;
+    }
+    ExpertSource src = make_source(L->expert_pool, L->expert_stride, L->num_experts, idx, nullptr, &L->offsets, L->top_k);
+    src.ids_in_smem = 1;
+    s = phase1_launch(ctx, src, x, ctx->d_acts, L->d, L->f, L->top_k, nullptr, nullptr, nullptr, L->scale_type, cs,
+                      name, &lp.p1);
+    if (s) return s;
+    s = phase2_launch(ctx, src, ctx->d_acts, w, residual, y, L->d, L->f, L->top_k, shared ? &L->shared_down : nullptr,
+                      ctx->d_shared_act, L->scale_type, cs, name, &lp.p2);
+    if (s) return s;
+    lp.p2.rw_in_smem = 1;
+    lp.has_shared = shared ? 1 : 0;
+    lp.bar_count = ctx->d_ticket + 1;
+    lp.bar_flags = ctx->d_flags;
+    lp.out_idx = idx;
+    lp.out_w = w;
+    lp.err = ctx->d_err;
+    return dispatch_scale(L->scale_type, [&](auto tag) -> tf_status {
+        using ST = decltype(tag);
+        size_t xb = RouterPolicy<ST>::x_bytes((int)L->d);
+        xb = std::max(xb, Phase1Policy<ST>::x_bytes((int)L->d));
+        xb = std::max(xb, Phase2Policy<ST>::x_bytes((int)L->top_k, (int)L->f, shared ? (int)L->shared_down.cols : 0));
+        const size_t smem = engine_fixed_smem() + xb + 1024;
+        static size_t static_smem = (size_t)-1;
+        if (static_smem == (size_t)-1) {
+            cudaFuncAttributes fa;
+            cudaError_t e = cudaFuncGetAttributes(&fa, fused_layer_kernel<ST>);
+            if (e != cudaSuccess) return cuda_check(ctx, e, name);
+            static_smem = fa.sharedSizeBytes;
+        }
+        const size_t limit = ctx->max_smem_optin - static_smem;
+        if (smem > limit) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: activations too large for shared memory", name);
+        static bool configured[64] = {};
+        if (!configured[ctx->device & 63]) {
+            cudaError_t e = cudaFuncSetAttribute(fused_layer_kernel<ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)limit);
+            if (e != cudaSuccess) return cuda_check(ctx, e, name);
+            configured[ctx->device & 63] = true;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)ctx->num_sms);
+        cfg.blockDim = dim3(kWarps * 32);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = cs;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident: the grid barrier is safe
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cuda_check(ctx, cudaLaunchKernelEx(&cfg, fused_layer_kernel<ST>, lp), name);
+    });
+}
+
 tf_status tf_moe_decode_layer(tf_context* ctx, const tf_moe_layer* L, const void* router_x, const void* x,
                               const void* residual, void* y, void* out_idx, void* out_w, void* stream) {
     tf_status s = check_ctx(ctx);
@@ -423,6 +530,9 @@ tf_status tf_moe_decode_layer(tf_context* ctx, const tf_moe_layer* L, const void
     cudaStream_t cs = static_cast<cudaStream_t>(stream);
     uint32_t* idx = out_idx ? static_cast<uint32_t*>(out_idx) : ctx->d_idx;
     __half* w = out_w ? static_cast<__half*>(out_w) : ctx->d_w;
+    // TFCUDA_UNFUSED=1 selects the three-launch path (same arithmetic).
+    static const bool unfused = getenv("TFCUDA_UNFUSED") && getenv("TFCUDA_UNFUSED")[0] == '1';
+    if (!unfused) return decode_layer_fused(ctx, L, router_x, x, residual, y, idx, w, cs);
     s = router_launch(ctx, L->router_w, L->router_s, L->router_b, router_x, L->eff_scale, L->per_expert_scale, idx, w,
                       L->num_experts, L->d, L->top_k, L->scale_type, cs);
     if (s) return s;
@@ -439,6 +549,6 @@ tf_status tf_moe_decode_layer(tf_context* ctx, const tf_moe_layer* L, const void
 
 #ifdef TF_TRACE
 extern "C" TF_API int tf_debug_trace(unsigned long long* out, int n) {
-    return (int)cudaMemcpyFromSymbol(out, tf::g_tf_trace, sizeof(unsigned long long) * 8 * n);
+    return (int)cudaMemcpyFromSymbol(out, tf::g_tf_trace, sizeof(unsigned long long) * 16 * n);
 }
 #endif

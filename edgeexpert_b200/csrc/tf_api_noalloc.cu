@@ -101,9 +101,9 @@ tf_status tf_router_topk_noalloc(const void* W, const void* S, const void* B, co
     p.ticket = reinterpret_cast<unsigned int*>(s->scratch + kNoAllocTicketOff);  // left at 0 by every launch
     p.out_idx = static_cast<uint32_t*>(out_idx);
     p.out_w = static_cast<__half*>(out_w);
-    p.aligned = aligned16(W) && aligned4(S) && aligned4(B) && (((uint64_t)E * (d / 64)) % 2 == 0);
+    p.aligned = make_weight_map(&p.map, W, d, E, 1, 0);
     p.err = reinterpret_cast<uint32_t*>(s->scratch + kNoAllocErrOff);
-    p.sched = make_sched(((int)E + 15) / 16, units_for_K((int)d, 8));
+    p.sched = make_sched(((int)E + 15) / 16, units_for_K((int)d, 8), 0, 1, ctx.num_sms);
     const int sj = p.sched.S_total;
     cudaStream_t cs = static_cast<cudaStream_t>(stream);
     if (st == TF_SCALE_F16)

@@ -18,7 +18,8 @@ struct tf_context {
     // Device workspace (allocated once at create time).
     uint32_t* d_err = nullptr;         // error bits raised by kernels
     float* d_logits = nullptr;         // [kMaxRouterExperts] router logits
-    unsigned int* d_ticket = nullptr;  // router selection ticket (always left 0)
+    unsigned int* d_ticket = nullptr;  // router selection ticket (always left 0), barrier count
+    unsigned int* d_flags = nullptr;   // fused-layer barrier release flags, 128 B apart
     uint32_t* d_idx = nullptr;         // [8] decode routing ids
     __half* d_w = nullptr;             // [8] decode routing weights
     __half* d_acts = nullptr;          // [8][kMaxF] routed activations
@@ -53,30 +54,28 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 inline bool aligned2(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 1u) == 0; }
 inline bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
 
-// Launch one engine instantiation: picks the ring depth that fits, sets the
-// dynamic shared-memory attribute once per instantiation, sizes the grid to
-// min(super-jobs, SMs) (one 256-thread CTA per SM).
+// Largest dynamic shared memory an engine launch may request.
 template <class Pol, typename ST>
-tf_status launch_engine(tf_context* ctx, typename Pol::Params p, size_t x_bytes, int superjobs,
-                        cudaStream_t stream, const char* name) {
-    if (superjobs <= 0) return TF_OK;
-    // Dynamic shared memory may use what the kernel's static shared memory leaves.
+size_t engine_smem_limit(tf_context* ctx) {
     static size_t static_smem = (size_t)-1;
     if (static_smem == (size_t)-1) {
         cudaFuncAttributes fa;
-        cudaError_t e = cudaFuncGetAttributes(&fa, engine_kernel<Pol, ST>);
-        if (e != cudaSuccess) return cuda_check(ctx, e, name);
+        if (cudaFuncGetAttributes(&fa, engine_kernel<Pol, ST>) != cudaSuccess) return 0;
         static_smem = fa.sharedSizeBytes;
     }
-    const size_t limit = ctx->max_smem_optin - static_smem;
-    int ns = 3;
-    size_t smem = engine_fixed_smem(ns) + x_bytes;
-    if (smem > limit) {
-        ns = 2;
-        smem = engine_fixed_smem(ns) + x_bytes;
-    }
+    return ctx->max_smem_optin - static_smem;
+}
+
+// Launch one engine instantiation: sets the dynamic shared-memory attribute
+// once per instantiation and device, sizes the grid to min(super-jobs, SMs)
+// (one kWarps-warp CTA per SM).
+template <class Pol, typename ST>
+tf_status launch_engine(tf_context* ctx, const typename Pol::Params& p, size_t x_bytes, int superjobs,
+                        cudaStream_t stream, const char* name) {
+    if (superjobs <= 0) return TF_OK;
+    const size_t limit = engine_smem_limit<Pol, ST>(ctx);
+    const size_t smem = engine_fixed_smem() + x_bytes + 1024;  // + slack for 1 KB alignment
     if (smem > limit) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: activation too large for shared memory", name);
-    p.ns = ns;
     static bool configured[64] = {};  // per instantiation, per device
     const int dev = ctx->device & 63;
     if (!configured[dev]) {
@@ -88,6 +87,47 @@ tf_status launch_engine(tf_context* ctx, typename Pol::Params p, size_t x_bytes,
     const int grid = superjobs < ctx->num_sms ? superjobs : ctx->num_sms;
     engine_kernel<Pol, ST><<<grid, kWarps * 32, smem, stream>>>(p);
     return cuda_check(ctx, cudaGetLastError(), name);
+}
+
+// ---------------------------------------------------------------------------
+// TMA descriptors.  A weight tensor is viewed as uint8 [depth][rows][row_bytes]
+// (depth = experts of a pool or matrices of a batch) and read in boxes of
+// 8 rows x 128 bytes with the 128-byte swizzle.
+// ---------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_tiled_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    }
+    return fn;
+}
+
+// Returns false when the tensor cannot be described (the caller then takes the
+// synchronous copy path).
+inline bool make_weight_map(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows, uint64_t depth,
+                            uint64_t depth_stride) {
+    memset(m, 0, sizeof(*m));
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn || !aligned16(base) || row_bytes % 16 || rows == 0 || depth == 0) return false;
+    const uint64_t ds = depth > 1 ? depth_stride : row_bytes * rows;
+    if (ds % 16 || ds >= (1ull << 40)) return false;
+    cuuint64_t dims[3] = {row_bytes, rows, depth};
+    cuuint64_t strides[2] = {row_bytes, ds};
+    cuuint32_t box[3] = {(cuuint32_t)kBox, (cuuint32_t)kBoxRows, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace tf

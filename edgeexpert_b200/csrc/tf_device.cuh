@@ -24,23 +24,21 @@
 namespace tf {
 
 constexpr int kGroup = 64;
-constexpr int kWarps = 8;             // consumer warps per CTA
+constexpr int kWarps = 12;            // consumer warps per CTA (one stage each)
 constexpr int kRowsPerTile = 16;      // MMA M
 constexpr int kMaxTok = 8;            // MMA N
-// Padded shared-memory row strides (bytes).  int4 tiles are read with 8-byte
-// loads in half-warps of 4 rows x 4 lanes: a stride of 8 (mod 32) words puts
-// those 4 rows on disjoint banks.  int8 tiles are read with 16-byte loads in
-// quarter-warps of 2 rows: 16 (mod 32) words.
-constexpr int kStageStride4 = 416;
-constexpr int kStageStride8 = 448;
-// Stage = 16 padded weight rows, then 32 slots of 32 bytes holding each row's
-// scales and biases for the unit's groups (4-byte-aligned superset copy).
-constexpr int kScaleOff = kRowsPerTile * kStageStride8;
-constexpr int kScaleSlot = 32;
-constexpr int kStageBytes = kScaleOff + 2 * kRowsPerTile * kScaleSlot;
-constexpr uint32_t kStageArrivals = 33;  // 1 expect_tx arrive + 32 cp.async arrives
-constexpr int kChunkGroups4 = 11;     // groups per unit, int4 (352 B per row)
-constexpr int kChunkGroups8 = 6;      // groups per unit, int8 (384 B per row)
+// Weight tiles arrive by TMA in boxes of 8 rows x 128 bytes with the 128-byte
+// swizzle (16-byte chunk c of row r stored at chunk c ^ (r % 8)), which makes
+// the fragment reads bank-conflict free without padding.
+constexpr int kBox = 128;                       // bytes of one box row
+constexpr int kBoxRows = 8;
+constexpr int kBoxBytes = kBox * kBoxRows;      // 1 KB, 1 KB aligned in smem
+constexpr int kMaxBoxes = 6;                    // boxes per half-tile per unit (768 B / row)
+constexpr int kHalfBytes = kMaxBoxes * kBoxBytes;
+constexpr int kMaxScaleGroups = 64;             // full-row scale copies up to K = 64 groups
+constexpr int kScaleArr = kBoxRows * kMaxScaleGroups * 2;
+// Stage: [half A: rows 0-7][half B: rows 8-15][scales A][biases A][scales B][biases B]
+constexpr int kStageBytes = 2 * kHalfBytes + 4 * kScaleArr;  // 16 KB
 constexpr uint32_t kSpinLimit = 1u << 22;  // bounded mbarrier wait (error flag after)
 
 // Error bits written to the context's device status word.
@@ -134,6 +132,20 @@ __device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
     asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Bring a TMA descriptor (kernel-parameter resident) into the descriptor cache.
+__device__ __forceinline__ void prefetch_tmap(const void* tmap) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// 3-D tiled TMA load (no multicast) into this CTA's shared memory.
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int x, int y, int z, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_u32(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t magic) {
     uint32_t r;
     asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(magic));
@@ -143,6 +155,12 @@ __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint3
 __device__ __forceinline__ uint32_t hsub2_u(uint32_t a, uint32_t b) {
     uint32_t r;
     asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t hmul2_u(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
     return r;
 }
 
@@ -180,6 +198,18 @@ __device__ __forceinline__ void dq4(uint32_t w, uint32_t p[4]) {
     p[3] = hfma2_u(lop3_and_or(w8, 0x00F000F0u, kMagic), kSixteenth, kNeg64);  // k3,k7
 }
 
+// Offset-folded variant: P0/P2 = 1024 + q, P1/P3 = 1024 + 16 q (exact fp16).
+// Paired with x staged with its odd pairs divided by 16, the MMA yields
+// sum(q*x) + 1024 * sum(staged x); the constant is removed per group.
+__device__ __forceinline__ void dq4_folded(uint32_t w, uint32_t p[4]) {
+    constexpr uint32_t kMagic = 0x64006400u;
+    const uint32_t w8 = w >> 8;
+    p[0] = lop3_and_or(w, 0x000F000Fu, kMagic);
+    p[1] = lop3_and_or(w, 0x00F000F0u, kMagic);
+    p[2] = lop3_and_or(w8, 0x000F000Fu, kMagic);
+    p[3] = lop3_and_or(w8, 0x00F000F0u, kMagic);
+}
+
 // One octet of int8 codes (w0 = k0..3, w1 = k4..7) -> P0..P3.
 __device__ __forceinline__ void dq8(uint32_t w0, uint32_t w1, uint32_t p[4]) {
     constexpr uint32_t kMagic = 0x64006400u;
@@ -203,9 +233,12 @@ __host__ __device__ constexpr int x_words_stride(int K) {
 
 // Per-group sums from the staged octet-pair words: one warp per (token,
 // group); the 32 words of a group hold its 64 values, one word per lane.
-// Callers synchronise the CTA between writing `xs` and calling this.
-__device__ __forceinline__ void stage_xsum_smem(const uint32_t* xs, int ws, int ntok, int K, float* xsum, int tid,
-                                                int nthreads) {
+// With `fold` the odd pairs (words 1 and 3 of each octet) hold x/16 (see
+// stage_words); then  xsum = true sum of x  and  xcorr = 1024 * (sum of the
+// staged values), the exact offset the folded MMA adds.  Callers synchronise
+// the CTA between writing `xs` and calling this.
+__device__ __forceinline__ void stage_xsum_smem(const uint32_t* xs, int ws, int ntok, int K, float* xsum,
+                                                float* xcorr, bool fold, int tid, int nthreads) {
     const int ng = K / kGroup;
     const int warp = tid >> 5, lane = tid & 31, nw = nthreads >> 5;
     for (int i = warp; i < ntok * ng; i += nw) {
@@ -213,34 +246,45 @@ __device__ __forceinline__ void stage_xsum_smem(const uint32_t* xs, int ws, int 
         const uint32_t w = xs[t * ws + g * 32 + lane];
         const __half2 h = *reinterpret_cast<const __half2*>(&w);
         float s = __low2float(h) + __high2float(h);
-        for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-        if (lane == 0) xsum[t * ng + g] = s;
+        float odd = (fold && (lane & 1)) ? s : 0.f;
+        for (int off = 16; off; off >>= 1) {
+            s += __shfl_xor_sync(0xffffffffu, s, off);
+            odd += __shfl_xor_sync(0xffffffffu, odd, off);
+        }
+        if (lane == 0) {
+            xsum[t * ng + g] = s + 15.f * odd;
+            if (fold) xcorr[t * ng + g] = 1024.f * s;
+        }
     }
 }
 
 // Cooperative staging of `ntok` activation rows (x[t*x_row_stride + k]) into
 // the octet-pair layout xs[t*x_words_stride(K) + ...] by `nthreads` threads.
 // 16-byte loads when `vec` (row starts 16-byte aligned), else 2-byte loads.
-// No barrier inside: callers synchronise before stage_xsum_smem.
+// With `fold`, the odd pairs P1 = (x1, x5) and P3 = (x3, x7) are stored
+// divided by 16 (exact in fp16 outside the subnormal range) for the
+// offset-folded MMA (dq4_folded).  No barrier inside.
 __device__ __forceinline__ void stage_words(const __half* __restrict__ x, int x_row_stride, int ntok, int K,
-                                            uint32_t* xs, bool vec, int tid, int nthreads) {
+                                            uint32_t* xs, bool vec, bool fold, int tid, int nthreads) {
     const int octets = K / 8;
     const int ws = x_words_stride(K);
+    const __half2 sixteenth = __float2half2_rn(0.0625f);
     for (int i = tid; i < ntok * octets; i += nthreads) {
         const int t = i / octets, q = i - t * octets;
         const __half* src = x + (size_t)t * x_row_stride + q * 8;
         __half h[8];
         if (vec) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(src);
+            const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(src));  // L2: may be another CTA's output
             memcpy(h, &raw, 16);
         } else {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) h[j] = src[j];
+            for (int j = 0; j < 8; ++j) h[j] = __ldcg(src + j);
         }
         uint32_t* dst = xs + t * ws + q * 4;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             __half2 p = __halves2half2(h[j], h[j + 4]);
+            if (fold && (j & 1)) p = __hmul2(p, sixteenth);
             dst[j] = *reinterpret_cast<uint32_t*>(&p);
         }
     }

@@ -2,7 +2,7 @@
 // Each policy maps the reference operator's output rows onto 16-row jobs.
 //
 // Policy interface:
-//   Params                      kernel parameters; carry `Sched sched`, `ns`,
+//   Params                      kernel parameters; carry `Sched sched`,
 //                               `aligned`, `err`
 //   stage_pre(p, tid)           tiny per-CTA set-up needed to issue copies
 //   stage_x(p, xa, tid, nt)     stage activations (all threads; may barrier)
@@ -13,10 +13,7 @@
 
 namespace tf {
 
-__device__ __forceinline__ const uint8_t* engine_xarea(int ns) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    return smem + engine_fixed_smem(ns);
-}
+__device__ __forceinline__ const uint8_t* engine_xarea() { return engine_smem_base() + engine_fixed_smem(); }
 
 // ===========================================================================
 // Plain affine GEMV, Y[tok][row] = sum_k W[row][k] * X[tok][k]
@@ -24,6 +21,7 @@ __device__ __forceinline__ const uint8_t* engine_xarea(int ns) {
 // a common activation block of up to 8 tokens).
 // ===========================================================================
 struct GemvParams {
+    CUtensorMap map;  // W as [batch][M][row_bytes], box 8 rows x 128 B
     const uint8_t* W;
     const void* S;
     const void* B;
@@ -36,7 +34,7 @@ struct GemvParams {
     __half* y;
     int y_row_stride;     // elements between tokens of y
     long long y_bstride;  // elements between matrices of y
-    int aligned, x_aligned, ns;
+    int aligned, x_aligned;
     uint32_t* err;
     Sched sched;
 };
@@ -44,16 +42,21 @@ struct GemvParams {
 template <typename ST>
 struct GemvPolicy {
     using Params = GemvParams;
-    static size_t x_bytes(int K) {
-        return (size_t)kMaxTok * x_words_stride(K) * 4 + (size_t)kMaxTok * (K / kGroup) * 4;
+    // [ntok][ws] words, [ntok][K/64] sums, [ntok][K/64] folded-offset corrections
+    static size_t x_bytes(int K, int ntok) {
+        return (size_t)ntok * x_words_stride(K) * 4 + 2 * (size_t)ntok * (K / kGroup) * 4;
     }
-    __device__ static void stage_pre(const Params&, int) {}
+    __device__ static void stage_pre(const Params& p, int tid) {
+        if (tid == 0 && p.aligned) prefetch_tmap(&p.map);
+    }
     __device__ static void stage_x(const Params& p, uint8_t* xa, int tid, int nt) {
         uint32_t* xs = reinterpret_cast<uint32_t*>(xa);
-        float* xsum = reinterpret_cast<float*>(xs + kMaxTok * x_words_stride(p.K));
-        stage_words(p.x, p.x_row_stride, p.ntok, p.K, xs, p.x_aligned, tid, nt);
+        float* xsum = reinterpret_cast<float*>(xs + p.ntok * x_words_stride(p.K));
+        float* xcorr = xsum + p.ntok * (p.K / kGroup);
+        const bool fold = p.ntok == 1;
+        stage_words(p.x, p.x_row_stride, p.ntok, p.K, xs, p.x_aligned, fold, tid, nt);
         __syncthreads();
-        stage_xsum_smem(xs, x_words_stride(p.K), p.ntok, p.K, xsum, tid, nt);
+        stage_xsum_smem(xs, x_words_stride(p.K), p.ntok, p.K, xsum, xcorr, fold, tid, nt);
     }
     __device__ static bool unit(const Params& p, int job, int u, SegDesc* d, int* chunk) {
         const int b = job / p.tiles, tile = job - b * p.tiles;
@@ -61,6 +64,8 @@ struct GemvPolicy {
         const ST* S = reinterpret_cast<const ST*>(p.S) + (size_t)b * p.sb_bstride;
         const ST* B = reinterpret_cast<const ST*>(p.B) + (size_t)b * p.sb_bstride;
         d->WA = d->WB = W;
+        d->mapA = d->mapB = &p.map;
+        d->eA = d->eB = b;
         d->SA = d->SB = S;
         d->BA = d->BB = B;
         d->rowA = tile * 16;
@@ -69,9 +74,11 @@ struct GemvPolicy {
         d->nB = max(0, min(8, p.M - d->rowB));
         d->K = p.K;
         d->bits = p.bits;
-        const uint32_t* xs = reinterpret_cast<const uint32_t*>(engine_xarea(p.ns));
+        const uint32_t* xs = reinterpret_cast<const uint32_t*>(engine_xarea());
         d->xs = xs;
-        d->xsum = reinterpret_cast<const float*>(xs + kMaxTok * x_words_stride(p.K));
+        d->xsum = reinterpret_cast<const float*>(xs + p.ntok * x_words_stride(p.K));
+        d->xcorr = d->xsum + p.ntok * (p.K / kGroup);
+        d->xfold = p.ntok == 1;
         d->xws = x_words_stride(p.K);
         d->ntok = p.ntok;
         d->mult = 1.0f;
@@ -105,6 +112,7 @@ struct ExpertSource {
     int num_experts;
     const uint8_t* blobs[8];
     uint32_t off[9];  // gate_w gate_s gate_b up_w up_s up_b down_w down_s down_b
+    int ids_in_smem;  // fused layer: ids already selected into ids_smem()
 };
 
 // Device expert ids are copied into shared memory once per CTA (stage_ids)
@@ -114,8 +122,14 @@ __device__ __forceinline__ uint32_t* ids_smem() {
     return ids;
 }
 
+// Routing weights of the fused layer, selected per CTA into shared memory.
+__device__ __forceinline__ __half* rw_smem() {
+    __shared__ __half rw[8];
+    return rw;
+}
+
 __device__ __forceinline__ void stage_ids(const ExpertSource& es, int top_k, int tid) {
-    if (es.ids != nullptr && tid < top_k) ids_smem()[tid] = __ldg(es.ids + tid);
+    if (es.ids != nullptr && !es.ids_in_smem && tid < top_k) ids_smem()[tid] = __ldg(es.ids + tid);
 }
 
 __device__ __forceinline__ const uint8_t* expert_blob(const ExpertSource& es, int slot, uint32_t* err) {
@@ -145,6 +159,9 @@ struct AffineMat {
 // so one thread ends up holding gate and up of one output.
 // ===========================================================================
 struct Phase1Params {
+    // pool mode: map[0] gate_w / map[8] up_w of all experts ([E][F][D/2]);
+    // blob mode: map[slot] / map[8 + slot]; shared expert: map[16] / map[17].
+    CUtensorMap map[18];
     ExpertSource src;
     int D, F, top_k, fjobs;  // fjobs = F / 8
     const __half* x;
@@ -152,7 +169,7 @@ struct Phase1Params {
     int has_shared, shared_bits, Fs;
     AffineMat sg, su;
     __half* shared_act;  // [Fs]
-    int aligned, x_aligned, ns;
+    int aligned, x_aligned;
     uint32_t* err;
     Sched sched;
 };
@@ -160,19 +177,29 @@ struct Phase1Params {
 template <typename ST>
 struct Phase1Policy {
     using Params = Phase1Params;
-    static size_t x_bytes(int D) { return (size_t)x_words_stride(D) * 4 + (size_t)(D / kGroup) * 4; }
-    __device__ static void stage_pre(const Params& p, int tid) { stage_ids(p.src, p.top_k, tid); }
+    static size_t x_bytes(int D) { return (size_t)x_words_stride(D) * 4 + 2 * (size_t)(D / kGroup) * 4; }
+    __device__ static void stage_pre(const Params& p, int tid) {
+        stage_ids(p.src, p.top_k, tid);
+        if (!p.aligned) return;
+        const bool pool = p.src.ids != nullptr;
+        const int nm = p.top_k ? (pool ? 1 : p.top_k) : 0;
+        if (tid < nm) prefetch_tmap(&p.map[tid]);
+        else if (tid >= 32 && tid < 32 + nm) prefetch_tmap(&p.map[8 + tid - 32]);
+        else if (p.has_shared && (tid == 64 || tid == 65)) prefetch_tmap(&p.map[16 + tid - 64]);
+    }
     __device__ static void stage_x(const Params& p, uint8_t* xa, int tid, int nt) {
         uint32_t* xs = reinterpret_cast<uint32_t*>(xa);
         float* xsum = reinterpret_cast<float*>(xs + x_words_stride(p.D));
-        stage_words(p.x, p.D, 1, p.D, xs, p.x_aligned, tid, nt);
+        stage_words(p.x, p.D, 1, p.D, xs, p.x_aligned, true, tid, nt);
         __syncthreads();
-        stage_xsum_smem(xs, x_words_stride(p.D), 1, p.D, xsum, tid, nt);
+        stage_xsum_smem(xs, x_words_stride(p.D), 1, p.D, xsum, xsum + p.D / kGroup, true, tid, nt);
     }
     __device__ static bool unit(const Params& p, int job, int u, SegDesc* d, int* chunk) {
-        const uint32_t* xs = reinterpret_cast<const uint32_t*>(engine_xarea(p.ns));
+        const uint32_t* xs = reinterpret_cast<const uint32_t*>(engine_xarea());
         d->xs = xs;
         d->xsum = reinterpret_cast<const float*>(xs + x_words_stride(p.D));
+        d->xcorr = d->xsum + p.D / kGroup;
+        d->xfold = 1;
         d->xws = x_words_stride(p.D);
         d->ntok = 1;
         d->mult = 1.0f;
@@ -185,6 +212,10 @@ struct Phase1Policy {
             d->rowA = d->rowB = f0;
             d->nA = d->nB = b ? 8 : 0;
             if (!b) b = p.src.pool ? p.src.pool : p.src.blobs[0];
+            const bool pool = p.src.ids != nullptr;
+            d->mapA = &p.map[pool ? 0 : slot];
+            d->mapB = &p.map[pool ? 8 : 8 + slot];
+            d->eA = d->eB = pool ? (int)ids_smem()[slot] : 0;
             d->WA = b + p.src.off[0];
             d->SA = b + p.src.off[1];
             d->BA = b + p.src.off[2];
@@ -196,6 +227,9 @@ struct Phase1Policy {
             d->bits = p.shared_bits;
             d->rowA = d->rowB = f0;
             d->nA = d->nB = 8;
+            d->mapA = &p.map[16];
+            d->mapB = &p.map[17];
+            d->eA = d->eB = 0;
             d->WA = p.sg.W;
             d->SA = p.sg.S;
             d->BA = p.sg.B;
@@ -234,6 +268,9 @@ struct Phase1Policy {
 // [top_k][F/64], then the shared act words [ws(Fs)] and sums [Fs/64].
 // ===========================================================================
 struct Phase2Params {
+    // pool mode: map[0] down_w of all experts ([E][D][F/2]); blob mode:
+    // map[slot]; shared expert down: map[8].
+    CUtensorMap map[9];
     ExpertSource src;
     int D, F, top_k, upf;     // upf = units per routed down row (F)
     const __half* acts;       // [top_k][F]
@@ -243,7 +280,8 @@ struct Phase2Params {
     int has_shared, shared_bits, Fs;
     AffineMat sd;
     const __half* shared_act;  // [Fs]
-    int aligned, ns;
+    int rw_in_smem;            // fused layer: routing weights in rw_smem()
+    int aligned;
     uint32_t* err;
     Sched sched;
 };
@@ -252,26 +290,37 @@ template <typename ST>
 struct Phase2Policy {
     using Params = Phase2Params;
     __host__ __device__ static size_t routed_words(int top_k, int F) { return (size_t)top_k * x_words_stride(F); }
+    // routed: [top_k][ws] words, [top_k][F/64] sums, [top_k][F/64] corrections;
+    // shared (16-byte aligned): [ws] words, [Fs/64] sums, [Fs/64] corrections
     __host__ __device__ static size_t shared_off(int top_k, int F) {
-        return ((routed_words(top_k, F) * 4 + (size_t)top_k * (F / kGroup) * 4) + 15) / 16 * 16;
+        return ((routed_words(top_k, F) * 4 + 2 * (size_t)top_k * (F / kGroup) * 4) + 15) / 16 * 16;
     }
     static size_t x_bytes(int top_k, int F, int Fs) {
-        return shared_off(top_k, F) + (Fs > 0 ? (size_t)x_words_stride(Fs) * 4 + (size_t)(Fs / kGroup) * 4 : 0);
+        return shared_off(top_k, F) + (Fs > 0 ? (size_t)x_words_stride(Fs) * 4 + 2 * (size_t)(Fs / kGroup) * 4 : 0);
     }
-    __device__ static void stage_pre(const Params& p, int tid) { stage_ids(p.src, p.top_k, tid); }
+    __device__ static void stage_pre(const Params& p, int tid) {
+        stage_ids(p.src, p.top_k, tid);
+        if (!p.aligned) return;
+        const int nm = p.top_k ? (p.src.ids != nullptr ? 1 : p.top_k) : 0;
+        if (tid < nm) prefetch_tmap(&p.map[tid]);
+        else if (p.has_shared && tid == 32) prefetch_tmap(&p.map[8]);
+    }
     __device__ static void stage_x(const Params& p, uint8_t* xa, int tid, int nt) {
         uint32_t* xs = reinterpret_cast<uint32_t*>(xa);
         float* xsum = reinterpret_cast<float*>(xs + routed_words(p.top_k, p.F));
         uint32_t* xss = reinterpret_cast<uint32_t*>(xa + shared_off(p.top_k, p.F));
         float* xsums = reinterpret_cast<float*>(xss + x_words_stride(p.Fs));
-        if (p.top_k) stage_words(p.acts, p.F, p.top_k, p.F, xs, true, tid, nt);
-        if (p.has_shared) stage_words(p.shared_act, p.Fs, 1, p.Fs, xss, true, tid, nt);
+        if (p.top_k) stage_words(p.acts, p.F, p.top_k, p.F, xs, true, true, tid, nt);
+        if (p.has_shared) stage_words(p.shared_act, p.Fs, 1, p.Fs, xss, true, true, tid, nt);
         __syncthreads();
-        if (p.top_k) stage_xsum_smem(xs, x_words_stride(p.F), p.top_k, p.F, xsum, tid, nt);
-        if (p.has_shared) stage_xsum_smem(xss, x_words_stride(p.Fs), 1, p.Fs, xsums, tid, nt);
+        if (p.top_k)
+            stage_xsum_smem(xs, x_words_stride(p.F), p.top_k, p.F, xsum, xsum + p.top_k * (p.F / kGroup), true, tid,
+                            nt);
+        if (p.has_shared)
+            stage_xsum_smem(xss, x_words_stride(p.Fs), 1, p.Fs, xsums, xsums + p.Fs / kGroup, true, tid, nt);
     }
     __device__ static bool unit(const Params& p, int job, int u, SegDesc* d, int* chunk) {
-        const uint8_t* xa = engine_xarea(p.ns);
+        const uint8_t* xa = engine_xarea();
         const int d0 = job * 16;
         d->rowA = d0;
         d->rowB = d0 + 8;
@@ -285,6 +334,9 @@ struct Phase2Policy {
             if (!b) b = p.src.pool ? p.src.pool : p.src.blobs[0];
             d->nA = ok ? max(0, min(8, p.D - d0)) : 0;
             d->nB = ok ? max(0, min(8, p.D - d0 - 8)) : 0;
+            const bool pool = p.src.ids != nullptr;
+            d->mapA = d->mapB = &p.map[pool ? 0 : s];
+            d->eA = d->eB = pool ? (int)ids_smem()[s] : 0;
             d->WA = d->WB = b + p.src.off[6];
             d->SA = d->SB = b + p.src.off[7];
             d->BA = d->BB = b + p.src.off[8];
@@ -293,12 +345,16 @@ struct Phase2Policy {
             const uint32_t* xs = reinterpret_cast<const uint32_t*>(xa);
             d->xs = xs + (size_t)s * x_words_stride(p.F);
             d->xsum = reinterpret_cast<const float*>(xs + routed_words(p.top_k, p.F)) + s * (p.F / kGroup);
+            d->xcorr = d->xsum + p.top_k * (p.F / kGroup);
+            d->xfold = 1;
             d->xws = x_words_stride(p.F);
-            d->mult = __half2float(p.routing_w[s]);
+            d->mult = __half2float(p.rw_in_smem ? rw_smem()[s] : p.routing_w[s]);
         } else {
             *chunk = u - nr;
             d->nA = max(0, min(8, p.D - d0));
             d->nB = max(0, min(8, p.D - d0 - 8));
+            d->mapA = d->mapB = &p.map[8];
+            d->eA = d->eB = 0;
             d->WA = d->WB = p.sd.W;
             d->SA = d->SB = p.sd.S;
             d->BA = d->BB = p.sd.B;
@@ -307,6 +363,8 @@ struct Phase2Policy {
             const uint32_t* xss = reinterpret_cast<const uint32_t*>(xa + shared_off(p.top_k, p.F));
             d->xs = xss;
             d->xsum = reinterpret_cast<const float*>(xss + x_words_stride(p.Fs));
+            d->xcorr = d->xsum + p.Fs / kGroup;
+            d->xfold = 1;
             d->xws = x_words_stride(p.Fs);
             d->mult = 1.0f;
         }
@@ -336,6 +394,7 @@ struct Phase2Policy {
 // columns 0 and 1) so the tensor-core dot keeps ~22 bits of x~.
 // ===========================================================================
 struct RouterParams {
+    CUtensorMap map;  // W as [1][E][D], box 8 rows x 128 B
     const uint8_t* W;
     const void* S;
     const void* B;
@@ -347,7 +406,9 @@ struct RouterParams {
     unsigned int* ticket; // workspace counter, left at 0
     uint32_t* out_idx;
     __half* out_w;
-    int aligned, ns;
+    int fused;  // fused layer: write the logits only (selection runs per CTA later)
+    int replicas;  // copies of the logits written 256 floats apart (each CTA reads one)
+    int aligned;
     uint32_t* err;
     Sched sched;
 };
@@ -358,10 +419,15 @@ __device__ __forceinline__ void warp_topk_softmax(const float* logits, int E, in
     // Selection order = sort by (logit desc, expert id asc): identical to the
     // reference's insertion with strict '>' and ties to the lower id.
     constexpr int kPer = 8;  // E <= 256
+    // lane holds experts lane*8 .. lane*8+7: two 16-byte loads per lane
+    // (`logits` has room for 256 entries)
     float v[kPer];
-    for (int i = 0; i < kPer; ++i) {
-        const int e = lane + 32 * i;
-        v[i] = e < E ? __ldcg(logits + e) : -INFINITY;
+    {
+        const float4 a = __ldcg(reinterpret_cast<const float4*>(logits) + lane * 2);
+        const float4 b = __ldcg(reinterpret_cast<const float4*>(logits) + lane * 2 + 1);
+        const float t[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) v[i] = lane * kPer + i < E ? t[i] : -INFINITY;
     }
     float my_exp = 0.f;
     int my_e = -1;
@@ -370,8 +436,9 @@ __device__ __forceinline__ void warp_topk_softmax(const float* logits, int E, in
     for (int r = 0; r < k; ++r) {
         float bv = -INFINITY;
         int be = 0x7fffffff;
+#pragma unroll
         for (int i = 0; i < kPer; ++i) {
-            const int e = lane + 32 * i;
+            const int e = lane * kPer + i;
             if (e < E && (v[i] > bv || (v[i] == bv && e < be))) {
                 bv = v[i];
                 be = e;
@@ -392,7 +459,9 @@ __device__ __forceinline__ void warp_topk_softmax(const float* logits, int E, in
             my_e = be;
             my_exp = ex;
         }
-        if (be < E && (be & 31) == lane) v[be >> 5] = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i)
+            if (lane * kPer + i == be) v[i] = -INFINITY;
         if (be >= E) break;
     }
     if (lane < k && my_e >= 0) {
@@ -401,11 +470,51 @@ __device__ __forceinline__ void warp_topk_softmax(const float* logits, int E, in
     }
 }
 
+// CTA-parallel selection for E <= 256 experts (threads 0..255 take part;
+// every thread of the CTA must call it).  Expert e's rank = number of experts
+// ordered before it by (logit desc, id asc), the same order as the
+// reference's insertion (moe.metal:152-169).  Experts with rank < k are the
+// selection, in rank order; softmax over them, times the per-expert gain.
+// `scratch` = 256 floats of shared memory.
+__device__ __forceinline__ void cta_topk_softmax(const float* logits, int E, int k, const __nv_bfloat16* pes,
+                                                 uint32_t* out_idx, __half* out_w, float* scratch) {
+    const int e = threadIdx.x;
+    float v = -INFINITY;
+    if (e < 256) {
+        v = e < E ? __ldcg(logits + e) : -INFINITY;
+        scratch[e] = v;
+    }
+    __syncthreads();
+    int rank = 0;
+    if (e < E) {
+        for (int j = 0; j < E; ++j) {
+            const float o = scratch[j];
+            rank += (o > v || (o == v && j < e)) ? 1 : 0;
+        }
+    }
+    __syncthreads();  // everyone done reading scratch
+    if (e < E && rank < k) {
+        out_idx[rank] = (uint32_t)e;
+        scratch[rank] = v;  // selected logits in rank order
+    }
+    __syncthreads();
+    if (e < k) {
+        const float vmax = scratch[0];
+        float sum = 0.f;
+        for (int r = 0; r < k; ++r) sum += expf(scratch[r] - vmax);
+        const uint32_t ex = out_idx[e];
+        out_w[e] = __float2half_rn(expf(scratch[e] - vmax) / sum * __bfloat162float(pes[ex]));
+    }
+    __syncthreads();
+}
+
 template <typename ST>
 struct RouterPolicy {
     using Params = RouterParams;
     static size_t x_bytes(int D) { return (size_t)2 * x_words_stride(D) * 4 + (size_t)2 * (D / kGroup) * 4; }
-    __device__ static void stage_pre(const Params&, int) {}
+    __device__ static void stage_pre(const Params& p, int tid) {
+        if (tid == 0 && p.aligned) prefetch_tmap(&p.map);
+    }
     __device__ static void stage_x(const Params& p, uint8_t* xa, int tid, int nt) {
         uint32_t* xs = reinterpret_cast<uint32_t*>(xa);
         const int ws = x_words_stride(p.D);
@@ -442,8 +551,10 @@ struct RouterPolicy {
         }
     }
     __device__ static bool unit(const Params& p, int job, int u, SegDesc* d, int* chunk) {
-        const uint32_t* xs = reinterpret_cast<const uint32_t*>(engine_xarea(p.ns));
+        const uint32_t* xs = reinterpret_cast<const uint32_t*>(engine_xarea());
         d->WA = d->WB = p.W;
+        d->mapA = d->mapB = &p.map;
+        d->eA = d->eB = 0;
         d->SA = d->SB = p.S;
         d->BA = d->BB = p.B;
         d->rowA = job * 16;
@@ -454,6 +565,8 @@ struct RouterPolicy {
         d->bits = 8;
         d->xs = xs;
         d->xsum = reinterpret_cast<const float*>(xs + 2 * x_words_stride(p.D));
+        d->xcorr = nullptr;
+        d->xfold = 0;
         d->xws = x_words_stride(p.D);
         d->ntok = 2;
         d->mult = 1.0f;
@@ -464,9 +577,12 @@ struct RouterPolicy {
         const int g = lane >> 2, t = lane & 3;
         if (t == 0) {
             const int e0 = job * 16 + g, e1 = e0 + 8;
-            if (e0 < p.E) p.logits[e0] = f[0] + f[1];
-            if (e1 < p.E) p.logits[e1] = f[2] + f[3];
+            for (int r = 0; r < max(1, p.replicas); ++r) {
+                if (e0 < p.E) p.logits[r * 256 + e0] = f[0] + f[1];
+                if (e1 < p.E) p.logits[r * 256 + e1] = f[2] + f[3];
+            }
         }
+        if (p.fused) return;
         __threadfence();
         __syncwarp();
         unsigned int tk = 0;
