@@ -53,6 +53,25 @@ class AffineMatrix(C.Structure):
                 ("rows", C.c_uint32), ("cols", C.c_uint32), ("bits", C.c_uint32)]
 
 
+class TokenExpertPair(C.Structure):
+    """tf_token_expert_pair == PrefillTokenExpertPair (PrefillRouter.swift:4-28)."""
+
+    _fields_ = [("token", C.c_uint32), ("expert", C.c_uint32), ("rank", C.c_uint32), ("weight_bits", C.c_uint32)]
+
+
+class MoEGroup(C.Structure):
+    _fields_ = [("expert", C.c_uint32), ("pair_start", C.c_uint32), ("pair_count", C.c_uint32)]
+
+
+class MoETile(C.Structure):
+    _fields_ = [("group_start", C.c_uint32), ("group_count", C.c_uint32), ("pair_start", C.c_uint32),
+                ("pair_count", C.c_uint32)]
+
+
+class GroupingError(C.Structure):
+    _fields_ = [("code", C.c_int), ("a", C.c_uint32), ("b", C.c_uint32)]
+
+
 class MoELayer(C.Structure):
     """tf_moe_layer."""
 
@@ -92,6 +111,10 @@ _PROTOS = {
                           _P, _P, _I, _P], _I),
     "tf_moe_decode_layer": ([_P, C.POINTER(MoELayer), _P, _P, _P, _P, _P, _P, _P], _I),
     "tf_router_topk_noalloc": ([_P, _P, _P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _I, _P], _I),
+    "tf_group_token_expert_pairs": ([_P, _U32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, _U32, _P, _P, _P,
+                                     _P, _P, _P, _P, C.POINTER(GroupingError)], _I),
+    "tf_router_topk_batched": ([_P, _P, _P, _P, _P, _U32, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _I, _P], _I),
+    "tf_moe_route_sort": ([_P, _P, _P, _U32, _U32, _U32, _U32, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
 }
 
 # Symbols of include/tfcuda.h added by later milestones register here too.

@@ -198,6 +198,68 @@ TF_API tf_status tf_moe_decode_layer(tf_context* ctx, const tf_moe_layer* layer,
                               const void* x, const void* residual, void* y, void* out_indices,
                               void* out_weights, void* stream);
 
+/* PrefillRouter.encodeGemma4Block (Sources/TurboFieldfare/Kernels/Prefill/MoE/PrefillRouter.swift:37-89;
+ * prefill_router_gemma4_block, Metal/Prefill/prefill.metal:478-573): the router for
+ * T tokens at once, hidden[t * hidden_stride + k] (fp16).  Per token: int8
+ * logits as tf_router_topk, top_k (1..64) by logit with ties to the lower id,
+ * softmax over the k, times per_expert_scale.  out_indices uint32[T][top_k],
+ * out_weights fp16[T][top_k] (device).  num_experts <= 256; W 16-byte aligned. */
+TF_API tf_status tf_router_topk_batched(tf_context* ctx, const void* W, const void* scales, const void* biases,
+                                        const void* hidden, uint32_t hidden_stride, const void* eff_scale,
+                                        const void* per_expert_scale, void* out_indices, void* out_weights,
+                                        uint32_t T, uint32_t num_experts, uint32_t d, uint32_t top_k,
+                                        tf_scale_type st, void* stream);
+
+/* ---- token -> expert grouping ------------------------------------------------ */
+/* PrefillTokenExpertPair (Sources/TurboFieldfare/Kernels/Prefill/MoE/PrefillRouter.swift:4-28):
+ * weight_bits holds the fp16 routing weight in its low 16 bits. */
+typedef struct { uint32_t token, expert, rank, weight_bits; } tf_token_expert_pair;
+/* PrefillMoEGroup / PrefillMoETile (PrefillMoEGrouping.swift:3-29). */
+typedef struct { uint32_t expert, pair_start, pair_count; } tf_moe_group;
+typedef struct { uint32_t group_start, group_count, pair_start, pair_count; } tf_moe_tile;
+
+/* PrefillMoEGroupingError cases (PrefillMoEGrouping.swift:52-88). */
+typedef enum {
+    TF_GROUPING_OK = 0,
+    TF_GROUPING_INVALID_QUERY_COUNT = 1,
+    TF_GROUPING_INVALID_TOP_K = 2,
+    TF_GROUPING_INVALID_NUM_EXPERTS = 3,
+    TF_GROUPING_INVALID_TILE_EXPERT_COUNT = 4,
+    TF_GROUPING_PAIR_COUNT_MISMATCH = 5,
+    TF_GROUPING_TOKEN_OUT_OF_RANGE = 6,
+    TF_GROUPING_RANK_OUT_OF_RANGE = 7,
+    TF_GROUPING_EXPERT_OUT_OF_RANGE = 8,
+    TF_GROUPING_DUPLICATE_TOKEN_RANK = 9,
+    TF_GROUPING_SORT_KEY_COUNT_MISMATCH = 10
+} tf_grouping_code;
+typedef struct { tf_grouping_code code; uint32_t a, b; } tf_grouping_error;
+
+/* PrefillMoEGrouping.groupTokenExpertPairs (PrefillMoEGrouping.swift:91-192), HOST
+ * memory, caller's thread: validates (first offending pair wins, in the
+ * reference's check order), sorts by (sort key?, expert, token, rank) and builds
+ * per-expert offsets (UINT32_MAX when empty) / counts (num_experts each), groups
+ * and tiles (<= num_experts each).  TF_ERR_GROUPING with `error` filled on
+ * rejected metadata. */
+TF_API tf_status tf_group_token_expert_pairs(const tf_token_expert_pair* pairs, uint32_t n_pairs,
+                                             int32_t query_count, int32_t top_k, int32_t num_experts,
+                                             int32_t tile_expert_count, const uint64_t* sort_keys,
+                                             uint32_t n_sort_keys, tf_token_expert_pair* sorted,
+                                             uint32_t* offsets, uint32_t* counts, tf_moe_group* groups,
+                                             uint32_t* n_groups, tf_moe_tile* tiles, uint32_t* n_tiles,
+                                             tf_grouping_error* error);
+
+/* The same grouping on the device for the GPU pipeline: the input is the
+ * router's token-major routing (expert_ids uint32[T*K], weights fp16[T*K]),
+ * the replacement for PrefillRouter.makeTokenExpertPairs + groupTokenExpertPairs
+ * without the host round trip (RealForwardRunner.swift:1750-1822).  All
+ * arrays are device memory; n_groups / n_tiles are device uint32 scalars.
+ * sort_keys: device uint64[num_experts] or NULL.  num_experts <= 256.
+ * Out-of-range expert ids are skipped and raise the context's device error bit. */
+TF_API tf_status tf_moe_route_sort(tf_context* ctx, const void* expert_ids, const void* weights, uint32_t T,
+                                   uint32_t top_k, uint32_t num_experts, uint32_t tile_expert_count,
+                                   const void* sort_keys, void* sorted_pairs, void* offsets, void* counts,
+                                   void* groups, void* n_groups, void* tiles, void* n_tiles, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
