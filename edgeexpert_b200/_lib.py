@@ -115,6 +115,12 @@ _PROTOS = {
                                      _P, _P, _P, _P, C.POINTER(GroupingError)], _I),
     "tf_router_topk_batched": ([_P, _P, _P, _P, _P, _U32, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _I, _P], _I),
     "tf_moe_route_sort": ([_P, _P, _P, _U32, _U32, _U32, _U32, _P, _P, _P, _P, _P, _P, _P, _P, _P], _I),
+    "tf_int4_qmm": ([_P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _I, _P], _I),
+    "tf_prefill_shared_expert": ([_P, _P, _U32, C.POINTER(AffineMatrix), C.POINTER(AffineMatrix),
+                                  C.POINTER(AffineMatrix), _P, _P, _U32, _U32, _I, _P], _I),
+    "tf_moe_grouped_routed": ([_P, _P, _U64, _U32, C.POINTER(ExpertOffsets), _P, _P, _P, _P, _U32, _P, _P, _U32,
+                               _U32, _U32, _U32, _I, _P], _I),
+    "tf_moe_reduce_token_major": ([_P, _P, _P, _P, _U32, _U32, _U32, _P], _I),
 }
 
 # Symbols of include/tfcuda.h added by later milestones register here too.

@@ -1,0 +1,781 @@
+// tf_qmm.cu -- prefill GEMMs with int4 affine (MLX group-64) weights on the
+// 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// Reference kernels replaced:
+//   prefill_dequant_int4_qmm_f16_block  (Metal/Prefill/prefill.metal:672-709,
+//       PrefillInt4QMM.encode, Kernels/Prefill/Primitives/PrefillPrimitives.swift:73-122)
+//   mpp_prefill_affine_threadgroup_f16  (Metal/TensorCore/tensorops.metal:8-105,
+//       MPPPrefillInt4QMM.encode) -- the same "dequantise a weight tile to fp16
+//       in on-chip memory, then run the matrix unit" scheme, here at 128 x 256.
+//   prefill_grouped_routed_moe_batched_phase1 / _down (prefill.metal:336-440,
+//       598-670; PrefillGroupedRoutedMoE.encodeStreamedBatched,
+//       Kernels/Prefill/MoE/PrefillGroupedRoutedMoE.swift:446-527)
+//   prefill_moe_reduce_token_major (prefill.metal:575-596; PrefillMoE.swift:11-40)
+//
+// One persistent kernel, one CTA per SM, warp-specialised:
+//   warps 0-3   epilogue: tcgen05.ld of the fp32 accumulator (TMEM lane = weight
+//               row), fused GELU(gate)*up, fp16 stores
+//   warps 4-7   activation loader: 256 token rows x 128 B per k-block by
+//               cp.async into the 128-byte-swizzled K-major operand layout
+//               (rows gathered through the sorted token->expert pairs)
+//   warps 8-15  weight loader: int4 nibbles + bf16/fp16 scale/bias ->
+//               fp16 w = fma(q, s, b) (one rounding), same swizzled layout
+//   warp 16     TMEM allocation and the single-thread tcgen05.mma issue
+// Tile: 128 weight rows (M) x up to 256 tokens (N), k-block 64 (= one
+// quantisation group), 4 shared-memory stages of 48 KB, two TMEM accumulators
+// of 256 fp32 columns so the epilogue of one tile overlaps the next tile's
+// main loop.  Gate/up projections interleave their rows (even = gate, odd = up)
+// so a lane pair holds both operands of GELU(g)*u after one shuffle.
+#include "tf_context.cuh"
+#include "tf_umma.cuh"
+
+using namespace tf;
+
+namespace {
+
+constexpr int kEpiWarps = 4;
+constexpr int kBWarps = 4;
+constexpr int kAWarps = 8;
+constexpr int kMmaWarp = kEpiWarps + kBWarps + kAWarps;  // 16
+constexpr int kQWarps = kMmaWarp + 1;
+constexpr int kQThreads = kQWarps * 32;
+constexpr int kStages = 4;
+constexpr int kTM = 128;               // weight rows per tile (MMA M)
+constexpr int kTN = 256;               // tokens per tile (MMA N, max)
+constexpr int kAStage = kTM * 128;     // 16 KB
+constexpr int kBStage = kTN * 128;     // 32 KB
+constexpr int kBLag = 2;               // cp.async groups in flight per loader thread
+constexpr int kAccCols = 256;
+constexpr int kTmemCols = 512;
+constexpr int kMaxGroups = 256;
+constexpr uint32_t kQSpin = 1u << 24;
+
+enum QMode : int { kDensePlain = 0, kDenseGateUp = 1, kGroupedGateUp = 2, kGroupedDown = 3 };
+
+struct QmmParams {
+    int mode;
+    int K;      // reduction length (multiple of 64)
+    int nfeat;  // rows of one weight matrix (output features)
+    int T;      // dense: tokens
+    // dense weights: matrix 0 (plain / gate), matrix 1 (up)
+    const uint8_t* w0;
+    const void* s0;
+    const void* b0;
+    const uint8_t* w1;
+    const void* s1;
+    const void* b1;
+    // grouped: expert e's matrix at pool + e*stride + offset
+    const uint8_t* pool;
+    uint64_t stride;
+    uint32_t ow0, os0, ob0, ow1, os1, ob1;
+    uint32_t num_experts;
+    const tf_moe_group* groups;
+    const uint32_t* n_groups;
+    const tf_token_expert_pair* pairs;
+    int top_k;
+    // activations
+    const __half* x;
+    long long ldx;
+    __half* y;
+    long long ldy;
+    int round_gu;  // gate/up rounded to fp16 before GELU (shared expert)
+    uint32_t* err;
+};
+
+struct QShared {
+    uint64_t full[kStages];
+    uint64_t empty[kStages];
+    uint64_t tfull[2];
+    uint64_t tempty[2];
+    uint64_t done;
+    uint32_t tmem_base;
+    int abort_flag;
+    int ng;
+    int total;
+    int prefix[kMaxGroups + 1];
+    int gstart[kMaxGroups];
+    int gcount[kMaxGroups];
+    int gexpert[kMaxGroups];
+};
+
+constexpr size_t kQSmemBytes = 1024 + (size_t)kStages * (kAStage + kBStage) + sizeof(QShared);
+
+struct QTile {
+    int feat0;
+    int row0;  // dense: first token row; grouped: first sorted pair
+    int cnt;   // tokens / pairs in the tile
+    int expert;
+};
+
+__device__ __forceinline__ int feat_per_tile(int mode) {
+    return (mode == kDenseGateUp || mode == kGroupedGateUp) ? kTM / 2 : kTM;
+}
+
+__device__ __forceinline__ bool decode_tile(const QmmParams& p, const QShared& sh, int idx, QTile& t) {
+    if (idx >= sh.total) return false;
+    const int fpt = feat_per_tile(p.mode);
+    const int nft = (p.nfeat + fpt - 1) / fpt;
+    if (p.mode == kDensePlain || p.mode == kDenseGateUp) {
+        const int tt = idx / nft, ft = idx % nft;
+        t.feat0 = ft * fpt;
+        t.row0 = tt * kTN;
+        t.cnt = min(kTN, p.T - t.row0);
+        t.expert = 0;
+        return true;
+    }
+    // largest g with prefix[g] <= idx
+    int lo = 0, hi = sh.ng - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (sh.prefix[mid] <= idx) lo = mid; else hi = mid - 1;
+    }
+    const int g = lo, local = idx - sh.prefix[g], c = sh.gcount[g];
+    const int ntt = (c + kTN - 1) / kTN;
+    const int q = (c + ntt - 1) / ntt;
+    const int tt = local / nft, ft = local % nft;
+    t.feat0 = ft * fpt;
+    t.row0 = sh.gstart[g] + tt * q;
+    t.cnt = min(q, c - tt * q);
+    t.expert = sh.gexpert[g];
+    return true;
+}
+
+// Bounded wait that gives up early once another role has given up.
+__device__ __forceinline__ bool qwait(uint64_t* bar, uint32_t parity, QShared& sh, uint32_t* err) {
+    for (uint32_t i = 0; i < kQSpin; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 255u && *reinterpret_cast<volatile int*>(&sh.abort_flag)) return false;
+    }
+    sh.abort_flag = 1;
+    if (err) atomicOr(err, kErrMbarTimeout);
+    return false;
+}
+
+__device__ __forceinline__ uint32_t sw128(int row, int chunk) {
+    return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+__device__ __forceinline__ uint4 ldg_nc16(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// fp16 bits of a bf16 / fp16 scale or bias
+template <typename ST>
+__device__ __forceinline__ uint32_t scale_bits_f16(const ST* p);
+template <>
+__device__ __forceinline__ uint32_t scale_bits_f16<__half>(const __half* p) {
+    return (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(p));
+}
+template <>
+__device__ __forceinline__ uint32_t scale_bits_f16<__nv_bfloat16>(const __nv_bfloat16* p) {
+    const unsigned short b = __ldg(reinterpret_cast<const unsigned short*>(p));
+    return (uint32_t)__half_as_ushort(__float2half_rn(__uint_as_float((uint32_t)b << 16)));
+}
+
+// 8 nibbles (elements 8c..8c+7, low nibble first) -> 4 half2 in k order,
+// w_k = fma(q_k, s, b) rounded once to fp16.
+__device__ __forceinline__ void dq8_natural(uint32_t w, uint32_t s2, uint32_t b2, uint32_t o[4]) {
+    constexpr uint32_t k1024 = 0x64006400u;
+    const uint32_t t = w & 0x0F0F0F0Fu;          // e0 e2 e4 e6
+    const uint32_t u = (w >> 4) & 0x0F0F0F0Fu;   // e1 e3 e5 e7
+    const uint32_t lo = __byte_perm(t, u, 0x5140);  // e0 e1 e2 e3
+    const uint32_t hi = __byte_perm(t, u, 0x7362);  // e4 e5 e6 e7
+    const uint32_t m = 0x64646464u;
+    o[0] = hfma2_u(hsub2_u(__byte_perm(lo, m, 0x4140), k1024), s2, b2);
+    o[1] = hfma2_u(hsub2_u(__byte_perm(lo, m, 0x4342), k1024), s2, b2);
+    o[2] = hfma2_u(hsub2_u(__byte_perm(hi, m, 0x4140), k1024), s2, b2);
+    o[3] = hfma2_u(hsub2_u(__byte_perm(hi, m, 0x4342), k1024), s2, b2);
+}
+
+// Iteration cursor over (tile, k-block) of this CTA.
+struct QCursor {
+    int idx, kb;
+    bool valid;
+    QTile t;
+};
+
+__device__ __forceinline__ void cursor_start(const QmmParams& p, const QShared& sh, QCursor& c) {
+    c.idx = blockIdx.x;
+    c.kb = 0;
+    c.valid = decode_tile(p, sh, c.idx, c.t);
+}
+
+__device__ __forceinline__ void cursor_next(const QmmParams& p, const QShared& sh, QCursor& c, int nkb) {
+    if (!c.valid) return;
+    if (++c.kb == nkb) {
+        c.kb = 0;
+        c.idx += gridDim.x;
+        c.valid = decode_tile(p, sh, c.idx, c.t);
+    }
+}
+
+struct ALoad {
+    uint4 q;
+    uint32_t s, b;
+    bool ok;
+};
+
+template <typename ST>
+__device__ __forceinline__ ALoad a_load(const QmmParams& p, const QCursor& c, int r, int h) {
+    ALoad a;
+    a.ok = false;
+    if (!c.valid) return a;
+    const bool gu = (p.mode == kDenseGateUp || p.mode == kGroupedGateUp);
+    const int mat = gu ? (r & 1) : 0;
+    const int f = c.t.feat0 + (gu ? (r >> 1) : r);
+    if (f >= p.nfeat) return a;
+    const uint8_t* W;
+    const ST* S;
+    const ST* B;
+    if (p.mode == kDensePlain || p.mode == kDenseGateUp) {
+        W = mat ? p.w1 : p.w0;
+        S = static_cast<const ST*>(mat ? p.s1 : p.s0);
+        B = static_cast<const ST*>(mat ? p.b1 : p.b0);
+    } else {
+        const uint8_t* base = p.pool + (uint64_t)c.t.expert * p.stride;
+        W = base + (mat ? p.ow1 : p.ow0);
+        S = reinterpret_cast<const ST*>(base + (mat ? p.os1 : p.os0));
+        B = reinterpret_cast<const ST*>(base + (mat ? p.ob1 : p.ob0));
+    }
+    const int G = p.K >> 6;
+    a.q = ldg_nc16(W + (size_t)f * (p.K >> 1) + c.kb * 32 + h * 16);
+    a.s = scale_bits_f16<ST>(S + (size_t)f * G + c.kb);
+    a.b = scale_bits_f16<ST>(B + (size_t)f * G + c.kb);
+    a.ok = true;
+    return a;
+}
+
+template <typename ST>
+__global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant__ QmmParams p) {
+    extern __shared__ uint8_t q_smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(q_smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* As = smem;
+    uint8_t* Bs = smem + kStages * kAStage;
+    QShared& sh = *reinterpret_cast<QShared*>(Bs + kStages * kBStage);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nkb = p.K >> 6;
+    const int fpt = feat_per_tile(p.mode);
+    const int nft = (p.nfeat + fpt - 1) / fpt;
+
+    // ---- setup: barriers, tile table, TMEM ----
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&sh.full[s], kAWarps + kBWarps);
+            mbar_init(&sh.empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&sh.tfull[a], 1);
+            mbar_init(&sh.tempty[a], kEpiWarps);
+        }
+        mbar_init(&sh.done, 1);
+        sh.abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (p.mode == kDensePlain || p.mode == kDenseGateUp) {
+        if (tid == 0) {
+            sh.ng = 0;
+            sh.total = ((p.T + kTN - 1) / kTN) * nft;
+        }
+    } else if (warp == 0) {
+        const int ng = min((int)*p.n_groups, kMaxGroups);
+        // each lane owns 8 consecutive groups
+        int cnt[8];
+        int run = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int g = lane * 8 + j;
+            int tiles = 0;
+            if (g < ng) {
+                const tf_moe_group gr = p.groups[g];
+                sh.gstart[g] = (int)gr.pair_start;
+                sh.gcount[g] = (int)gr.pair_count;
+                sh.gexpert[g] = (int)gr.expert;
+                if (gr.expert < p.num_experts) {
+                    tiles = (((int)gr.pair_count + kTN - 1) / kTN) * nft;
+                } else if (p.err) {
+                    atomicOr(p.err, kErrBadExpert);
+                }
+            }
+            cnt[j] = tiles;
+            run += tiles;
+        }
+        int incl = run;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        int acc = incl - run;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int g = lane * 8 + j;
+            if (g <= ng) sh.prefix[g] = acc;
+            acc += cnt[j];
+        }
+        if (lane == 31) sh.total = incl;
+        if (lane == 0) sh.ng = ng;
+        if (ng == kMaxGroups && lane == 31) sh.prefix[kMaxGroups] = incl;
+    }
+    if (warp == kMmaWarp) {
+        tmem_alloc(&sh.tmem_base, kTmemCols);
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = sh.tmem_base;
+
+    if (warp >= kEpiWarps + kBWarps && warp < kMmaWarp) {
+        // ================= weight loader / dequantiser =================
+        const int at = tid - (kEpiWarps + kBWarps) * 32;  // 0..255
+        const int r = at >> 1, h = at & 1;
+        QCursor lc, pc;
+        cursor_start(p, sh, lc);
+        pc = lc;
+        ALoad ring[kStages];
+#pragma unroll
+        for (int j = 0; j < kStages; ++j) {
+            ring[j] = a_load<ST>(p, lc, r, h);
+            cursor_next(p, sh, lc, nkb);
+        }
+        uint32_t phase = 0;
+        bool live = true;
+        while (pc.valid && live) {
+#pragma unroll
+            for (int j = 0; j < kStages; ++j) {
+                if (!pc.valid || !live) break;
+                const ALoad cur = ring[j];
+                ring[j] = a_load<ST>(p, lc, r, h);
+                cursor_next(p, sh, lc, nkb);
+                if (!qwait(&sh.empty[j], phase ^ 1u, sh, p.err)) {
+                    live = false;
+                    break;
+                }
+                const uint32_t dst = smem_u32(As + j * kAStage);
+                if (cur.ok) {
+                    const uint32_t s2 = cur.s | (cur.s << 16), b2 = cur.b | (cur.b << 16);
+                    const uint32_t wv[4] = {cur.q.x, cur.q.y, cur.q.z, cur.q.w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        uint32_t o[4];
+                        dq8_natural(wv[i], s2, b2, o);
+                        sts128(dst + sw128(r, h * 4 + i), o[0], o[1], o[2], o[3]);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) sts128(dst + sw128(r, h * 4 + i), 0u, 0u, 0u, 0u);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sh.full[j]);
+                cursor_next(p, sh, pc, nkb);
+            }
+            phase ^= 1u;
+        }
+    } else if (warp >= kEpiWarps && warp < kEpiWarps + kBWarps) {
+        // ================= activation loader (cp.async) =================
+        const int bt = tid - kEpiWarps * 32;  // 0..127
+        const int c = bt & 7, r0 = bt >> 3;   // rows r0 + 16 j
+        QCursor cur;
+        cursor_start(p, sh, cur);
+        long long roff[16];
+        int it = 0;
+        int last_idx = -1;
+        bool live = true;
+        while (cur.valid && live) {
+            if (cur.idx != last_idx) {
+                last_idx = cur.idx;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int row = r0 + 16 * j;
+                    long long off = -1;
+                    if (row < cur.t.cnt) {
+                        const int rr = cur.t.row0 + row;
+                        if (p.mode == kGroupedGateUp)
+                            off = (long long)p.pairs[rr].token * p.ldx;
+                        else
+                            off = (long long)rr * p.ldx;
+                    }
+                    roff[j] = off;
+                }
+            }
+            const int s = it % kStages;
+            const uint32_t ph = (uint32_t)(it / kStages) & 1u;
+            if (!qwait(&sh.empty[s], ph ^ 1u, sh, p.err)) {
+                live = false;
+                break;
+            }
+            const uint32_t dst = smem_u32(Bs + s * kBStage);
+            const __half* xk = p.x + cur.kb * 64 + c * 8;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (roff[j] >= 0) cp_async16(dst + sw128(r0 + 16 * j, c), xk + roff[j]);
+            cp_async_commit();
+            if (it >= kBLag) {
+                cp_async_wait<kBLag>();
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sh.full[(it - kBLag) % kStages]);
+            }
+            ++it;
+            cursor_next(p, sh, cur, nkb);
+        }
+        cp_async_wait<0>();
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (live && lane == 0)
+            for (int k = max(0, it - kBLag); k < it; ++k) mbar_arrive(&sh.full[k % kStages]);
+    } else if (warp == kMmaWarp) {
+        // ================= MMA issue (one thread) =================
+        int it = 0, lt = 0;
+        bool live = true;
+        for (int idx = blockIdx.x; live; idx += gridDim.x, ++lt) {
+            QTile t;
+            if (!decode_tile(p, sh, idx, t)) break;
+            const int acc = lt & 1;
+            if (!qwait(&sh.tempty[acc], (((uint32_t)lt >> 1) & 1u) ^ 1u, sh, p.err)) {
+                live = false;
+                break;
+            }
+            tc_fence_after();
+            const int N = max(16, (t.cnt + 15) & ~15);
+            const uint32_t idesc = make_idesc_f16(kTM, N);
+            const uint32_t d = tmem + (uint32_t)(acc * kAccCols);
+            for (int kb = 0; kb < nkb; ++kb, ++it) {
+                const int s = it % kStages;
+                if (!qwait(&sh.full[s], (uint32_t)(it / kStages) & 1u, sh, p.err)) {
+                    live = false;
+                    break;
+                }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint64_t ad = make_sw128_desc(As + s * kAStage);
+                    const uint64_t bd = make_sw128_desc(Bs + s * kBStage);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        umma_f16(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb | k) ? 1u : 0u);
+                    umma_commit(&sh.empty[s]);
+                }
+                __syncwarp();
+            }
+            if (!live) break;
+            if (lane == 0) umma_commit(&sh.tfull[acc]);
+            __syncwarp();
+        }
+        // all issued MMAs retire before TMEM is released
+        if (lane == 0) umma_commit(&sh.done);
+        __syncwarp();
+        uint32_t i = 0;
+        for (; i < kQSpin; ++i)
+            if (mbar_try_wait(&sh.done, 0)) break;
+        if (i == kQSpin && p.err) atomicOr(p.err, kErrMbarTimeout);
+    } else {
+        // ================= epilogue (warps 0-3) =================
+        const int ew = warp;  // TMEM lanes 32*ew .. 32*ew+31
+        const int row = ew * 32 + lane;
+        const bool gu = (p.mode == kDenseGateUp || p.mode == kGroupedGateUp);
+        int lt = 0;
+        for (int idx = blockIdx.x;; idx += gridDim.x, ++lt) {
+            QTile t;
+            if (!decode_tile(p, sh, idx, t)) break;
+            const int acc = lt & 1;
+            if (!qwait(&sh.tfull[acc], ((uint32_t)lt >> 1) & 1u, sh, p.err)) break;
+            tc_fence_after();
+            const uint32_t tbase = tmem + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * kAccCols);
+            const int f = t.feat0 + (gu ? (row >> 1) : row);
+            const bool fok = f < p.nfeat;
+            for (int cc = 0; cc * 32 < t.cnt; ++cc) {
+                float v[32];
+                tmem_ld32(tbase + (uint32_t)(cc * 32), v);
+                const int colbase = cc * 32;
+                if (gu) {
+                    const bool even = (lane & 1) == 0;
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) {
+                        const float send = even ? v[16 + jj] : v[jj];
+                        const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+                        float g = even ? v[jj] : recv;
+                        float u = even ? recv : v[16 + jj];
+                        const int col = colbase + (even ? jj : 16 + jj);
+                        if (p.round_gu) {
+                            g = __half2float(__float2half_rn(g));
+                            u = __half2float(__float2half_rn(u));
+                        }
+                        if (fok && col < t.cnt)
+                            p.y[(long long)(t.row0 + col) * p.ldy + f] = __float2half_rn(gelu_tanh(g) * u);
+                    }
+                } else if (p.mode == kGroupedDown) {
+                    long long orow = 0;
+                    if (colbase + lane < t.cnt) {
+                        const tf_token_expert_pair pr = p.pairs[t.row0 + colbase + lane];
+                        orow = (long long)pr.token * p.top_k + pr.rank;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const long long o = __shfl_sync(0xffffffffu, orow, j);
+                        if (fok && colbase + j < t.cnt) p.y[o * p.ldy + f] = __float2half_rn(v[j]);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (fok && colbase + j < t.cnt)
+                            p.y[(long long)(t.row0 + colbase + j) * p.ldy + f] = __float2half_rn(v[j]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.tempty[acc]);
+        }
+    }
+
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// h2[t][d] = half(sum_r fma(w[t][r], partial[t*K + r][d])) in rank order
+// (prefill.metal:575-596).  8 outputs per thread, 16-byte loads.
+__global__ void reduce_token_major_kernel(const __half* __restrict__ partials, const __half* __restrict__ w,
+                                          __half* __restrict__ h2, int T, int K, int D) {
+    const int d8 = D >> 3;
+    const long long n = (long long)T * d8;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int t = (int)(i / d8), dv = (int)(i % d8);
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+        for (int r = 0; r < K; ++r) {
+            const float wr = __half2float(w[(long long)t * K + r]);
+            const uint4 q = __ldcs(reinterpret_cast<const uint4*>(partials + ((long long)t * K + r) * D) + dv);
+            const __half2* hp = reinterpret_cast<const __half2*>(&q);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 f2 = __half22float2(hp[j]);
+                acc[2 * j] = fmaf(wr, f2.x, acc[2 * j]);
+                acc[2 * j + 1] = fmaf(wr, f2.y, acc[2 * j + 1]);
+            }
+        }
+        uint4 o;
+        __half2* op = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) op[j] = __floats2half2_rn(acc[2 * j], acc[2 * j + 1]);
+        reinterpret_cast<uint4*>(h2 + (long long)t * D)[dv] = o;
+    }
+}
+
+tf_status launch_qmm(tf_context* ctx, const QmmParams& p, tf_scale_type st, int grid, cudaStream_t stream,
+                     const char* name) {
+    const void* fn = st == TF_SCALE_BF16 ? reinterpret_cast<const void*>(&qmm_kernel<__nv_bfloat16>)
+                                         : reinterpret_cast<const void*>(&qmm_kernel<__half>);
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kQSmemBytes);
+    if (e != cudaSuccess) return cuda_check(ctx, e, name);
+    if (grid <= 0) return TF_OK;
+    if (st == TF_SCALE_BF16)
+        qmm_kernel<__nv_bfloat16><<<grid, kQThreads, kQSmemBytes, stream>>>(p);
+    else
+        qmm_kernel<__half><<<grid, kQThreads, kQSmemBytes, stream>>>(p);
+    return cuda_check(ctx, cudaGetLastError(), name);
+}
+
+bool scale_type_ok(tf_scale_type st) { return st == TF_SCALE_BF16 || st == TF_SCALE_F16; }
+
+}  // namespace
+
+extern "C" {
+
+tf_status tf_int4_qmm(tf_context* ctx, const void* weights, const void* scales, const void* biases, const void* x,
+                      void* y, uint32_t t, uint32_t n, uint32_t k, uint32_t x_stride, uint32_t y_stride,
+                      tf_scale_type st, void* stream) {
+    if (!ctx) return TF_ERR_INVALID_ARG;
+    const char* name = "tf_int4_qmm";
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, TF_ERR_CUDA, "cudaSetDevice failed");
+    if (!scale_type_ok(st)) return fail(ctx, TF_ERR_INVALID_ARG, "%s: bad scale type", name);
+    if (k == 0 || k % 64 || n == 0) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: k %% 64 == 0, n > 0", name);
+    if (x_stride == 0) x_stride = k;
+    if (y_stride == 0) y_stride = n;
+    if (x_stride < k || y_stride < n || x_stride % 8)
+        return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: x_stride >= k (multiple of 8), y_stride >= n", name);
+    if (t == 0) return TF_OK;
+    if (!weights || !scales || !biases || !x || !y) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
+    if (!aligned16(weights) || !aligned16(x) || !aligned2(y) || !aligned2(scales) || !aligned2(biases))
+        return fail(ctx, TF_ERR_MISALIGNED, "%s: weights/x 16-byte, y/scales/biases 2-byte aligned", name);
+    QmmParams p{};
+    p.mode = kDensePlain;
+    p.K = (int)k;
+    p.nfeat = (int)n;
+    p.T = (int)t;
+    p.w0 = static_cast<const uint8_t*>(weights);
+    p.s0 = scales;
+    p.b0 = biases;
+    p.x = static_cast<const __half*>(x);
+    p.ldx = x_stride;
+    p.y = static_cast<__half*>(y);
+    p.ldy = y_stride;
+    p.err = ctx->d_err;
+    const long long tiles = (long long)((t + kTN - 1) / kTN) * ((n + kTM - 1) / kTM);
+    return launch_qmm(ctx, p, st, (int)std::min<long long>(tiles, ctx->num_sms), static_cast<cudaStream_t>(stream),
+                      name);
+}
+
+tf_status tf_prefill_shared_expert(tf_context* ctx, const void* x, uint32_t x_stride, const tf_affine_matrix* gate,
+                                   const tf_affine_matrix* up, const tf_affine_matrix* down, void* act_scratch,
+                                   void* y, uint32_t y_stride, uint32_t t, tf_scale_type st, void* stream) {
+    if (!ctx) return TF_ERR_INVALID_ARG;
+    const char* name = "tf_prefill_shared_expert";
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, TF_ERR_CUDA, "cudaSetDevice failed");
+    if (!gate || !up || !down || !scale_type_ok(st)) return fail(ctx, TF_ERR_INVALID_ARG, "%s: bad argument", name);
+    if (gate->bits != 4 || up->bits != 4 || down->bits != 4)
+        return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: int4 projections only", name);
+    const uint32_t d = gate->cols, f = gate->rows;
+    if (up->rows != f || up->cols != d || down->rows != d || down->cols != f)
+        return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: projection shapes disagree", name);
+    if (d % 64 || f % 64 || d == 0 || f == 0) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: d, f multiples of 64", name);
+    if (x_stride == 0) x_stride = d;
+    if (y_stride == 0) y_stride = d;
+    if (x_stride < d || x_stride % 8 || y_stride < d)
+        return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: strides", name);
+    if (t == 0) return TF_OK;
+    if (!x || !y || !act_scratch) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
+    const tf_affine_matrix* ms[3] = {gate, up, down};
+    for (const tf_affine_matrix* m : ms)
+        if (!m->weights || !m->scales || !m->biases || !aligned16(m->weights) || !aligned2(m->scales) ||
+            !aligned2(m->biases))
+            return fail(ctx, TF_ERR_MISALIGNED, "%s: projection pointers", name);
+    if (!aligned16(x) || !aligned16(act_scratch) || !aligned2(y))
+        return fail(ctx, TF_ERR_MISALIGNED, "%s: x/act_scratch 16-byte aligned", name);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    QmmParams p{};
+    p.mode = kDenseGateUp;
+    p.K = (int)d;
+    p.nfeat = (int)f;
+    p.T = (int)t;
+    p.w0 = static_cast<const uint8_t*>(gate->weights);
+    p.s0 = gate->scales;
+    p.b0 = gate->biases;
+    p.w1 = static_cast<const uint8_t*>(up->weights);
+    p.s1 = up->scales;
+    p.b1 = up->biases;
+    p.x = static_cast<const __half*>(x);
+    p.ldx = x_stride;
+    p.y = static_cast<__half*>(act_scratch);
+    p.ldy = f;
+    p.round_gu = 1;
+    p.err = ctx->d_err;
+    long long tiles = (long long)((t + kTN - 1) / kTN) * ((f + kTM / 2 - 1) / (kTM / 2));
+    tf_status rc = launch_qmm(ctx, p, st, (int)std::min<long long>(tiles, ctx->num_sms), s, name);
+    if (rc != TF_OK) return rc;
+    QmmParams q{};
+    q.mode = kDensePlain;
+    q.K = (int)f;
+    q.nfeat = (int)d;
+    q.T = (int)t;
+    q.w0 = static_cast<const uint8_t*>(down->weights);
+    q.s0 = down->scales;
+    q.b0 = down->biases;
+    q.x = static_cast<const __half*>(act_scratch);
+    q.ldx = f;
+    q.y = static_cast<__half*>(y);
+    q.ldy = y_stride;
+    q.err = ctx->d_err;
+    tiles = (long long)((t + kTN - 1) / kTN) * ((d + kTM - 1) / kTM);
+    return launch_qmm(ctx, q, st, (int)std::min<long long>(tiles, ctx->num_sms), s, name);
+}
+
+tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64_t expert_stride, uint32_t num_experts,
+                                const tf_expert_offsets* off, const void* sorted_pairs, const void* groups,
+                                const void* n_groups, const void* hidden, uint32_t hidden_stride, void* act_scratch,
+                                void* route_partials, uint32_t t, uint32_t d, uint32_t f, uint32_t top_k,
+                                tf_scale_type st, void* stream) {
+    if (!ctx) return TF_ERR_INVALID_ARG;
+    const char* name = "tf_moe_grouped_routed";
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, TF_ERR_CUDA, "cudaSetDevice failed");
+    if (!off || !scale_type_ok(st)) return fail(ctx, TF_ERR_INVALID_ARG, "%s: bad argument", name);
+    if (d % 64 || f % 64 || d == 0 || f == 0 || top_k == 0 || num_experts == 0 || num_experts > (uint32_t)kMaxGroups)
+        return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: d, f multiples of 64; 1 <= num_experts <= 256", name);
+    if (hidden_stride == 0) hidden_stride = d;
+    if (hidden_stride < d || hidden_stride % 8) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: hidden stride", name);
+    if (t == 0) return TF_OK;
+    if (!pool || !sorted_pairs || !groups || !n_groups || !hidden || !act_scratch || !route_partials)
+        return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
+    if (!aligned16(pool) || expert_stride % 16 || off->gate_w % 16 || off->up_w % 16 || off->down_w % 16 ||
+        off->gate_s % 2 || off->gate_b % 2 || off->up_s % 2 || off->up_b % 2 || off->down_s % 2 || off->down_b % 2)
+        return fail(ctx, TF_ERR_MISALIGNED, "%s: weight matrices 16-byte aligned", name);
+    if (!aligned16(hidden) || !aligned16(act_scratch) || !aligned2(route_partials) || !aligned4(sorted_pairs) ||
+        !aligned4(groups) || !aligned4(n_groups))
+        return fail(ctx, TF_ERR_MISALIGNED, "%s: activation pointers", name);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    QmmParams p{};
+    p.mode = kGroupedGateUp;
+    p.K = (int)d;
+    p.nfeat = (int)f;
+    p.pool = static_cast<const uint8_t*>(pool);
+    p.stride = expert_stride;
+    p.ow0 = off->gate_w;
+    p.os0 = off->gate_s;
+    p.ob0 = off->gate_b;
+    p.ow1 = off->up_w;
+    p.os1 = off->up_s;
+    p.ob1 = off->up_b;
+    p.num_experts = num_experts;
+    p.groups = static_cast<const tf_moe_group*>(groups);
+    p.n_groups = static_cast<const uint32_t*>(n_groups);
+    p.pairs = static_cast<const tf_token_expert_pair*>(sorted_pairs);
+    p.top_k = (int)top_k;
+    p.x = static_cast<const __half*>(hidden);
+    p.ldx = hidden_stride;
+    p.y = static_cast<__half*>(act_scratch);
+    p.ldy = f;
+    p.err = ctx->d_err;
+    tf_status rc = launch_qmm(ctx, p, st, ctx->num_sms, s, name);
+    if (rc != TF_OK) return rc;
+    QmmParams q = p;
+    q.mode = kGroupedDown;
+    q.K = (int)f;
+    q.nfeat = (int)d;
+    q.ow0 = off->down_w;
+    q.os0 = off->down_s;
+    q.ob0 = off->down_b;
+    q.x = static_cast<const __half*>(act_scratch);
+    q.ldx = f;
+    q.y = static_cast<__half*>(route_partials);
+    q.ldy = d;
+    return launch_qmm(ctx, q, st, ctx->num_sms, s, name);
+}
+
+tf_status tf_moe_reduce_token_major(tf_context* ctx, const void* route_partials, const void* routing_weights,
+                                    void* h2, uint32_t t, uint32_t top_k, uint32_t d, void* stream) {
+    if (!ctx) return TF_ERR_INVALID_ARG;
+    const char* name = "tf_moe_reduce_token_major";
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, TF_ERR_CUDA, "cudaSetDevice failed");
+    if (d == 0 || d % 8 || top_k == 0) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: d %% 8 == 0, top_k > 0", name);
+    if (t == 0) return TF_OK;
+    if (!route_partials || !routing_weights || !h2) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
+    if (!aligned16(route_partials) || !aligned16(h2) || !aligned2(routing_weights))
+        return fail(ctx, TF_ERR_MISALIGNED, "%s: partials/h2 16-byte aligned", name);
+    const long long n = (long long)t * (d / 8);
+    const int threads = 256;
+    const int grid = (int)std::min<long long>((n + threads - 1) / threads, (long long)ctx->num_sms * 8);
+    reduce_token_major_kernel<<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __half*>(route_partials), static_cast<const __half*>(routing_weights),
+        static_cast<__half*>(h2), (int)t, (int)top_k, (int)d);
+    return cuda_check(ctx, cudaGetLastError(), name);
+}
+
+}  // extern "C"

@@ -158,3 +158,76 @@ def route_sort(expert_ids, weights, T: int, top_k: int, num_experts: int, tile_e
                                  ptr(out.n_tiles), stream_ptr(stream))
     ctx.check(st, "tf_moe_route_sort")
     return out
+
+
+class PrefillInt4QMM:
+    """Dense int4 x fp16 GEMM on the tensor cores (PrefillInt4QMM.encode,
+    PrefillPrimitives.swift:73-122; MPPPrefillInt4QMM.encode, MPPPrefillInt4QMM.swift:34-78)."""
+
+    def __init__(self, context: Context | None = None):
+        import torch
+        self.ctx = context or Context.get(torch.cuda.current_device())
+
+    def encode(self, weights, scales, biases, x, y, t: int, n: int, k: int, bits: int = 4,
+               x_stride: int = 0, y_stride: int = 0, stream=None):
+        from .quant import scale_type_of
+        if bits != 4:
+            raise TFError(3, f"unsupported prefill QMM bits {bits}")
+        st = lib().tf_int4_qmm(self.ctx.handle, ptr(weights), ptr(scales), ptr(biases), ptr(x), ptr(y), t, n, k,
+                               x_stride, y_stride, scale_type_of(scales), stream_ptr(stream))
+        self.ctx.check(st, "PrefillInt4QMM.encode")
+
+
+class PrefillSharedExpert:
+    """Shared expert over T prefill tokens (per-token SharedExpertRuntime arithmetic)."""
+
+    def __init__(self, context: Context | None = None):
+        import torch
+        self.ctx = context or Context.get(torch.cuda.current_device())
+
+    def encode(self, x, gate, up, down, act_scratch, y, t: int, x_stride: int = 0, y_stride: int = 0, stream=None):
+        from .quant import scale_type_of
+        g, u, dn = gate.as_c(), up.as_c(), down.as_c()
+        st = lib().tf_prefill_shared_expert(self.ctx.handle, ptr(x), x_stride, C.byref(g), C.byref(u), C.byref(dn),
+                                            ptr(act_scratch), ptr(y), y_stride, t, scale_type_of(gate.scales),
+                                            stream_ptr(stream))
+        self.ctx.check(st, "PrefillSharedExpert.encode")
+
+
+class PrefillGroupedRoutedMoE:
+    """Grouped routed experts for a prefill chunk (PrefillGroupedRoutedMoE.encodeStreamedBatched,
+    PrefillGroupedRoutedMoE.swift:446-527): every group of the device routes in one pair of launches."""
+
+    def __init__(self, context: Context | None = None):
+        import torch
+        self.ctx = context or Context.get(torch.cuda.current_device())
+
+    def encode(self, experts, routes: "DeviceRoutes", hidden, act_scratch, route_partials, t: int, top_k: int,
+               hidden_stride: int = 0, stream=None):
+        from .quant import scale_type_of
+        st = lib().tf_moe_grouped_routed(
+            self.ctx.handle, ptr(experts.blob), experts.stride, experts.num_experts, C.byref(experts.offsets),
+            ptr(routes.sorted_pairs), ptr(routes.groups), ptr(routes.n_groups), ptr(hidden), hidden_stride,
+            ptr(act_scratch), ptr(route_partials), t, experts.d, experts.f, top_k,
+            0 if experts.scale_dtype == _bf16() else 1, stream_ptr(stream))
+        self.ctx.check(st, "PrefillGroupedRoutedMoE.encodeStreamedBatched")
+
+    encodeStreamedBatched = encode
+
+
+class PrefillMoE:
+    @staticmethod
+    def encode_reduce_token_major(route_partials, routing_weights, h2, t: int, top_k: int, d: int, stream=None,
+                                  context: Context | None = None):
+        """PrefillMoE.encodeReduceTokenMajor (PrefillMoE.swift:11-40)."""
+        ctx = context or Context.get(h2.device.index or 0)
+        st = lib().tf_moe_reduce_token_major(ctx.handle, ptr(route_partials), ptr(routing_weights), ptr(h2), t, top_k,
+                                             d, stream_ptr(stream))
+        ctx.check(st, "PrefillMoE.encodeReduceTokenMajor")
+
+    encodeReduceTokenMajor = encode_reduce_token_major
+
+
+def _bf16():
+    import torch
+    return torch.bfloat16

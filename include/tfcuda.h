@@ -260,6 +260,50 @@ TF_API tf_status tf_moe_route_sort(tf_context* ctx, const void* expert_ids, cons
                                    const void* sort_keys, void* sorted_pairs, void* offsets, void* counts,
                                    void* groups, void* n_groups, void* tiles, void* n_tiles, void* stream);
 
+/* ---- prefill GEMMs (tensor cores) -------------------------------------------------- */
+/* PrefillInt4QMM.encode (Sources/TurboFieldfare/Kernels/Prefill/Primitives/PrefillPrimitives.swift:73-122;
+ * prefill.metal:672-709) and MPPPrefillInt4QMM.encode (Kernels/TensorCore/MPPPrefillInt4QMM.swift:34-78):
+ * Y[t][j] = half(sum_i w[j][i] * X[t][i]) for t < T, j < n, with w the int4
+ * affine weight [n][k] dequantised to fp16 (fma(q, s, b), one rounding) and
+ * an fp32 accumulator.  x_stride / y_stride in elements (0 = dense).
+ * k % 64 == 0; weights and x 16-byte aligned; x_stride % 8 == 0. */
+TF_API tf_status tf_int4_qmm(tf_context* ctx, const void* weights, const void* scales, const void* biases,
+                             const void* x, void* y, uint32_t t, uint32_t n, uint32_t k, uint32_t x_stride,
+                             uint32_t y_stride, tf_scale_type st, void* stream);
+
+/* Prefill shared expert: per token the SharedExpertRuntime.encode arithmetic
+ * (SharedExpertInt4.swift:97-137, g = half(gate.x), u = half(up.x),
+ * act = half(gelu(g) * u), y = half(down.act)) over T tokens at once
+ * (the reference loops T GEMVs, PrefillSharedExpert.swift:43-58).
+ * act_scratch: fp16[T][gate.rows], 16-byte aligned.  int4 projections only. */
+TF_API tf_status tf_prefill_shared_expert(tf_context* ctx, const void* x, uint32_t x_stride,
+                                          const tf_affine_matrix* gate, const tf_affine_matrix* up,
+                                          const tf_affine_matrix* down, void* act_scratch, void* y,
+                                          uint32_t y_stride, uint32_t T, tf_scale_type st, void* stream);
+
+/* PrefillGroupedRoutedMoE.encodeStreamedBatched
+ * (Sources/TurboFieldfare/Kernels/Prefill/MoE/PrefillGroupedRoutedMoE.swift:446-527;
+ * prefill.metal:336-440,598-670) over every group at once: for sorted pair p
+ * = (token t, expert e, rank r)
+ *   act_scratch[p][j]          = half(gelu(gate_e[j].x_t) * (up_e[j].x_t))
+ *   route_partials[t*top_k+r][i] = half(down_e[i].act_scratch[p])
+ * sorted_pairs / groups / n_groups are the device outputs of tf_moe_route_sort
+ * (or the host grouping copied to the device).  act_scratch: fp16[T*top_k][f];
+ * route_partials: fp16[T*top_k][d].  num_experts <= 256, d and f multiples of 64,
+ * expert matrices 16-byte aligned inside the blob. */
+TF_API tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64_t expert_stride,
+                                       uint32_t num_experts, const tf_expert_offsets* offsets,
+                                       const void* sorted_pairs, const void* groups, const void* n_groups,
+                                       const void* hidden, uint32_t hidden_stride, void* act_scratch,
+                                       void* route_partials, uint32_t T, uint32_t d, uint32_t f, uint32_t top_k,
+                                       tf_scale_type st, void* stream);
+
+/* PrefillMoE.encodeReduceTokenMajor (Sources/TurboFieldfare/Kernels/Prefill/MoE/PrefillMoE.swift:11-40;
+ * prefill.metal:575-596): h2[t][i] = half(sum_r fma(w[t][r], partial[t*top_k+r][i])), rank order.
+ * routing_weights fp16[T][top_k]; partials and h2 16-byte aligned, d % 8 == 0. */
+TF_API tf_status tf_moe_reduce_token_major(tf_context* ctx, const void* route_partials, const void* routing_weights,
+                                           void* h2, uint32_t T, uint32_t top_k, uint32_t d, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,174 @@
+"""GPU parity of the tensor-core prefill GEMMs against the C oracle.
+
+* tf_int4_qmm              vs orc_int4_qmm (PrefillInt4QMM, prefill.metal:672-709)
+* tf_prefill_shared_expert vs the per-token shared expert (SharedExpertRuntime arithmetic)
+* tf_moe_grouped_routed    vs orc_grouped_routed (prefill.metal:336-440,598-670)
+* tf_moe_reduce_token_major vs orc_reduce_token_major (bit-exact: same fma order)
+Tolerance: RelError (RelError.swift:7-16) <= 2e-3 for fp16 outputs.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from edgeexpert_b200.prefill import (PrefillGroupedRoutedMoE, PrefillInt4QMM, PrefillMoE, PrefillRouter,
+                                     PrefillSharedExpert, route_sort)
+
+pytestmark = pytest.mark.gpu
+FP16_TOL = 2e-3
+
+
+def dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return t.view(dtype) if dtype is not None else t
+
+
+def f16(t):
+    return t.cpu().numpy().view(np.uint16)
+
+
+def sdt(scale_type):
+    return torch.bfloat16 if scale_type == 0 else torch.float16
+
+
+@pytest.mark.parametrize("T,N,K,st", [(1, 128, 64, 0), (17, 200, 128, 0), (300, 2112, 2816, 0), (256, 384, 704, 0),
+                                      (257, 128, 256, 1), (513, 136, 192, 0)])
+def test_int4_qmm(cuda, T, N, K, st):
+    rng = O.seed_tree(T * 31 + N, f"qmm-{K}-{st}")
+    W, S, B = rng.synthetic_affine(N, K, 4, st)
+    X = rng.normal_f16(T * K).reshape(T, K)
+    _, y32 = O.int4_qmm(W, S, B, X, T, N, K, st)
+    y = torch.empty(T, N, dtype=torch.float16, device="cuda")
+    PrefillInt4QMM().encode(dev(W), dev(S, sdt(st)), dev(B, sdt(st)), dev(X, torch.float16), y, T, N, K)
+    torch.cuda.synchronize()
+    assert O.rel_error(O.f16_to_f32(f16(y)), y32) < FP16_TOL
+
+
+def test_int4_qmm_strided_rows(cuda):
+    T, N, K, LX, LY = 40, 256, 256, 320, 272
+    rng = O.seed_tree(5, "qmm-strided")
+    W, S, B = rng.synthetic_affine(N, K, 4, 0)
+    X = rng.normal_f16(T * K).reshape(T, K)
+    Xs = np.zeros((T, LX), np.uint16)
+    Xs[:, :K] = X
+    _, y32 = O.int4_qmm(W, S, B, X, T, N, K, 0)
+    y = torch.full((T, LY), 7.0, dtype=torch.float16, device="cuda")
+    PrefillInt4QMM().encode(dev(W), dev(S, torch.bfloat16), dev(B, torch.bfloat16), dev(Xs, torch.float16), y, T,
+                            N, K, x_stride=LX, y_stride=LY)
+    torch.cuda.synchronize()
+    out = y.cpu().float().numpy()
+    assert O.rel_error(out[:, :N].reshape(-1), y32) < FP16_TOL
+    assert np.all(out[:, N:] == 7.0)  # nothing written past n
+
+
+def test_int4_qmm_deterministic(cuda):
+    T, N, K = 300, 384, 512
+    rng = O.seed_tree(8, "qmm-det")
+    W, S, B = rng.synthetic_affine(N, K, 4, 0)
+    X = rng.normal_f16(T * K).reshape(T, K)
+    args = (dev(W), dev(S, torch.bfloat16), dev(B, torch.bfloat16), dev(X, torch.float16))
+    ys = []
+    for _ in range(2):
+        y = torch.empty(T, N, dtype=torch.float16, device="cuda")
+        PrefillInt4QMM().encode(*args, y, T, N, K)
+        ys.append(f16(y))
+    torch.cuda.synchronize()
+    assert np.array_equal(ys[0], ys[1])
+
+
+@pytest.mark.parametrize("T,D,Fs", [(5, 128, 64), (40, 2816, 2112)])
+def test_prefill_shared_expert(cuda, T, D, Fs):
+    from edgeexpert_b200.moe import SharedExpertProjection
+    rng = O.seed_tree(T, f"pshared-{D}")
+    g = rng.synthetic_affine(Fs, D, 4, 0)
+    u = rng.synthetic_affine(Fs, D, 4, 0)
+    d = rng.synthetic_affine(D, Fs, 4, 0)
+    X = rng.normal_f16(T * D).reshape(T, D)
+    act_ref = np.empty((T, Fs), np.uint16)
+    y_ref = np.empty((T, D), np.float32)
+    for t in range(T):
+        a, _, y32 = O.shared_expert(g, u, d, X[t], D, Fs, 4)
+        act_ref[t], y_ref[t] = a, y32
+
+    def proj(m, rows, cols):
+        return SharedExpertProjection(dev(m[0]), dev(m[1], torch.bfloat16), dev(m[2], torch.bfloat16), rows, cols, 4)
+    act = torch.empty(T, Fs, dtype=torch.float16, device="cuda")
+    y = torch.empty(T, D, dtype=torch.float16, device="cuda")
+    PrefillSharedExpert().encode(dev(X, torch.float16), proj(g, Fs, D), proj(u, Fs, D), proj(d, D, Fs), act, y, T)
+    torch.cuda.synchronize()
+    assert O.rel_error(O.f16_to_f32(f16(act)), O.f16_to_f32(act_ref)) < FP16_TOL
+    assert O.rel_error(O.f16_to_f32(f16(y)), y_ref) < FP16_TOL
+
+
+class Experts:
+    """num_experts random experts in the reference blob layout (host + pool)."""
+
+    def __init__(self, E, D, F, scale_type=0, label="gexperts"):
+        from edgeexpert_b200.format import expert_layout
+        self.E, self.D, self.F, self.st = E, D, F, scale_type
+        self.lay = expert_layout(D, F)
+        rng = O.seed_tree(0xE1, label)
+        o = self.lay.offsets
+        self.host = np.zeros((E, self.lay.stride), np.uint8)
+        for e in range(E):
+            for proj, rows, cols in (("gate", F, D), ("up", F, D), ("down", D, F)):
+                W, S, B = rng.synthetic_affine(rows, cols, 4, scale_type)
+                for part, arr in (("w", W), ("s", S), ("b", B)):
+                    b = np.ascontiguousarray(arr).view(np.uint8).reshape(-1)
+                    off = getattr(o, f"{proj}_{part}")
+                    self.host[e, off:off + b.size] = b
+        self.off = O.Offsets(*[getattr(o, n) for n, _ in O.Offsets._fields_])
+
+    def pool(self):
+        from edgeexpert_b200.moe import ExpertPool
+        return ExpertPool(dev(self.host.reshape(-1)), self.lay.stride, self.E, self.lay.offsets, self.D, self.F,
+                          sdt(self.st))
+
+
+def skewed_routing(T, K, E, seed):
+    rng = np.random.default_rng(seed)
+    p = rng.random(E) ** 3 + 1e-3
+    p /= p.sum()
+    idx = np.stack([rng.choice(E, K, replace=False, p=p) for _ in range(T)]).astype(np.uint32)
+    w = (rng.random((T, K)) * 0.3 + 0.05).astype(np.float16)
+    return idx, w
+
+
+@pytest.mark.parametrize("T,K,E,D,F,st", [(37, 4, 16, 128, 64, 0), (300, 2, 2, 128, 64, 0), (64, 8, 16, 2816, 704, 0),
+                                          (9, 8, 32, 256, 128, 1)])
+def test_grouped_routed_and_reduce(cuda, T, K, E, D, F, st):
+    ex = Experts(E, D, F, st, f"g-{E}-{D}-{F}-{st}")
+    idx, w = skewed_routing(T, K, E, T + E)
+    X = O.seed_tree(T, f"gx-{D}").normal_f16(T * D).reshape(T, D)
+    pairs = PrefillRouter.make_token_expert_pairs(idx, w, T, K)
+    ref = O.group_pairs(pairs, T, K, E, 16)
+    part_ref = O.grouped_routed(ex.host.reshape(-1), ex.lay.stride, ex.off, ref["sorted"], X, D, D, F, K, T, st)
+    routes = route_sort(dev(idx.view(np.int32)), dev(w), T, K, E, 16)
+    act = torch.empty(T * K, F, dtype=torch.float16, device="cuda")
+    part = torch.empty(T * K, D, dtype=torch.float16, device="cuda")
+    PrefillGroupedRoutedMoE().encode(ex.pool(), routes, dev(X, torch.float16), act, part, T, K)
+    torch.cuda.synchronize()
+    assert O.rel_error(O.f16_to_f32(f16(part)), O.f16_to_f32(part_ref)) < FP16_TOL
+    # token-major reduce of the oracle's partials: same fma order, bit-exact
+    h2 = torch.empty(T, D, dtype=torch.float16, device="cuda")
+    PrefillMoE.encode_reduce_token_major(dev(part_ref, torch.float16), dev(w), h2, T, K, D)
+    torch.cuda.synchronize()
+    h2_ref = O.reduce_token_major(part_ref, w.view(np.uint16), T, K, D)
+    assert np.array_equal(f16(h2).reshape(-1), h2_ref)
+
+
+def test_grouped_routed_empty_routes(cuda):
+    """T = 0 is a no-op; a route table with no groups writes nothing."""
+    ex = Experts(4, 128, 64, 0, "g-empty")
+    T, K = 3, 2
+    routes = route_sort(dev(np.zeros((T, K), np.int32)), dev(np.zeros((T, K), np.float16)), T, K, 4, 16)
+    routes.n_groups.zero_()
+    part = torch.full((T * K, 128), 3.0, dtype=torch.float16, device="cuda")
+    act = torch.empty(T * K, 64, dtype=torch.float16, device="cuda")
+    PrefillGroupedRoutedMoE().encode(ex.pool(), routes, torch.zeros(T, 128, dtype=torch.float16, device="cuda"),
+                                     act, part, T, K)
+    torch.cuda.synchronize()
+    assert bool((part == 3.0).all())
+    PrefillGroupedRoutedMoE().encode(ex.pool(), routes, torch.zeros(T, 128, dtype=torch.float16, device="cuda"),
+                                     act, part, 0, K)
+    torch.cuda.synchronize()
