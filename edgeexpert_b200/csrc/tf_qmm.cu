@@ -15,17 +15,22 @@
 // One persistent kernel, one CTA per SM, warp-specialised:
 //   warps 0-3   epilogue: tcgen05.ld of the fp32 accumulator (TMEM lane = weight
 //               row), fused GELU(gate)*up, fp16 stores
-//   warps 4-7   activation loader: 256 token rows x 128 B per k-block by
-//               cp.async into the 128-byte-swizzled K-major operand layout
-//               (rows gathered through the sorted token->expert pairs)
-//   warps 8-15  weight loader: int4 nibbles + bf16/fp16 scale/bias ->
-//               fp16 w = fma(q, s, b) (one rounding), same swizzled layout
-//   warp 16     TMEM allocation and the single-thread tcgen05.mma issue
+//   warp 4      loader: one thread issues, per k-block, the TMA loads of the
+//               raw int4 weight tile (2 boxes of 64 rows x 32 B, 3-D maps so
+//               a pool expert is one coordinate) and of the activation rows
+//               (64-row boxes, 128-byte swizzle = the K-major operand layout,
+//               only as many boxes as the tile has rows)
+//   warps 5-12  dequantiser: raw nibbles from shared memory + bf16/fp16
+//               scale/bias -> fp16 w = fma(q, s, b) (one rounding) in the
+//               swizzled K-major layout; scales come through a register ring
+//   warp 13     TMEM allocation and the single-thread tcgen05.mma issue
 // Tile: 128 weight rows (M) x up to 256 tokens (N), k-block 64 (= one
-// quantisation group), 4 shared-memory stages of 48 KB, two TMEM accumulators
+// quantisation group), 4 shared-memory stages of 52 KB, two TMEM accumulators
 // of 256 fp32 columns so the epilogue of one tile overlaps the next tile's
 // main loop.  Gate/up projections interleave their rows (even = gate, odd = up)
-// so a lane pair holds both operands of GELU(g)*u after one shuffle.
+// so a lane pair holds both operands of GELU(g)*u after one shuffle.  Routed
+// rows are first gathered into sorted-pair order (gather_rows_kernel) so that
+// every expert's tokens are one contiguous TMA range.
 #include "tf_context.cuh"
 #include "tf_umma.cuh"
 
@@ -34,17 +39,20 @@ using namespace tf;
 namespace {
 
 constexpr int kEpiWarps = 4;
-constexpr int kBWarps = 4;
+constexpr int kLoadWarp = 4;
 constexpr int kAWarps = 8;
-constexpr int kMmaWarp = kEpiWarps + kBWarps + kAWarps;  // 16
+constexpr int kAWarp0 = 5;
+constexpr int kMmaWarp = kAWarp0 + kAWarps;  // 13
 constexpr int kQWarps = kMmaWarp + 1;
 constexpr int kQThreads = kQWarps * 32;
 constexpr int kStages = 4;
+constexpr int kRing = 8;               // scale/bias prefetch depth (k-blocks)
 constexpr int kTM = 128;               // weight rows per tile (MMA M)
 constexpr int kTN = 256;               // tokens per tile (MMA N, max)
-constexpr int kAStage = kTM * 128;     // 16 KB
-constexpr int kBStage = kTN * 128;     // 32 KB
-constexpr int kBLag = 2;               // cp.async groups in flight per loader thread
+constexpr int kAStage = kTM * 128;     // 16 KB fp16 operand
+constexpr int kBStage = kTN * 128;     // 32 KB fp16 operand
+constexpr int kRawStage = kTM * 32;    // 4 KB packed int4
+constexpr int kBBoxRows = 64;          // rows per activation TMA box (8 KB)
 constexpr int kAccCols = 256;
 constexpr int kTmemCols = 512;
 constexpr int kMaxGroups = 256;
@@ -53,29 +61,23 @@ constexpr uint32_t kQSpin = 1u << 24;
 enum QMode : int { kDensePlain = 0, kDenseGateUp = 1, kGroupedGateUp = 2, kGroupedDown = 3 };
 
 struct QmmParams {
+    CUtensorMap xmap;   // activations [rows][K] fp16
+    CUtensorMap wmap0;  // packed weights (plain / gate), [depth][rows][K/2] uint8
+    CUtensorMap wmap1;  // packed weights (up)
     int mode;
     int K;      // reduction length (multiple of 64)
     int nfeat;  // rows of one weight matrix (output features)
     int T;      // dense: tokens
-    // dense weights: matrix 0 (plain / gate), matrix 1 (up)
-    const uint8_t* w0;
-    const void* s0;
-    const void* b0;
-    const uint8_t* w1;
-    const void* s1;
-    const void* b1;
-    // grouped: expert e's matrix at pool + e*stride + offset
-    const uint8_t* pool;
+    // scales/biases of matrix 0 (plain / gate) and 1 (up); grouped: offsets
+    // from the expert's blob at pool + e*stride
+    const uint8_t* sbase;
     uint64_t stride;
-    uint32_t ow0, os0, ob0, ow1, os1, ob1;
+    uint64_t os0, ob0, os1, ob1;
     uint32_t num_experts;
     const tf_moe_group* groups;
     const uint32_t* n_groups;
     const tf_token_expert_pair* pairs;
     int top_k;
-    // activations
-    const __half* x;
-    long long ldx;
     __half* y;
     long long ldy;
     int round_gu;  // gate/up rounded to fp16 before GELU (shared expert)
@@ -83,8 +85,9 @@ struct QmmParams {
 };
 
 struct QShared {
-    uint64_t full[kStages];
-    uint64_t empty[kStages];
+    uint64_t ldfull[kStages];  // TMA bytes (raw weights + activations) landed
+    uint64_t full[kStages];    // dequantised operand written
+    uint64_t empty[kStages];   // MMAs of the stage retired
     uint64_t tfull[2];
     uint64_t tempty[2];
     uint64_t done;
@@ -98,7 +101,8 @@ struct QShared {
     int gexpert[kMaxGroups];
 };
 
-constexpr size_t kQSmemBytes = 1024 + (size_t)kStages * (kAStage + kBStage) + sizeof(QShared);
+constexpr size_t kQSmemBytes = 1024 + (size_t)kStages * (kAStage + kBStage + kRawStage) + sizeof(QShared);
+static_assert(kQSmemBytes <= 232448, "shared memory");
 
 struct QTile {
     int feat0;
@@ -107,16 +111,16 @@ struct QTile {
     int expert;
 };
 
-__device__ __forceinline__ int feat_per_tile(int mode) {
-    return (mode == kDenseGateUp || mode == kGroupedGateUp) ? kTM / 2 : kTM;
-}
+__device__ __forceinline__ bool gate_up(int mode) { return mode == kDenseGateUp || mode == kGroupedGateUp; }
+__device__ __forceinline__ bool grouped(int mode) { return mode == kGroupedGateUp || mode == kGroupedDown; }
+__device__ __forceinline__ int feat_per_tile(int mode) { return gate_up(mode) ? kTM / 2 : kTM; }
 
 __device__ __forceinline__ bool decode_tile(const QmmParams& p, const QShared& sh, int idx, QTile& t) {
     if (idx >= sh.total) return false;
     const int fpt = feat_per_tile(p.mode);
     const int nft = (p.nfeat + fpt - 1) / fpt;
-    if (p.mode == kDensePlain || p.mode == kDenseGateUp) {
-        const int tt = idx / nft, ft = idx % nft;
+    if (!grouped(p.mode)) {
+        const int tt = idx / nft, ft = idx - tt * nft;
         t.feat0 = ft * fpt;
         t.row0 = tt * kTN;
         t.cnt = min(kTN, p.T - t.row0);
@@ -132,7 +136,7 @@ __device__ __forceinline__ bool decode_tile(const QmmParams& p, const QShared& s
     const int g = lo, local = idx - sh.prefix[g], c = sh.gcount[g];
     const int ntt = (c + kTN - 1) / kTN;
     const int q = (c + ntt - 1) / ntt;
-    const int tt = local / nft, ft = local % nft;
+    const int tt = local / nft, ft = local - tt * nft;
     t.feat0 = ft * fpt;
     t.row0 = sh.gstart[g] + tt * q;
     t.cnt = min(q, c - tt * q);
@@ -155,23 +159,23 @@ __device__ __forceinline__ uint32_t sw128(int row, int chunk) {
     return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
 __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
-__device__ __forceinline__ uint4 ldg_nc16(const void* p) {
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
     uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+                 : "memory");
     return v;
+}
+
+__device__ __forceinline__ void tma_load_3d_u8(void* dst, const void* tmap, int x, int y, int z, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_u32(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
 }
 
 // fp16 bits of a bf16 / fp16 scale or bias
@@ -224,39 +228,28 @@ __device__ __forceinline__ void cursor_next(const QmmParams& p, const QShared& s
     }
 }
 
-struct ALoad {
-    uint4 q;
-    uint32_t s, b;
-    bool ok;
+struct SLoad {
+    uint32_t sb;  // fp16 scale (low) | fp16 bias (high); 0 = row absent
 };
 
+// scale and bias of this thread's row for the cursor's k-block
 template <typename ST>
-__device__ __forceinline__ ALoad a_load(const QmmParams& p, const QCursor& c, int r, int h) {
-    ALoad a;
-    a.ok = false;
+__device__ __forceinline__ SLoad s_load(const QmmParams& p, const QCursor& c, int r) {
+    SLoad a;
+    a.sb = 0;
     if (!c.valid) return a;
-    const bool gu = (p.mode == kDenseGateUp || p.mode == kGroupedGateUp);
+    const bool gu = gate_up(p.mode);
     const int mat = gu ? (r & 1) : 0;
     const int f = c.t.feat0 + (gu ? (r >> 1) : r);
     if (f >= p.nfeat) return a;
-    const uint8_t* W;
-    const ST* S;
-    const ST* B;
-    if (p.mode == kDensePlain || p.mode == kDenseGateUp) {
-        W = mat ? p.w1 : p.w0;
-        S = static_cast<const ST*>(mat ? p.s1 : p.s0);
-        B = static_cast<const ST*>(mat ? p.b1 : p.b0);
-    } else {
-        const uint8_t* base = p.pool + (uint64_t)c.t.expert * p.stride;
-        W = base + (mat ? p.ow1 : p.ow0);
-        S = reinterpret_cast<const ST*>(base + (mat ? p.os1 : p.os0));
-        B = reinterpret_cast<const ST*>(base + (mat ? p.ob1 : p.ob0));
-    }
-    const int G = p.K >> 6;
-    a.q = ldg_nc16(W + (size_t)f * (p.K >> 1) + c.kb * 32 + h * 16);
-    a.s = scale_bits_f16<ST>(S + (size_t)f * G + c.kb);
-    a.b = scale_bits_f16<ST>(B + (size_t)f * G + c.kb);
-    a.ok = true;
+    // dense: os/ob are addresses; grouped: byte offsets inside the expert's blob
+    const uint64_t base = grouped(p.mode) ? reinterpret_cast<uint64_t>(p.sbase) + (uint64_t)c.t.expert * p.stride : 0;
+    const ST* S = reinterpret_cast<const ST*>(base + (mat ? p.os1 : p.os0));
+    const ST* B = reinterpret_cast<const ST*>(base + (mat ? p.ob1 : p.ob0));
+    const size_t i = (size_t)f * (p.K >> 6) + c.kb;
+    const uint32_t s = scale_bits_f16<ST>(S + i), b = scale_bits_f16<ST>(B + i);
+    a.sb = s | (b << 16);
+    // a present row whose scale and bias are both +0 still dequantises to 0
     return a;
 }
 
@@ -265,8 +258,9 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
     extern __shared__ uint8_t q_smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(q_smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* As = smem;
-    uint8_t* Bs = smem + kStages * kAStage;
-    QShared& sh = *reinterpret_cast<QShared*>(Bs + kStages * kBStage);
+    uint8_t* Bs = As + kStages * kAStage;
+    uint8_t* Ws = Bs + kStages * kBStage;
+    QShared& sh = *reinterpret_cast<QShared*>(Ws + kStages * kRawStage);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nkb = p.K >> 6;
     const int fpt = feat_per_tile(p.mode);
@@ -275,7 +269,8 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
     // ---- setup: barriers, tile table, TMEM ----
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(&sh.full[s], kAWarps + kBWarps);
+            mbar_init(&sh.ldfull[s], 1);
+            mbar_init(&sh.full[s], kAWarps);
             mbar_init(&sh.empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -286,7 +281,7 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
         sh.abort_flag = 0;
         fence_mbar_init();
     }
-    if (p.mode == kDensePlain || p.mode == kDenseGateUp) {
+    if (!grouped(p.mode)) {
         if (tid == 0) {
             sh.ng = 0;
             sh.total = ((p.T + kTN - 1) / kTN) * nft;
@@ -339,106 +334,83 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
     tc_fence_after();
     const uint32_t tmem = sh.tmem_base;
 
-    if (warp >= kEpiWarps + kBWarps && warp < kMmaWarp) {
-        // ================= weight loader / dequantiser =================
-        const int at = tid - (kEpiWarps + kBWarps) * 32;  // 0..255
+    if (warp >= kAWarp0 && warp < kMmaWarp) {
+        // ================= dequantiser =================
+        const int at = tid - kAWarp0 * 32;  // 0..255
         const int r = at >> 1, h = at & 1;
+        // raw rows: plain = r; gate/up = gate rows 0-63, up rows 64-127
+        const int rr = gate_up(p.mode) ? ((r & 1) * 64 + (r >> 1)) : r;
         QCursor lc, pc;
         cursor_start(p, sh, lc);
         pc = lc;
-        ALoad ring[kStages];
+        SLoad ring[kRing];
 #pragma unroll
-        for (int j = 0; j < kStages; ++j) {
-            ring[j] = a_load<ST>(p, lc, r, h);
+        for (int j = 0; j < kRing; ++j) {
+            ring[j] = s_load<ST>(p, lc, r);
             cursor_next(p, sh, lc, nkb);
         }
-        uint32_t phase = 0;
         bool live = true;
         while (pc.valid && live) {
 #pragma unroll
-            for (int j = 0; j < kStages; ++j) {
+            for (int j = 0; j < kRing; ++j) {
                 if (!pc.valid || !live) break;
-                const ALoad cur = ring[j];
-                ring[j] = a_load<ST>(p, lc, r, h);
+                const int s = j & (kStages - 1);
+                const uint32_t par = (uint32_t)(j / kStages) & 1u;
+                const SLoad cur = ring[j];
+                ring[j] = s_load<ST>(p, lc, r);
                 cursor_next(p, sh, lc, nkb);
-                if (!qwait(&sh.empty[j], phase ^ 1u, sh, p.err)) {
+                if (!qwait(&sh.ldfull[s], par, sh, p.err)) {
                     live = false;
                     break;
                 }
-                const uint32_t dst = smem_u32(As + j * kAStage);
-                if (cur.ok) {
-                    const uint32_t s2 = cur.s | (cur.s << 16), b2 = cur.b | (cur.b << 16);
-                    const uint32_t wv[4] = {cur.q.x, cur.q.y, cur.q.z, cur.q.w};
+                const uint4 q = lds128(smem_u32(Ws + s * kRawStage + rr * 32 + h * 16));
+                const uint32_t s2 = (cur.sb & 0xFFFFu) * 0x10001u, b2 = (cur.sb >> 16) * 0x10001u;
+                const uint32_t dst = smem_u32(As + s * kAStage);
+                const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        uint32_t o[4];
-                        dq8_natural(wv[i], s2, b2, o);
-                        sts128(dst + sw128(r, h * 4 + i), o[0], o[1], o[2], o[3]);
-                    }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) sts128(dst + sw128(r, h * 4 + i), 0u, 0u, 0u, 0u);
+                for (int i = 0; i < 4; ++i) {
+                    uint32_t o[4];
+                    dq8_natural(wv[i], s2, b2, o);
+                    sts128(dst + sw128(r, h * 4 + i), o[0], o[1], o[2], o[3]);
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&sh.full[j]);
+                if (lane == 0) mbar_arrive(&sh.full[s]);
                 cursor_next(p, sh, pc, nkb);
             }
-            phase ^= 1u;
         }
-    } else if (warp >= kEpiWarps && warp < kEpiWarps + kBWarps) {
-        // ================= activation loader (cp.async) =================
-        const int bt = tid - kEpiWarps * 32;  // 0..127
-        const int c = bt & 7, r0 = bt >> 3;   // rows r0 + 16 j
-        QCursor cur;
-        cursor_start(p, sh, cur);
-        long long roff[16];
-        int it = 0;
-        int last_idx = -1;
-        bool live = true;
-        while (cur.valid && live) {
-            if (cur.idx != last_idx) {
-                last_idx = cur.idx;
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int row = r0 + 16 * j;
-                    long long off = -1;
-                    if (row < cur.t.cnt) {
-                        const int rr = cur.t.row0 + row;
-                        if (p.mode == kGroupedGateUp)
-                            off = (long long)p.pairs[rr].token * p.ldx;
-                        else
-                            off = (long long)rr * p.ldx;
-                    }
-                    roff[j] = off;
+    } else if (warp == kLoadWarp) {
+        // ================= TMA loader (one thread) =================
+        if (lane == 0) {
+            prefetch_tmap(&p.xmap);
+            prefetch_tmap(&p.wmap0);
+            if (gate_up(p.mode)) prefetch_tmap(&p.wmap1);
+            QCursor cur;
+            cursor_start(p, sh, cur);
+            int it = 0;
+            while (cur.valid) {
+                const int s = it % kStages;
+                if (!qwait(&sh.empty[s], ((uint32_t)(it / kStages) & 1u) ^ 1u, sh, p.err)) break;
+                const int nbox = (cur.t.cnt + kBBoxRows - 1) / kBBoxRows;
+                mbar_arrive_expect_tx(&sh.ldfull[s], (uint32_t)(nbox * kBBoxRows * 128 + kRawStage));
+                uint8_t* w = Ws + s * kRawStage;
+                const int z = cur.t.expert;
+                if (gate_up(p.mode)) {
+                    tma_load_3d_u8(w, &p.wmap0, cur.kb * 32, cur.t.feat0, z, &sh.ldfull[s]);
+                    tma_load_3d_u8(w + kRawStage / 2, &p.wmap1, cur.kb * 32, cur.t.feat0, z, &sh.ldfull[s]);
+                } else {
+                    tma_load_3d_u8(w, &p.wmap0, cur.kb * 32, cur.t.feat0, z, &sh.ldfull[s]);
+                    tma_load_3d_u8(w + kRawStage / 2, &p.wmap0, cur.kb * 32, cur.t.feat0 + 64, z, &sh.ldfull[s]);
                 }
+                uint8_t* dst = Bs + s * kBStage;
+                for (int i = 0; i < nbox; ++i)
+                    tma_load_2d(dst + i * kBBoxRows * 128, &p.xmap, cur.kb * 64, cur.t.row0 + i * kBBoxRows,
+                                &sh.ldfull[s]);
+                ++it;
+                cursor_next(p, sh, cur, nkb);
             }
-            const int s = it % kStages;
-            const uint32_t ph = (uint32_t)(it / kStages) & 1u;
-            if (!qwait(&sh.empty[s], ph ^ 1u, sh, p.err)) {
-                live = false;
-                break;
-            }
-            const uint32_t dst = smem_u32(Bs + s * kBStage);
-            const __half* xk = p.x + cur.kb * 64 + c * 8;
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-                if (roff[j] >= 0) cp_async16(dst + sw128(r0 + 16 * j, c), xk + roff[j]);
-            cp_async_commit();
-            if (it >= kBLag) {
-                cp_async_wait<kBLag>();
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sh.full[(it - kBLag) % kStages]);
-            }
-            ++it;
-            cursor_next(p, sh, cur, nkb);
         }
-        cp_async_wait<0>();
-        fence_proxy_async_smem();
         __syncwarp();
-        if (live && lane == 0)
-            for (int k = max(0, it - kBLag); k < it; ++k) mbar_arrive(&sh.full[k % kStages]);
     } else if (warp == kMmaWarp) {
         // ================= MMA issue (one thread) =================
         int it = 0, lt = 0;
@@ -457,7 +429,8 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
             const uint32_t d = tmem + (uint32_t)(acc * kAccCols);
             for (int kb = 0; kb < nkb; ++kb, ++it) {
                 const int s = it % kStages;
-                if (!qwait(&sh.full[s], (uint32_t)(it / kStages) & 1u, sh, p.err)) {
+                const uint32_t par = (uint32_t)(it / kStages) & 1u;
+                if (!qwait(&sh.full[s], par, sh, p.err) || !qwait(&sh.ldfull[s], par, sh, p.err)) {
                     live = false;
                     break;
                 }
@@ -487,7 +460,7 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
         // ================= epilogue (warps 0-3) =================
         const int ew = warp;  // TMEM lanes 32*ew .. 32*ew+31
         const int row = ew * 32 + lane;
-        const bool gu = (p.mode == kDenseGateUp || p.mode == kGroupedGateUp);
+        const bool gu = gate_up(p.mode);
         int lt = 0;
         for (int idx = blockIdx.x;; idx += gridDim.x, ++lt) {
             QTile t;
@@ -549,6 +522,26 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
     }
 }
 
+// Xg[p][:] = X[pairs[p].token][:] (16-byte units): the routed rows in
+// sorted-pair order, so each expert's tokens are one contiguous TMA range.
+__global__ void gather_rows_kernel(const __half* __restrict__ x, long long ldx,
+                                   const tf_token_expert_pair* __restrict__ pairs, __half* __restrict__ xg, int P,
+                                   int D, int T, uint32_t* err) {
+    const int d8 = D >> 3;
+    const long long n = (long long)P * d8;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int pr = (int)(i / d8), c = (int)(i - (long long)pr * d8);
+        const uint32_t tok = __ldg(&pairs[pr].token);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (tok < (uint32_t)T)
+            v = __ldg(reinterpret_cast<const uint4*>(x + (long long)tok * ldx) + c);
+        else if (c == 0 && err)
+            atomicOr(err, kErrBadExpert);
+        reinterpret_cast<uint4*>(xg + (long long)pr * D)[c] = v;
+    }
+}
+
 // h2[t][d] = half(sum_r fma(w[t][r], partial[t*K + r][d])) in rank order
 // (prefill.metal:575-596).  8 outputs per thread, 16-byte loads.
 __global__ void reduce_token_major_kernel(const __half* __restrict__ partials, const __half* __restrict__ w,
@@ -596,6 +589,21 @@ tf_status launch_qmm(tf_context* ctx, const QmmParams& p, tf_scale_type st, int 
 
 bool scale_type_ok(tf_scale_type st) { return st == TF_SCALE_BF16 || st == TF_SCALE_F16; }
 
+
+// Dense weight matrix [n][k] as a one-deep raw map plus scale/bias addresses.
+bool dense_weights(QmmParams& p, CUtensorMap* m, const void* w, uint32_t rows, uint32_t k, const void* sc,
+                   const void* bi, int which) {
+    if (!make_raw_map(m, w, k / 2, rows, 1, 0)) return false;
+    if (which == 0) {
+        p.os0 = reinterpret_cast<uint64_t>(sc);
+        p.ob0 = reinterpret_cast<uint64_t>(bi);
+    } else {
+        p.os1 = reinterpret_cast<uint64_t>(sc);
+        p.ob1 = reinterpret_cast<uint64_t>(bi);
+    }
+    return true;
+}
+
 }  // namespace
 
 extern "C" {
@@ -621,11 +629,8 @@ tf_status tf_int4_qmm(tf_context* ctx, const void* weights, const void* scales, 
     p.K = (int)k;
     p.nfeat = (int)n;
     p.T = (int)t;
-    p.w0 = static_cast<const uint8_t*>(weights);
-    p.s0 = scales;
-    p.b0 = biases;
-    p.x = static_cast<const __half*>(x);
-    p.ldx = x_stride;
+    if (!dense_weights(p, &p.wmap0, weights, n, k, scales, biases, 0) || !make_act_map(&p.xmap, x, k, t, x_stride))
+        return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: tensor map rejected", name);
     p.y = static_cast<__half*>(y);
     p.ldy = y_stride;
     p.err = ctx->d_err;
@@ -666,14 +671,10 @@ tf_status tf_prefill_shared_expert(tf_context* ctx, const void* x, uint32_t x_st
     p.K = (int)d;
     p.nfeat = (int)f;
     p.T = (int)t;
-    p.w0 = static_cast<const uint8_t*>(gate->weights);
-    p.s0 = gate->scales;
-    p.b0 = gate->biases;
-    p.w1 = static_cast<const uint8_t*>(up->weights);
-    p.s1 = up->scales;
-    p.b1 = up->biases;
-    p.x = static_cast<const __half*>(x);
-    p.ldx = x_stride;
+    if (!dense_weights(p, &p.wmap0, gate->weights, f, d, gate->scales, gate->biases, 0) ||
+        !dense_weights(p, &p.wmap1, up->weights, f, d, up->scales, up->biases, 1) ||
+        !make_act_map(&p.xmap, x, d, t, x_stride))
+        return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: tensor map rejected", name);
     p.y = static_cast<__half*>(act_scratch);
     p.ldy = f;
     p.round_gu = 1;
@@ -686,11 +687,9 @@ tf_status tf_prefill_shared_expert(tf_context* ctx, const void* x, uint32_t x_st
     q.K = (int)f;
     q.nfeat = (int)d;
     q.T = (int)t;
-    q.w0 = static_cast<const uint8_t*>(down->weights);
-    q.s0 = down->scales;
-    q.b0 = down->biases;
-    q.x = static_cast<const __half*>(act_scratch);
-    q.ldx = f;
+    if (!dense_weights(q, &q.wmap0, down->weights, d, f, down->scales, down->biases, 0) ||
+        !make_act_map(&q.xmap, act_scratch, f, t, f))
+        return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: tensor map rejected", name);
     q.y = static_cast<__half*>(y);
     q.ldy = y_stride;
     q.err = ctx->d_err;
@@ -717,20 +716,20 @@ tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64_t expe
     if (!aligned16(pool) || expert_stride % 16 || off->gate_w % 16 || off->up_w % 16 || off->down_w % 16 ||
         off->gate_s % 2 || off->gate_b % 2 || off->up_s % 2 || off->up_b % 2 || off->down_s % 2 || off->down_b % 2)
         return fail(ctx, TF_ERR_MISALIGNED, "%s: weight matrices 16-byte aligned", name);
-    if (!aligned16(hidden) || !aligned16(act_scratch) || !aligned2(route_partials) || !aligned4(sorted_pairs) ||
+    if (!aligned16(hidden) || !aligned16(act_scratch) || !aligned16(route_partials) || !aligned4(sorted_pairs) ||
         !aligned4(groups) || !aligned4(n_groups))
         return fail(ctx, TF_ERR_MISALIGNED, "%s: activation pointers", name);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const uint32_t P = t * top_k;
+    const uint8_t* pb = static_cast<const uint8_t*>(pool);
     QmmParams p{};
     p.mode = kGroupedGateUp;
     p.K = (int)d;
     p.nfeat = (int)f;
-    p.pool = static_cast<const uint8_t*>(pool);
+    p.sbase = pb;
     p.stride = expert_stride;
-    p.ow0 = off->gate_w;
     p.os0 = off->gate_s;
     p.ob0 = off->gate_b;
-    p.ow1 = off->up_w;
     p.os1 = off->up_s;
     p.ob1 = off->up_b;
     p.num_experts = num_experts;
@@ -738,24 +737,38 @@ tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64_t expe
     p.n_groups = static_cast<const uint32_t*>(n_groups);
     p.pairs = static_cast<const tf_token_expert_pair*>(sorted_pairs);
     p.top_k = (int)top_k;
-    p.x = static_cast<const __half*>(hidden);
-    p.ldx = hidden_stride;
     p.y = static_cast<__half*>(act_scratch);
     p.ldy = f;
     p.err = ctx->d_err;
-    tf_status rc = launch_qmm(ctx, p, st, ctx->num_sms, s, name);
-    if (rc != TF_OK) return rc;
+    // the routed rows in sorted-pair order are staged in the partials buffer
+    // (same [T*top_k][d] shape; the down projection overwrites it afterwards)
+    if (!make_raw_map(&p.wmap0, pb + off->gate_w, d / 2, f, num_experts, expert_stride) ||
+        !make_raw_map(&p.wmap1, pb + off->up_w, d / 2, f, num_experts, expert_stride) ||
+        !make_act_map(&p.xmap, route_partials, d, P, d))
+        return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: tensor map rejected", name);
     QmmParams q = p;
     q.mode = kGroupedDown;
     q.K = (int)f;
     q.nfeat = (int)d;
-    q.ow0 = off->down_w;
     q.os0 = off->down_s;
     q.ob0 = off->down_b;
-    q.x = static_cast<const __half*>(act_scratch);
-    q.ldx = f;
     q.y = static_cast<__half*>(route_partials);
     q.ldy = d;
+    if (!make_raw_map(&q.wmap0, pb + off->down_w, f / 2, d, num_experts, expert_stride) ||
+        !make_act_map(&q.xmap, act_scratch, f, P, f))
+        return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: tensor map rejected", name);
+    {
+        const long long n = (long long)P * (d / 8);
+        const int grid = (int)std::min<long long>((n + 255) / 256, (long long)ctx->num_sms * 8);
+        gather_rows_kernel<<<grid, 256, 0, s>>>(static_cast<const __half*>(hidden), hidden_stride,
+                                                static_cast<const tf_token_expert_pair*>(sorted_pairs),
+                                                static_cast<__half*>(route_partials), (int)P, (int)d, (int)t,
+                                                ctx->d_err);
+        tf_status rc0 = cuda_check(ctx, cudaGetLastError(), name);
+        if (rc0 != TF_OK) return rc0;
+    }
+    tf_status rc = launch_qmm(ctx, p, st, ctx->num_sms, s, name);
+    if (rc != TF_OK) return rc;
     return launch_qmm(ctx, q, st, ctx->num_sms, s, name);
 }
 
