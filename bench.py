@@ -49,6 +49,10 @@ def parse():
     ap.add_argument("--scale-dtype", choices=["bf16", "f16"], default="bf16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--workload", choices=["decode", "batched", "prefill"], default="decode",
+                    help="decode = config 1 (default, the headline); batched = config 2 (64 tokens); "
+                         "prefill = config 3 (4096 tokens)")
+    ap.add_argument("--tokens", type=int, default=0, help="override the chunk's token count (batched/prefill)")
     return ap.parse_args()
 
 
@@ -160,6 +164,25 @@ def run_reference(a, rank):
     if rank != 0:
         return
     lps, threads, sample = cpu_sample(max(5.0, a.cpu_seconds), "reference")
+    if a.workload != "decode":
+        T = a.tokens or CHUNK_TOKENS[a.workload]
+        step_s = T / lps
+        if a.workload == "prefill":
+            metric, unit, v = "MoE prefill TFLOP/s (config 3)", "TFLOP/s", chunk_flops(T) / step_s / 1e12
+        else:
+            # a CPU reads the weights of every routed expert the chunk hits; count all 128 (64 tokens x top-8
+            # over 128 experts hits nearly every expert)
+            metric, unit, v = "MoE batched-decode weight GB/s (config 2)", "GB/s", chunk_bytes(E) / step_s / 1e9
+        line = {"metric": metric, "value": v, "unit": unit, "impl": "reference", "n_gpus": a.gpus, "steps": a.steps,
+                "warmup": a.warmup, "ms_per_step": step_s * 1e3, "tok_s": lps, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32-acc/int4",
+                "data": "synthetic (BASELINE distributions, SplitMix64 seed 0)",
+                "config": {"workload": f"{T}-token chunk through the config-1 MoE layer", "tokens": T},
+                "cpu_baseline": {"value": v, "unit": unit, "cores": threads, "kind": "port",
+                                 "sample": sample + f"; scaled to a {T}-token chunk"},
+                "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     per_layer_b = layer_bytes()
     gbs = lps * per_layer_b / 1e9
     line = {
@@ -355,6 +378,234 @@ def run_ours(a, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------ chunk workloads ----
+CHUNK_TOKENS = {"batched": 64, "prefill": 4096}
+
+
+def chunk_flops(T: int) -> float:
+    """Algorithmic FLOPs of one chunk through the config-1 layer: router,
+    top-8 routed experts (gate, up, down) and the shared expert."""
+    return 2.0 * T * (TOPK * 3 * F * D + 3 * FS * D + E * D)
+
+
+def chunk_bytes(distinct: int) -> int:
+    """Algorithmic weight bytes of one chunk: every distinct routed expert,
+    the shared expert and the router, each read once."""
+    from edgeexpert_b200.format import affine_bytes
+    expert = 2 * affine_bytes(F, D) + affine_bytes(D, F)
+    shared = 2 * affine_bytes(FS, D) + affine_bytes(D, FS)
+    router = E * D + 2 * E * (D // 64) * 2
+    return distinct * expert + shared + router
+
+
+def run_chunk(a, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from edgeexpert_b200._lib import Context
+    from edgeexpert_b200.format import synthetic_moe_layer
+    from edgeexpert_b200.prefill import (PrefillGroupedRoutedMoE, PrefillMoE, PrefillRouter, PrefillSharedExpert,
+                                         route_sort)
+
+    T = a.tokens or CHUNK_TOKENS[a.workload]
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    ctx = Context.get(local_rank)
+    sdt = torch.bfloat16 if a.scale_dtype == "bf16" else torch.float16
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4321 + rank)
+    nl = 4  # ring of distinct layers (>= 1.7 GB of weights: no L2 reuse between steps)
+    layers = [synthetic_moe_layer(D, F, FS, E, TOPK, 4, sdt, dev, gen) for _ in range(nl)]
+    # random router weights give a skewed expert histogram (BASELINE config 2)
+    for L in layers:
+        L.per_expert_scale.copy_((1.0 + 0.3 * torch.randn(E, device=dev, generator=gen)).abs().to(torch.bfloat16))
+    xs = torch.randn(nl, T, D, device=dev, generator=gen).to(torch.float16)
+    idx = torch.empty(T, TOPK, dtype=torch.int32, device=dev)
+    wts = torch.empty(T, TOPK, dtype=torch.float16, device=dev)
+    act = torch.empty(T * TOPK, F, dtype=torch.float16, device=dev)
+    part = torch.empty(T * TOPK, D, dtype=torch.float16, device=dev)
+    h2 = torch.empty(T, D, dtype=torch.float16, device=dev)
+    acts = torch.empty(T, FS, dtype=torch.float16, device=dev)
+    ys = torch.empty(T, D, dtype=torch.float16, device=dev)
+    x_in = torch.empty(T, D, dtype=torch.float16, device=dev)
+    routes = route_sort(idx.zero_(), wts.zero_(), T, TOPK, E, 16, context=ctx)
+    router, grouped, shared = PrefillRouter(ctx), PrefillGroupedRoutedMoE(ctx), PrefillSharedExpert(ctx)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(L, x, s):
+        router.encode_gemma4_block(L.router_w, L.router_s, L.router_b, x, L.eff_scale, L.per_expert_scale, idx, wts,
+                                   T, E, D, TOPK, stream=s)
+        route_sort(idx, wts, T, TOPK, E, 16, stream=s, context=ctx, out=routes)
+        grouped.encode(L.experts, routes, x, act, part, T, TOPK, stream=s)
+        PrefillMoE.encode_reduce_token_major(part, wts, h2, T, TOPK, D, stream=s, context=ctx)
+        shared.encode(x, L.shared_gate, L.shared_up, L.shared_down, acts, ys, T, stream=s)
+
+    launches_per_step = 8  # router, sort, gather, 2 grouped QMM, reduce, 2 shared QMM
+    with torch.cuda.stream(stream):
+        step(layers[0], xs[0], stream)
+    torch.cuda.synchronize()
+    graphs = []
+    for r in range(nl + 1):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            step(layers[r % nl], xs[r] if r < nl else x_in, stream)
+        graphs.append(g)
+    torch.cuda.synchronize()
+    # distinct experts hit per layer (the weight bytes a step must read)
+    distinct = []
+    for r in range(nl):
+        graphs[r].replay()
+        torch.cuda.synchronize()
+        distinct.append(int(routes.n_groups.item()))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    with torch.cuda.stream(stream):
+        for i in range(a.warmup):
+            graphs[i % nl].replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for i in range(a.steps):
+            graphs[i % nl].replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / a.steps)
+    clk = clocks.stop()
+
+    # end to end: the chunk's activations H2D from pinned memory, both outputs D2H
+    h_in = torch.empty(nl, T, D, dtype=torch.float16, pin_memory=True)
+    h_in.copy_(xs.cpu())
+    h_h2 = torch.empty(T, D, dtype=torch.float16, pin_memory=True)
+    h_ys = torch.empty(T, D, dtype=torch.float16, pin_memory=True)
+    h_ids = torch.empty(T, TOPK, dtype=torch.int32, pin_memory=True)
+
+    def e2e_step(i):
+        x_in.copy_(h_in[i % nl], non_blocking=True)
+        graphs[nl].replay()
+        h_h2.copy_(h2, non_blocking=True)
+        h_ys.copy_(ys, non_blocking=True)
+        h_ids.copy_(idx, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for i in range(a.warmup):
+            e2e_step(i)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(a.steps):
+            e2e_step(i)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+    h2d = T * D * 2
+    d2h = 2 * T * D * 2 + T * TOPK * 4
+
+    # roofline of the dominant kernel: the grouped gate/up tcgen05 GEMM, timed alone
+    from edgeexpert_b200._lib import lib, ptr, stream_ptr
+    import ctypes as C
+    L0 = layers[0]
+    with torch.cuda.stream(stream):
+        graphs[0].replay()
+    torch.cuda.synchronize()
+    gg = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gg, stream=stream):
+        for _ in range(5):
+            grouped.encode(L0.experts, routes, xs[0], act, part, T, TOPK, stream=stream)
+    with torch.cuda.stream(stream):
+        gg.replay()
+    torch.cuda.synchronize()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        g0.record(stream)
+        gg.replay()
+        g1.record(stream)
+    torch.cuda.synchronize()
+    grouped_us = g0.elapsed_time(g1) * 1e3 / 5
+    grouped_flops = 2.0 * T * TOPK * 3 * F * D
+    ctx.check_device(stream)
+
+    peaks = {}
+    pk_path = ROOT / "MEASURED_PEAKS.json"
+    if pk_path.exists():
+        peaks = json.loads(pk_path.read_text())
+    if a.workload == "prefill":
+        peak, peak_src, unit_r = (peaks.get("bf16_tflops", 1590.0), "measured" if "bf16_tflops" in peaks else
+                                  "fallback", "TFLOP/s")
+        achieved = grouped_flops / (grouped_us * 1e-6) / 1e12
+        bound = "tensor"
+    else:
+        peak, peak_src, unit_r = (peaks.get("hbm_gbs", 6650.0), "measured" if "hbm_gbs" in peaks else "fallback",
+                                  "GB/s")
+        achieved = (chunk_bytes(distinct[0]) - chunk_bytes(0)) / (grouped_us * 1e-6) / 1e9
+        bound = "hbm"
+
+    flops = chunk_flops(T)
+    bytes_step = sum(chunk_bytes(d) for d in distinct) / nl
+    if a.workload == "prefill":
+        metric, unit = "MoE prefill TFLOP/s (config 3)", "TFLOP/s"
+        value = world * flops / (ms * 1e-3) / 1e12
+        e2e_value = world * flops / (ms_e2e * 1e-3) / 1e12
+    else:
+        metric, unit = "MoE batched-decode weight GB/s (config 2)", "GB/s"
+        value = world * bytes_step / (ms * 1e-3) / 1e9
+        e2e_value = world * bytes_step / (ms_e2e * 1e-3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        lps, threads, sample = cpu_sample(a.cpu_seconds)
+        cpu_ms = T * 1e3 / lps
+        cpu_v = flops / (cpu_ms * 1e-3) / 1e12 if a.workload == "prefill" else bytes_step / (cpu_ms * 1e-3) / 1e9
+        cpu = {"value": cpu_v, "unit": unit, "cores": threads, "kind": "port",
+               "sample": sample + f"; scaled to a {T}-token chunk"}
+
+    if rank == 0:
+        line = {
+            "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16-act/int4-w/fp32-acc", "data": "synthetic (BASELINE distributions, random-init weights)",
+            "config": {"workload": f"config{3 if a.workload == 'prefill' else 2}: {T}-token chunk through the "
+                                   "config-1 MoE layer (router, device grouping, grouped routed experts, "
+                                   "token-major reduce, shared expert)",
+                       "tokens": T, "d": D, "f": F, "fs": FS, "experts": E, "top_k": TOPK, "layer_ring": nl,
+                       "distinct_experts": distinct, "scale_dtype": a.scale_dtype,
+                       "l2": "ring of 4 layers (%.1f GB) exceeds L2; no flush needed" %
+                             (nl * chunk_bytes(E) / 1e9),
+                       "outputs": "routed h2 and shared y kept separate (the reference combines them in its norm "
+                                  "kernel, outside this path)"},
+            "tok_s": world * T * 1e3 / ms, "tok_s_e2e": world * T * 1e3 / ms_e2e,
+            "flops_per_step": flops, "weight_bytes_per_step": bytes_step,
+            "e2e": {"value": e2e_value, "unit": unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "roofline": {"bound": bound, "kernel": "qmm_kernel (grouped gate/up + down, incl. row gather)",
+                         "achieved": achieved, "peak": peak, "peak_source": f"{peak_src}", "unit": unit_r,
+                         "frac": achieved / peak, "traffic": None, "us_per_launch": grouped_us,
+                         "work_per_launch": grouped_flops if bound == "tensor" else
+                         chunk_bytes(distinct[0]) - chunk_bytes(0)},
+            "cpu_baseline": cpu,
+            "clocks": clk,
+            "gpu_launches": launches_per_step * a.steps,
+        }
+        print(json.dumps(line), flush=True)
+
+
 def main():
     a = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -368,7 +619,10 @@ def main():
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
-    run_ours(a, rank, world, local_rank)
+    if a.workload == "decode":
+        run_ours(a, rank, world, local_rank)
+    else:
+        run_chunk(a, rank, world, local_rank)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

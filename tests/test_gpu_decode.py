@@ -289,10 +289,13 @@ def test_shared_expert(cuda, bits, D, Fs):
     assert O.rel_error(O.f16_to_f32(f16(y)), y32_ref) < FP16_TOL
 
 
-def test_moe_decode_layer_config1(cuda):
+@pytest.mark.parametrize("fused", [False, True])
+def test_moe_decode_layer_config1(cuda, fused, monkeypatch):
     """BASELINE config 1 at full shape: router int8 128x2816 -> top-8 -> routed
     gate/up/down (F=704) + shared int4 (Fs=2112).  Routing bit-exact (or a
-    near tie), output within 2e-3 of the oracle layer."""
+    near tie), output within 2e-3 of the oracle layer.  Both the default
+    three-launch path and the single cooperative launch (TFCUDA_FUSED=1)."""
+    monkeypatch.setenv("TFCUDA_FUSED", "1" if fused else "0")
     from edgeexpert_b200.moe import (ExpertPool, MoELayerWeights, SharedExpertProjection, moe_decode_layer)
     E, D, F, Fs = 128, 2816, 704, 2112
     ex = Experts(E, D, F, 0, "layer-cfg1")
