@@ -24,7 +24,11 @@ struct tf_context {
     __half* d_w = nullptr;             // [8] decode routing weights
     __half* d_acts = nullptr;          // [8][kMaxF] routed activations
     __half* d_shared_act = nullptr;    // [kMaxFs] shared-expert activation
+    uint32_t* d_sort_cnt = nullptr;    // [kRouteSortChunks][256] per-chunk expert counts / bases
 };
+
+// Device grouping: pairs are split into at most this many chunks (one CTA each).
+constexpr int kRouteSortChunks = 1024;
 
 namespace tf {
 

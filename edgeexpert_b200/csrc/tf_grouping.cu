@@ -23,36 +23,40 @@ namespace {
 constexpr int kSortThreads = 1024;
 constexpr int kSortMaxExperts = 256;
 
-// One CTA.  Token-major input (pair index p = token * K + rank) is already in
-// (token, rank) order, so a stable counting scatter by expert reproduces the
-// reference's (expert, token, rank) order exactly.
-__global__ void __launch_bounds__(kSortThreads) route_sort_kernel(
-    const uint32_t* __restrict__ ids, const __half* __restrict__ w, int T, int K, int E, int tile_e,
-    const unsigned long long* __restrict__ sort_keys, tf_token_expert_pair* sorted, uint32_t* offsets,
-    uint32_t* counts, tf_moe_group* groups, uint32_t* n_groups, tf_moe_tile* tiles, uint32_t* n_tiles,
-    uint32_t* err) {
-    __shared__ uint32_t cnt[kSortMaxExperts];
-    __shared__ uint32_t order[kSortMaxExperts];   // sorted position -> expert
-    __shared__ uint32_t start[kSortMaxExperts];   // expert -> first sorted pair
-    __shared__ uint32_t run[kSortMaxExperts];     // expert -> pairs placed so far
-    __shared__ uint32_t wcnt[kSortThreads / 32][kSortMaxExperts];
-    __shared__ uint32_t gidx[kSortMaxExperts];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int n = T * K;
-    for (int e = tid; e < E; e += blockDim.x) {
-        cnt[e] = 0;
-        run[e] = 0;
-    }
+// Pass 1, one CTA per chunk of the token-major pair list (pair p = token*K + rank):
+// per-chunk expert histogram -> cnt[chunk][expert].
+__global__ void __launch_bounds__(kSortThreads) route_count_kernel(const uint32_t* __restrict__ ids, int n,
+                                                                   int chunk, int E, uint32_t* cnt, uint32_t* err) {
+    __shared__ uint32_t c[kSortMaxExperts];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) c[e] = 0;
     __syncthreads();
-    for (int p = tid; p < n; p += blockDim.x) {
+    const int p0 = blockIdx.x * chunk, p1 = min(n, p0 + chunk);
+    for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
         const uint32_t e = ids[p];
         if (e < (uint32_t)E)
-            atomicAdd(&cnt[e], 1u);
+            atomicAdd(&c[e], 1u);
         else
             atomicOr(err, kErrBadExpert);
     }
-    // expert order: by (key, id) when keys are given, else by id
-    for (int e = tid; e < E; e += blockDim.x) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[blockIdx.x * kSortMaxExperts + e] = c[e];
+}
+
+// Pass 2, one CTA: expert order (by sort key, then id), per-expert offsets and
+// counts, groups, tiles, and each chunk's first destination per expert
+// (cnt[chunk][e] is replaced by that base).
+__global__ void __launch_bounds__(kSortMaxExperts) route_plan_kernel(
+    uint32_t* cnt, int nb, int E, int tile_e, const unsigned long long* __restrict__ sort_keys, uint32_t* offsets,
+    uint32_t* counts, tf_moe_group* groups, uint32_t* n_groups, tf_moe_tile* tiles, uint32_t* n_tiles) {
+    __shared__ uint32_t tot[kSortMaxExperts];
+    __shared__ uint32_t order[kSortMaxExperts];
+    __shared__ uint32_t start[kSortMaxExperts];
+    __shared__ uint32_t gidx[kSortMaxExperts];
+    const int e = threadIdx.x;
+    if (e < E) {
+        uint32_t t = 0;
+        for (int b = 0; b < nb; ++b) t += cnt[b * kSortMaxExperts + e];
+        tot[e] = t;
         int pos = e;
         if (sort_keys) {
             const unsigned long long k = sort_keys[e];
@@ -65,40 +69,61 @@ __global__ void __launch_bounds__(kSortThreads) route_sort_kernel(
         order[pos] = (uint32_t)e;
     }
     __syncthreads();
-    if (tid == 0) {
+    if (e == 0) {
         uint32_t acc = 0, ng = 0;
         for (int i = 0; i < E; ++i) {
-            const uint32_t e = order[i];
-            start[e] = acc;
-            offsets[e] = cnt[e] ? acc : 0xFFFFFFFFu;
-            counts[e] = cnt[e];
-            if (cnt[e]) {
-                groups[ng] = tf_moe_group{e, acc, cnt[e]};
-                gidx[ng] = e;
+            const uint32_t x = order[i];
+            start[x] = acc;
+            offsets[x] = tot[x] ? acc : 0xFFFFFFFFu;
+            counts[x] = tot[x];
+            if (tot[x]) {
+                groups[ng] = tf_moe_group{x, acc, tot[x]};
+                gidx[ng] = x;
                 ++ng;
             }
-            acc += cnt[e];
+            acc += tot[x];
         }
         uint32_t nt = 0;
         for (uint32_t g0 = 0; g0 < ng; g0 += (uint32_t)tile_e) {
             const uint32_t g1 = min(ng, g0 + (uint32_t)tile_e);
             const uint32_t ps = start[gidx[g0]];
-            const uint32_t pe = start[gidx[g1 - 1]] + cnt[gidx[g1 - 1]];
+            const uint32_t pe = start[gidx[g1 - 1]] + tot[gidx[g1 - 1]];
             tiles[nt++] = tf_moe_tile{g0, g1 - g0, ps, pe - ps};
         }
         *n_groups = ng;
         *n_tiles = nt;
     }
     __syncthreads();
-    // stable scatter, 1024 pairs per round
-    for (int base = 0; base < n; base += blockDim.x) {
-        const int p = base + tid;
-        const bool valid = p < n;
+    if (e < E) {
+        uint32_t run = start[e];
+        for (int b = 0; b < nb; ++b) {
+            const uint32_t v = cnt[b * kSortMaxExperts + e];
+            cnt[b * kSortMaxExperts + e] = run;
+            run += v;
+        }
+    }
+}
+
+// Pass 3, one CTA per chunk: stable scatter.  Within a 1024-pair round the
+// rank of a pair among equal experts is (earlier warps' count + lanes below
+// it in its own warp), so the (expert, token, rank) order of the reference
+// is reproduced exactly.
+__global__ void __launch_bounds__(kSortThreads) route_scatter_kernel(
+    const uint32_t* __restrict__ ids, const __half* __restrict__ w, int n, int K, int chunk, int E,
+    const uint32_t* __restrict__ base, tf_token_expert_pair* sorted) {
+    __shared__ uint32_t run[kSortMaxExperts];
+    __shared__ uint32_t wcnt[kSortThreads / 32][kSortMaxExperts];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int e = tid; e < E; e += blockDim.x) run[e] = base[blockIdx.x * kSortMaxExperts + e];
+    __syncthreads();
+    const int p0 = blockIdx.x * chunk, p1 = min(n, p0 + chunk);
+    for (int r0 = p0; r0 < p1; r0 += blockDim.x) {
+        const int p = r0 + tid;
+        const bool valid = p < p1;
         const uint32_t e = valid ? ids[p] : 0xFFFFFFFFu;
         const bool ok = valid && e < (uint32_t)E;
         const unsigned int same = __match_any_sync(0xffffffffu, ok ? e : 0xFFFFFFFFu);
         const uint32_t intra = __popc(same & ((1u << lane) - 1u));
-        // per-warp counts of this round
         for (int i = lane; i < E; i += 32) wcnt[warp][i] = 0;
         __syncwarp();
         if (ok && intra == 0) wcnt[warp][e] = __popc(same);
@@ -106,13 +131,12 @@ __global__ void __launch_bounds__(kSortThreads) route_sort_kernel(
         if (ok) {
             uint32_t before = 0;
             for (int w2 = 0; w2 < warp; ++w2) before += wcnt[w2][e];
-            const uint32_t dst = start[e] + run[e] + before + intra;
             tf_token_expert_pair pr;
             pr.token = (uint32_t)(p / K);
             pr.expert = e;
             pr.rank = (uint32_t)(p % K);
             pr.weight_bits = (uint32_t)__half_as_ushort(w[p]);
-            sorted[dst] = pr;
+            sorted[run[e] + before + intra] = pr;
         }
         __syncthreads();
         for (int i = tid; i < E; i += blockDim.x) {
@@ -207,12 +231,24 @@ tf_status tf_moe_route_sort(tf_context* ctx, const void* expert_ids, const void*
     if ((T && (!expert_ids || !weights || !sorted_pairs)) || !offsets || !counts || !groups || !n_groups || !tiles ||
         !n_tiles)
         return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
-    route_sort_kernel<<<1, kSortThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const uint32_t*>(expert_ids), static_cast<const __half*>(weights), (int)T, (int)K, (int)E,
-        (int)tile_expert_count, static_cast<const unsigned long long*>(sort_keys),
-        static_cast<tf_token_expert_pair*>(sorted_pairs), static_cast<uint32_t*>(offsets),
-        static_cast<uint32_t*>(counts), static_cast<tf_moe_group*>(groups), static_cast<uint32_t*>(n_groups),
-        static_cast<tf_moe_tile*>(tiles), static_cast<uint32_t*>(n_tiles), ctx->d_err);
+    cudaStream_t cs = static_cast<cudaStream_t>(stream);
+    const int n = (int)(T * K);
+    int nb = 0, chunk = kSortThreads;
+    if (n > 0) {
+        nb = std::min(kRouteSortChunks, (n + kSortThreads - 1) / kSortThreads);
+        chunk = ((n + nb - 1) / nb + kSortThreads - 1) / kSortThreads * kSortThreads;
+        nb = (n + chunk - 1) / chunk;
+        route_count_kernel<<<nb, kSortThreads, 0, cs>>>(static_cast<const uint32_t*>(expert_ids), n, chunk, (int)E,
+                                                         ctx->d_sort_cnt, ctx->d_err);
+    }
+    route_plan_kernel<<<1, kSortMaxExperts, 0, cs>>>(
+        ctx->d_sort_cnt, nb, (int)E, (int)tile_expert_count, static_cast<const unsigned long long*>(sort_keys),
+        static_cast<uint32_t*>(offsets), static_cast<uint32_t*>(counts), static_cast<tf_moe_group*>(groups),
+        static_cast<uint32_t*>(n_groups), static_cast<tf_moe_tile*>(tiles), static_cast<uint32_t*>(n_tiles));
+    if (n > 0)
+        route_scatter_kernel<<<nb, kSortThreads, 0, cs>>>(
+            static_cast<const uint32_t*>(expert_ids), static_cast<const __half*>(weights), n, (int)K, chunk, (int)E,
+            ctx->d_sort_cnt, static_cast<tf_token_expert_pair*>(sorted_pairs));
     return cuda_check(ctx, cudaGetLastError(), name);
 }
 

@@ -2,10 +2,11 @@
 // (prefill_router_gemma4_block, Sources/TurboFieldfare/Metal/Prefill/prefill.metal:478-573;
 //  PrefillRouter.encodeGemma4Block, Kernels/Prefill/MoE/PrefillRouter.swift:37-89).
 //
-// One CTA serves 4 tokens.  x~ = float(half h) * float(bf16 es) is staged per
-// token as two fp16 terms (hi, lo), giving 8 MMA columns (token t -> columns
-// 2t, 2t+1).  Each warp takes 16-expert tiles and streams the int8 router
-// rows from L2 straight into MMA fragments (codes exact in fp16), folding the
+// One CTA serves 8 tokens.  x~ = float(half h) * float(bf16 es) is staged per
+// token as two fp16 terms (hi, lo), giving 16 MMA columns (token t -> columns
+// 2t, 2t+1) in two 8-column groups.  Each warp takes 16-expert tiles and
+// streams the int8 router rows from L2 straight into MMA fragments (codes
+// exact in fp16), reusing each fragment for both column groups, and folds the
 // per-group scale/bias in fp32.  Then every token selects its top-k by rank
 // (logit desc, id asc -- the reference's insertion order), softmax over the
 // k, times the per-expert gain.
@@ -15,10 +16,12 @@ using namespace tf;
 
 namespace {
 
-constexpr int kRtTok = 4;          // tokens per CTA
+constexpr int kRtTok = 8;          // tokens per CTA
+constexpr int kRtCG = kRtTok / 4;  // 8-column MMA groups
 constexpr int kRtThreads = 256;
 constexpr int kRtMaxE = 256;
 constexpr int kRtMaxK = 64;
+constexpr int kRtSmemMax = 200 * 1024;  // d = 2816 needs ~104 KB: two CTAs per SM
 
 template <typename ST>
 __global__ void __launch_bounds__(kRtThreads) prefill_router_kernel(
@@ -28,11 +31,11 @@ __global__ void __launch_bounds__(kRtThreads) prefill_router_kernel(
     extern __shared__ __align__(16) uint8_t smem[];
     const int ws = x_words_stride(D);
     const int ng = D / kGroup;
-    uint32_t* xs = reinterpret_cast<uint32_t*>(smem);                         // [8][ws]
-    float* xsum = reinterpret_cast<float*>(xs + 2 * kRtTok * ws);               // [4][ng]
-    float* logits = xsum + kRtTok * ng;                                         // [4][256]
-    float* sel = logits + kRtTok * kRtMaxE;                                     // [4][64] selected logits
-    uint32_t* selid = reinterpret_cast<uint32_t*>(sel + kRtTok * kRtMaxK);      // [4][64]
+    uint32_t* xs = reinterpret_cast<uint32_t*>(smem);                         // [2*kRtTok][ws]
+    float* xsum = reinterpret_cast<float*>(xs + 2 * kRtTok * ws);               // [kRtTok][ng]
+    float* logits = xsum + kRtTok * ng;                                         // [kRtTok][256]
+    float* sel = logits + kRtTok * kRtMaxE;                                     // [kRtTok][64] selected logits
+    uint32_t* selid = reinterpret_cast<uint32_t*>(sel + kRtTok * kRtMaxK);      // [kRtTok][64]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t0 = blockIdx.x * kRtTok;
     const int ntok = min(kRtTok, T - t0);
@@ -75,36 +78,44 @@ __global__ void __launch_bounds__(kRtThreads) prefill_router_kernel(
         const bool va = rA < E, vb = rB < E;
         const uint8_t* wA = W + (size_t)(va ? rA : 0) * D;
         const uint8_t* wB = W + (size_t)(vb ? rB : 0) * D;
-        float accA = 0.f, accB = 0.f;  // (row g, token t), (row g+8, token t)
+        float accA[kRtCG], accB[kRtCG];  // (row g, token 4c+t), (row g+8, token 4c+t)
+#pragma unroll
+        for (int c = 0; c < kRtCG; ++c) accA[c] = accB[c] = 0.f;
         for (int G = 0; G < ng; ++G) {
             const uint4 qa = __ldg(reinterpret_cast<const uint4*>(wA + G * 64 + t * 16));
             const uint4 qb = __ldg(reinterpret_cast<const uint4*>(wB + G * 64 + t * 16));
-            // B fragment: column g = token g/2, part g%2
-            const uint4* xp = reinterpret_cast<const uint4*>(xs + g * ws + (G * 8 + 2 * t) * 4);
-            const uint4 x0 = xp[0], x1 = xp[1];
             uint32_t pa0[4], pa1[4], pb0[4], pb1[4];
             dq8(qa.x, qa.y, pa0);
             dq8(qa.z, qa.w, pa1);
             dq8(qb.x, qb.y, pb0);
             dq8(qb.z, qb.w, pb1);
-            float c[4] = {0.f, 0.f, 0.f, 0.f}, cb[4] = {0.f, 0.f, 0.f, 0.f};
-            mma16816(c, pa0[0], pb0[0], pa0[1], pb0[1], x0.x, x0.y);
-            mma16816(cb, pa0[2], pb0[2], pa0[3], pb0[3], x0.z, x0.w);
-            mma16816(c, pa1[0], pb1[0], pa1[1], pb1[1], x1.x, x1.y);
-            mma16816(cb, pa1[2], pb1[2], pa1[3], pb1[3], x1.z, x1.w);
             const float sa = va ? scale_to_float(S[(size_t)rA * ng + G]) : 0.f;
             const float ba = va ? scale_to_float(B[(size_t)rA * ng + G]) : 0.f;
             const float sb = vb ? scale_to_float(S[(size_t)rB * ng + G]) : 0.f;
             const float bb = vb ? scale_to_float(B[(size_t)rB * ng + G]) : 0.f;
-            const float xsm = xsum[t * ng + G];
-            // columns 2t (hi) and 2t+1 (lo) of this lane are token t
-            accA = fmaf(sa, (c[0] + cb[0]) + (c[1] + cb[1]), accA);
-            accA = fmaf(ba, xsm, accA);
-            accB = fmaf(sb, (c[2] + cb[2]) + (c[3] + cb[3]), accB);
-            accB = fmaf(bb, xsm, accB);
+#pragma unroll
+            for (int cg = 0; cg < kRtCG; ++cg) {
+                // B fragment: column g of group cg = token 4cg + g/2, part g%2
+                const uint4* xp = reinterpret_cast<const uint4*>(xs + (cg * 8 + g) * ws + (G * 8 + 2 * t) * 4);
+                const uint4 x0 = xp[0], x1 = xp[1];
+                float c[4] = {0.f, 0.f, 0.f, 0.f}, cb[4] = {0.f, 0.f, 0.f, 0.f};
+                mma16816(c, pa0[0], pb0[0], pa0[1], pb0[1], x0.x, x0.y);
+                mma16816(cb, pa0[2], pb0[2], pa0[3], pb0[3], x0.z, x0.w);
+                mma16816(c, pa1[0], pb1[0], pa1[1], pb1[1], x1.x, x1.y);
+                mma16816(cb, pa1[2], pb1[2], pa1[3], pb1[3], x1.z, x1.w);
+                const float xsm = xsum[(4 * cg + t) * ng + G];
+                // columns 2t (hi) and 2t+1 (lo) of this lane are token 4cg + t
+                accA[cg] = fmaf(sa, (c[0] + cb[0]) + (c[1] + cb[1]), accA[cg]);
+                accA[cg] = fmaf(ba, xsm, accA[cg]);
+                accB[cg] = fmaf(sb, (c[2] + cb[2]) + (c[3] + cb[3]), accB[cg]);
+                accB[cg] = fmaf(bb, xsm, accB[cg]);
+            }
         }
-        if (va) logits[t * kRtMaxE + rA] = accA;
-        if (vb) logits[t * kRtMaxE + rB] = accB;
+#pragma unroll
+        for (int cg = 0; cg < kRtCG; ++cg) {
+            if (va) logits[(4 * cg + t) * kRtMaxE + rA] = accA[cg];
+            if (vb) logits[(4 * cg + t) * kRtMaxE + rB] = accB[cg];
+        }
     }
     __syncthreads();
 
@@ -165,11 +176,11 @@ tf_status tf_router_topk_batched(tf_context* ctx, const void* W, const void* S, 
     auto run = [&](auto* kernel) -> tf_status {
         static bool configured[64] = {};
         if (!configured[ctx->device & 63]) {
-            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem < 65536 ? 65536 : (int)smem);
+            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRtSmemMax);
             if (e != cudaSuccess) return cuda_check(ctx, e, name);
             configured[ctx->device & 63] = true;
         }
-        if (smem > 65536) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: d too large", name);
+        if (smem > (size_t)kRtSmemMax) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: d too large", name);
         return TF_OK;
     };
     tf_status s;
