@@ -43,20 +43,31 @@ constexpr int kLoadWarp = 4;
 constexpr int kAWarps = 8;
 constexpr int kAWarp0 = 5;
 constexpr int kMmaWarp = kAWarp0 + kAWarps;  // 13
-constexpr int kQWarps = kMmaWarp + 1;
+constexpr int kScaleWarp = kMmaWarp + 1;       // 14, 15
+constexpr int kScaleWarps = 2;
+constexpr int kQWarps = kScaleWarp + kScaleWarps;
 constexpr int kQThreads = kQWarps * 32;
-constexpr int kStages = 4;
-constexpr int kRing = 8;               // scale/bias prefetch depth (k-blocks)
-constexpr int kTM = 128;               // weight rows per tile (MMA M)
+constexpr int kTM = 128;               // weight rows per CTA (MMA M per CTA)
 constexpr int kTN = 256;               // tokens per tile (MMA N, max)
 constexpr int kAStage = kTM * 128;     // 16 KB fp16 operand
-constexpr int kBStage = kTN * 128;     // 32 KB fp16 operand
 constexpr int kRawStage = kTM * 32;    // 4 KB packed int4
 constexpr int kBBoxRows = 64;          // rows per activation TMA box (8 KB)
 constexpr int kAccCols = 256;
 constexpr int kTmemCols = 512;
 constexpr int kMaxGroups = 256;
 constexpr uint32_t kQSpin = 1u << 24;
+
+// CG = CTAs per MMA (1: one SM, 128 x N tiles; 2: a CTA pair, 256 x N tiles,
+// each CTA holding half of the weight rows and half of the token rows).
+template <int CG>
+struct QCfg {
+    static constexpr int kStages = CG == 2 ? 9 : 5;  // load ring: raw weights + token rows + scales
+    static constexpr int kAStages = 2;               // dequantised operand ring
+    static constexpr int kBRows = kTN / CG;          // token rows staged per CTA
+    static constexpr int kBStage = kBRows * 128;
+    static constexpr int kSStage = kTM * 4;          // fp16 scale | bias per weight row
+    static constexpr int kScaleAhead = 8;            // scale loads in flight (k-blocks)
+};
 
 enum QMode : int { kDensePlain = 0, kDenseGateUp = 1, kGroupedGateUp = 2, kGroupedDown = 3 };
 
@@ -84,12 +95,19 @@ struct QmmParams {
     uint32_t* err;
 };
 
+template <int CG>
 struct QShared {
-    uint64_t ldfull[kStages];  // TMA bytes (raw weights + activations) landed
-    uint64_t full[kStages];    // dequantised operand written
-    uint64_t empty[kStages];   // MMAs of the stage retired
+    static constexpr int S = QCfg<CG>::kStages;
+    static constexpr int SA = QCfg<CG>::kAStages;
+    uint64_t rawfull[S];  // this CTA's raw weight bytes landed
+    uint64_t bfull[S];    // (leader) activation bytes of the pair landed
+    uint64_t empty[S];    // MMAs reading the stage's token rows retired (both CTAs)
+    uint64_t sfull[S];    // scales of the stage written
+    uint64_t sempty[S];   // scales of the stage read by every dequantiser warp
+    uint64_t afull[SA];   // (leader) dequantised operand of the pair written
+    uint64_t aempty[SA];  // MMAs reading the operand retired (both CTAs)
     uint64_t tfull[2];
-    uint64_t tempty[2];
+    uint64_t tempty[2];   // (leader) epilogues of the pair released the accumulator
     uint64_t done;
     uint32_t tmem_base;
     int abort_flag;
@@ -101,8 +119,13 @@ struct QShared {
     int gexpert[kMaxGroups];
 };
 
-constexpr size_t kQSmemBytes = 1024 + (size_t)kStages * (kAStage + kBStage + kRawStage) + sizeof(QShared);
-static_assert(kQSmemBytes <= 232448, "shared memory");
+template <int CG>
+constexpr size_t qsmem_bytes() {
+    using C = QCfg<CG>;
+    return 1024 + (size_t)C::kAStages * kAStage +
+           (size_t)C::kStages * (C::kBStage + kRawStage + C::kSStage) + sizeof(QShared<CG>);
+}
+static_assert(qsmem_bytes<1>() <= 232448 && qsmem_bytes<2>() <= 232448, "shared memory");
 
 struct QTile {
     int feat0;
@@ -113,11 +136,13 @@ struct QTile {
 
 __device__ __forceinline__ bool gate_up(int mode) { return mode == kDenseGateUp || mode == kGroupedGateUp; }
 __device__ __forceinline__ bool grouped(int mode) { return mode == kGroupedGateUp || mode == kGroupedDown; }
-__device__ __forceinline__ int feat_per_tile(int mode) { return gate_up(mode) ? kTM / 2 : kTM; }
+// output features covered by one tile
+__device__ __forceinline__ int feat_per_tile(int mode, int cg) { return (gate_up(mode) ? kTM / 2 : kTM) * cg; }
 
-__device__ __forceinline__ bool decode_tile(const QmmParams& p, const QShared& sh, int idx, QTile& t) {
+template <int CG>
+__device__ __forceinline__ bool decode_tile(const QmmParams& p, const QShared<CG>& sh, int idx, QTile& t) {
     if (idx >= sh.total) return false;
-    const int fpt = feat_per_tile(p.mode);
+    const int fpt = feat_per_tile(p.mode, CG);
     const int nft = (p.nfeat + fpt - 1) / fpt;
     if (!grouped(p.mode)) {
         const int tt = idx / nft, ft = idx - tt * nft;
@@ -144,8 +169,9 @@ __device__ __forceinline__ bool decode_tile(const QmmParams& p, const QShared& s
     return true;
 }
 
-// Bounded wait that gives up early once another role has given up.
-__device__ __forceinline__ bool qwait(uint64_t* bar, uint32_t parity, QShared& sh, uint32_t* err) {
+// Bounded wait that gives up early once another role of this CTA has given up.
+template <int CG>
+__device__ __forceinline__ bool qwait(uint64_t* bar, uint32_t parity, QShared<CG>& sh, uint32_t* err) {
     for (uint32_t i = 0; i < kQSpin; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 255u) == 255u && *reinterpret_cast<volatile int*>(&sh.abort_flag)) return false;
@@ -153,6 +179,15 @@ __device__ __forceinline__ bool qwait(uint64_t* bar, uint32_t parity, QShared& s
     sh.abort_flag = 1;
     if (err) atomicOr(err, kErrMbarTimeout);
     return false;
+}
+
+// arrive on the pair leader's copy of `bar` (this CTA's own when CG == 1)
+template <int CG>
+__device__ __forceinline__ void arrive_leader(uint64_t* bar) {
+    if constexpr (CG == 1)
+        mbar_arrive(bar);
+    else
+        mbar_arrive_cluster(mapa_shared(bar, 0));
 }
 
 __device__ __forceinline__ uint32_t sw128(int row, int chunk) {
@@ -206,76 +241,85 @@ __device__ __forceinline__ void dq8_natural(uint32_t w, uint32_t s2, uint32_t b2
     o[3] = hfma2_u(hsub2_u(__byte_perm(hi, m, 0x4342), k1024), s2, b2);
 }
 
-// Iteration cursor over (tile, k-block) of this CTA.
+// Iteration cursor over (tile, k-block) of this CTA (pair).
 struct QCursor {
     int idx, kb;
     bool valid;
     QTile t;
 };
 
-__device__ __forceinline__ void cursor_start(const QmmParams& p, const QShared& sh, QCursor& c) {
-    c.idx = blockIdx.x;
+template <int CG>
+__device__ __forceinline__ void cursor_start(const QmmParams& p, const QShared<CG>& sh, QCursor& c) {
+    c.idx = blockIdx.x / CG;
     c.kb = 0;
-    c.valid = decode_tile(p, sh, c.idx, c.t);
+    c.valid = decode_tile<CG>(p, sh, c.idx, c.t);
 }
 
-__device__ __forceinline__ void cursor_next(const QmmParams& p, const QShared& sh, QCursor& c, int nkb) {
+template <int CG>
+__device__ __forceinline__ void cursor_next(const QmmParams& p, const QShared<CG>& sh, QCursor& c, int nkb) {
     if (!c.valid) return;
     if (++c.kb == nkb) {
         c.kb = 0;
-        c.idx += gridDim.x;
-        c.valid = decode_tile(p, sh, c.idx, c.t);
+        c.idx += gridDim.x / CG;
+        c.valid = decode_tile<CG>(p, sh, c.idx, c.t);
     }
 }
 
-struct SLoad {
-    uint32_t sb;  // fp16 scale (low) | fp16 bias (high); 0 = row absent
-};
-
-// scale and bias of this thread's row for the cursor's k-block
-template <typename ST>
-__device__ __forceinline__ SLoad s_load(const QmmParams& p, const QCursor& c, int r) {
-    SLoad a;
-    a.sb = 0;
-    if (!c.valid) return a;
-    const bool gu = gate_up(p.mode);
-    const int mat = gu ? (r & 1) : 0;
-    const int f = c.t.feat0 + (gu ? (r >> 1) : r);
-    if (f >= p.nfeat) return a;
-    // dense: os/ob are addresses; grouped: byte offsets inside the expert's blob
-    const uint64_t base = grouped(p.mode) ? reinterpret_cast<uint64_t>(p.sbase) + (uint64_t)c.t.expert * p.stride : 0;
-    const ST* S = reinterpret_cast<const ST*>(base + (mat ? p.os1 : p.os0));
-    const ST* B = reinterpret_cast<const ST*>(base + (mat ? p.ob1 : p.ob0));
-    const size_t i = (size_t)f * (p.K >> 6) + c.kb;
-    const uint32_t s = scale_bits_f16<ST>(S + i), b = scale_bits_f16<ST>(B + i);
-    a.sb = s | (b << 16);
-    // a present row whose scale and bias are both +0 still dequantises to 0
-    return a;
+// first output feature of this CTA's 128 weight rows
+template <int CG>
+__device__ __forceinline__ int cta_feat0(const QmmParams& p, const QTile& t, int rank) {
+    return t.feat0 + rank * (gate_up(p.mode) ? kTM / 2 : kTM);
 }
 
-template <typename ST>
+// Scale and bias rows of weight row r (0..127 of this CTA) in the cursor's
+// tile; null when the row is past the matrix (it then dequantises to 0).
+template <typename ST, int CG>
+__device__ __forceinline__ const ST* scale_row(const QmmParams& p, const QTile& t, int r, int rank, bool bias) {
+    const bool gu = gate_up(p.mode);
+    const int mat = gu ? (r & 1) : 0;
+    const int f = cta_feat0<CG>(p, t, rank) + (gu ? (r >> 1) : r);
+    if (f >= p.nfeat) return nullptr;
+    // dense: os/ob are addresses; grouped: byte offsets inside the expert's blob
+    const uint64_t base = grouped(p.mode) ? reinterpret_cast<uint64_t>(p.sbase) + (uint64_t)t.expert * p.stride : 0;
+    const uint64_t off = bias ? (mat ? p.ob1 : p.ob0) : (mat ? p.os1 : p.os0);
+    return reinterpret_cast<const ST*>(base + off) + (size_t)f * (p.K >> 6);
+}
+
+template <typename ST, int CG>
 __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant__ QmmParams p) {
+    using Cfg = QCfg<CG>;
+    constexpr int S = Cfg::kStages;
+    constexpr int SA = Cfg::kAStages;
     extern __shared__ uint8_t q_smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(q_smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* As = smem;
-    uint8_t* Bs = As + kStages * kAStage;
-    uint8_t* Ws = Bs + kStages * kBStage;
-    QShared& sh = *reinterpret_cast<QShared*>(Ws + kStages * kRawStage);
+    uint8_t* Bs = As + SA * kAStage;
+    uint8_t* Ws = Bs + S * Cfg::kBStage;
+    uint32_t* Ss = reinterpret_cast<uint32_t*>(Ws + S * kRawStage);
+    QShared<CG>& sh = *reinterpret_cast<QShared<CG>*>(reinterpret_cast<uint8_t*>(Ss) + S * Cfg::kSStage);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rank = CG == 2 ? (int)cluster_ctarank() : 0;
+    const bool leader = rank == 0;
     const int nkb = p.K >> 6;
-    const int fpt = feat_per_tile(p.mode);
+    const int fpt = feat_per_tile(p.mode, CG);
     const int nft = (p.nfeat + fpt - 1) / fpt;
 
     // ---- setup: barriers, tile table, TMEM ----
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&sh.ldfull[s], 1);
-            mbar_init(&sh.full[s], kAWarps);
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&sh.rawfull[s], 1);
+            mbar_init(&sh.bfull[s], CG);
             mbar_init(&sh.empty[s], 1);
+            mbar_init(&sh.sfull[s], kScaleWarps);
+            mbar_init(&sh.sempty[s], kAWarps);
+        }
+        for (int a = 0; a < SA; ++a) {
+            mbar_init(&sh.afull[a], kAWarps * CG);
+            mbar_init(&sh.aempty[a], 1);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&sh.tfull[a], 1);
-            mbar_init(&sh.tempty[a], kEpiWarps);
+            mbar_init(&sh.tempty[a], kEpiWarps * CG);
         }
         mbar_init(&sh.done, 1);
         sh.abort_flag = 0;
@@ -302,7 +346,7 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
                 sh.gexpert[g] = (int)gr.expert;
                 if (gr.expert < p.num_experts) {
                     tiles = (((int)gr.pair_count + kTN - 1) / kTN) * nft;
-                } else if (p.err) {
+                } else if (p.err && rank == 0) {
                     atomicOr(p.err, kErrBadExpert);
                 }
             }
@@ -327,56 +371,96 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
         if (ng == kMaxGroups && lane == 31) sh.prefix[kMaxGroups] = incl;
     }
     if (warp == kMmaWarp) {
-        tmem_alloc(&sh.tmem_base, kTmemCols);
+        if constexpr (CG == 2)
+            tmem_alloc_pair(&sh.tmem_base, kTmemCols);
+        else
+            tmem_alloc(&sh.tmem_base, kTmemCols);
         tc_fence_before();
     }
     __syncthreads();
+    if constexpr (CG == 2) cluster_sync_all();  // peer barriers initialised, TMEM of both allocated
     tc_fence_after();
     const uint32_t tmem = sh.tmem_base;
 
     if (warp >= kAWarp0 && warp < kMmaWarp) {
         // ================= dequantiser =================
+        // k-blocks of this CTA: nkb per tile, tiles blockIdx/CG, + units, ...
+        const int units = gridDim.x / CG, u0 = blockIdx.x / CG;
+        const int iters = (sh.total > u0 ? (sh.total - u0 + units - 1) / units : 0) * nkb;
         const int at = tid - kAWarp0 * 32;  // 0..255
         const int r = at >> 1, h = at & 1;
         // raw rows: plain = r; gate/up = gate rows 0-63, up rows 64-127
         const int rr = gate_up(p.mode) ? ((r & 1) * 64 + (r >> 1)) : r;
-        QCursor lc, pc;
-        cursor_start(p, sh, lc);
-        pc = lc;
-        SLoad ring[kRing];
+        for (int it = 0; it < iters; ++it) {
+            const int s = it % S, a = it % SA;
+            const uint32_t ps = (uint32_t)(it / S) & 1u, pa = (uint32_t)(it / SA) & 1u;
+            if (!qwait<CG>(&sh.rawfull[s], ps, sh, p.err) || !qwait<CG>(&sh.sfull[s], ps, sh, p.err) ||
+                !qwait<CG>(&sh.aempty[a], pa ^ 1u, sh, p.err))
+                break;
+            const uint4 q = lds128(smem_u32(Ws + s * kRawStage + rr * 32 + h * 16));
+            const uint32_t sb = Ss[s * kTM + r];
+            const uint32_t s2 = (sb & 0xFFFFu) * 0x10001u, b2 = (sb >> 16) * 0x10001u;
+            const uint32_t dst = smem_u32(As + a * kAStage);
+            const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-        for (int j = 0; j < kRing; ++j) {
-            ring[j] = s_load<ST>(p, lc, r);
-            cursor_next(p, sh, lc, nkb);
+            for (int i = 0; i < 4; ++i) {
+                uint32_t o[4];
+                dq8_natural(wv[i], s2, b2, o);
+                sts128(dst + sw128(r, h * 4 + i), o[0], o[1], o[2], o[3]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                arrive_leader<CG>(&sh.afull[a]);
+                mbar_arrive(&sh.sempty[s]);
+            }
         }
-        bool live = true;
-        while (pc.valid && live) {
+    } else if (warp >= kScaleWarp) {
+        // ================= scale / bias loader =================
+        // two warps, 2 weight rows per lane; loads run kScaleAhead k-blocks
+        // ahead of use; row pointers are set once per tile
+        constexpr int D = Cfg::kScaleAhead;
+        const int r0 = (warp - kScaleWarp) * 64 + lane;  // rows r0, r0 + 32
+        QCursor lc;
+        cursor_start<CG>(p, sh, lc);
+        const int units = gridDim.x / CG, u0 = blockIdx.x / CG;
+        const int iters = (sh.total > u0 ? (sh.total - u0 + units - 1) / units : 0) * nkb;
+        const ST* ps[2] = {nullptr, nullptr};
+        const ST* pb[2] = {nullptr, nullptr};
+        auto fetch = [&](uint32_t v[2]) {
+            if (lc.valid && lc.kb == 0) {
 #pragma unroll
-            for (int j = 0; j < kRing; ++j) {
-                if (!pc.valid || !live) break;
-                const int s = j & (kStages - 1);
-                const uint32_t par = (uint32_t)(j / kStages) & 1u;
-                const SLoad cur = ring[j];
-                ring[j] = s_load<ST>(p, lc, r);
-                cursor_next(p, sh, lc, nkb);
-                if (!qwait(&sh.ldfull[s], par, sh, p.err)) {
+                for (int i = 0; i < 2; ++i) {
+                    ps[i] = scale_row<ST, CG>(p, lc.t, r0 + 32 * i, rank, false);
+                    pb[i] = scale_row<ST, CG>(p, lc.t, r0 + 32 * i, rank, true);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+                v[i] = (lc.valid && ps[i]) ? (scale_bits_f16<ST>(ps[i] + lc.kb) | (scale_bits_f16<ST>(pb[i] + lc.kb) << 16))
+                                           : 0u;
+            cursor_next<CG>(p, sh, lc, nkb);
+        };
+        uint32_t ring[D][2];
+#pragma unroll
+        for (int j = 0; j < D; ++j) fetch(ring[j]);
+        bool live = true;
+        for (int it0 = 0; it0 < iters && live; it0 += D) {
+#pragma unroll
+            for (int j = 0; j < D; ++j) {
+                const int it = it0 + j;
+                if (it >= iters) break;
+                const uint32_t c0 = ring[j][0], c1 = ring[j][1];
+                fetch(ring[j]);
+                const int s = it % S;
+                if (!qwait<CG>(&sh.sempty[s], (((uint32_t)(it / S)) & 1u) ^ 1u, sh, p.err)) {
                     live = false;
                     break;
                 }
-                const uint4 q = lds128(smem_u32(Ws + s * kRawStage + rr * 32 + h * 16));
-                const uint32_t s2 = (cur.sb & 0xFFFFu) * 0x10001u, b2 = (cur.sb >> 16) * 0x10001u;
-                const uint32_t dst = smem_u32(As + s * kAStage);
-                const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    uint32_t o[4];
-                    dq8_natural(wv[i], s2, b2, o);
-                    sts128(dst + sw128(r, h * 4 + i), o[0], o[1], o[2], o[3]);
-                }
-                fence_proxy_async_smem();
+                Ss[s * kTM + r0] = c0;
+                Ss[s * kTM + r0 + 32] = c1;
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&sh.full[s]);
-                cursor_next(p, sh, pc, nkb);
+                if (lane == 0) mbar_arrive(&sh.sfull[s]);
             }
         }
     } else if (warp == kLoadWarp) {
@@ -386,72 +470,109 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
             prefetch_tmap(&p.wmap0);
             if (gate_up(p.mode)) prefetch_tmap(&p.wmap1);
             QCursor cur;
-            cursor_start(p, sh, cur);
+            cursor_start<CG>(p, sh, cur);
             int it = 0;
             while (cur.valid) {
-                const int s = it % kStages;
-                if (!qwait(&sh.empty[s], ((uint32_t)(it / kStages) & 1u) ^ 1u, sh, p.err)) break;
-                const int nbox = (cur.t.cnt + kBBoxRows - 1) / kBBoxRows;
-                mbar_arrive_expect_tx(&sh.ldfull[s], (uint32_t)(nbox * kBBoxRows * 128 + kRawStage));
+                const int s = it % S;
+                if (!qwait<CG>(&sh.empty[s], ((uint32_t)(it / S) & 1u) ^ 1u, sh, p.err)) break;
+                // raw int4 weight rows of this CTA -> local barrier
+                mbar_arrive_expect_tx(&sh.rawfull[s], (uint32_t)kRawStage);
                 uint8_t* w = Ws + s * kRawStage;
-                const int z = cur.t.expert;
+                const int z = cur.t.expert, fb = cta_feat0<CG>(p, cur.t, rank);
                 if (gate_up(p.mode)) {
-                    tma_load_3d_u8(w, &p.wmap0, cur.kb * 32, cur.t.feat0, z, &sh.ldfull[s]);
-                    tma_load_3d_u8(w + kRawStage / 2, &p.wmap1, cur.kb * 32, cur.t.feat0, z, &sh.ldfull[s]);
+                    tma_load_3d_u8(w, &p.wmap0, cur.kb * 32, fb, z, &sh.rawfull[s]);
+                    tma_load_3d_u8(w + kRawStage / 2, &p.wmap1, cur.kb * 32, fb, z, &sh.rawfull[s]);
                 } else {
-                    tma_load_3d_u8(w, &p.wmap0, cur.kb * 32, cur.t.feat0, z, &sh.ldfull[s]);
-                    tma_load_3d_u8(w + kRawStage / 2, &p.wmap0, cur.kb * 32, cur.t.feat0 + 64, z, &sh.ldfull[s]);
+                    tma_load_3d_u8(w, &p.wmap0, cur.kb * 32, fb, z, &sh.rawfull[s]);
+                    tma_load_3d_u8(w + kRawStage / 2, &p.wmap0, cur.kb * 32, fb + 64, z, &sh.rawfull[s]);
                 }
-                uint8_t* dst = Bs + s * kBStage;
-                for (int i = 0; i < nbox; ++i)
-                    tma_load_2d(dst + i * kBBoxRows * 128, &p.xmap, cur.kb * 64, cur.t.row0 + i * kBBoxRows,
-                                &sh.ldfull[s]);
+                // this CTA's token rows -> the leader's barrier
+                const int N = max(16, (cur.t.cnt + 15) & ~15);
+                const int brows = CG == 2 ? N / 2 : cur.t.cnt;
+                const int brow0 = cur.t.row0 + rank * (N / 2);
+                const int nbox = (brows + kBBoxRows - 1) / kBBoxRows;
+                uint8_t* dst = Bs + s * Cfg::kBStage;
+                if constexpr (CG == 2) {
+                    const uint32_t lb = mapa_shared(&sh.bfull[s], 0);
+                    mbar_arrive_expect_tx_cluster(lb, (uint32_t)(nbox * kBBoxRows * 128));
+                    for (int i = 0; i < nbox; ++i)
+                        tma_load_2d_pair(dst + i * kBBoxRows * 128, &p.xmap, cur.kb * 64, brow0 + i * kBBoxRows, lb);
+                } else {
+                    mbar_arrive_expect_tx(&sh.bfull[s], (uint32_t)(nbox * kBBoxRows * 128));
+                    for (int i = 0; i < nbox; ++i)
+                        tma_load_2d(dst + i * kBBoxRows * 128, &p.xmap, cur.kb * 64, brow0 + i * kBBoxRows,
+                                    &sh.bfull[s]);
+                }
                 ++it;
-                cursor_next(p, sh, cur, nkb);
+                cursor_next<CG>(p, sh, cur, nkb);
             }
         }
         __syncwarp();
     } else if (warp == kMmaWarp) {
-        // ================= MMA issue (one thread) =================
-        int it = 0, lt = 0;
-        bool live = true;
-        for (int idx = blockIdx.x; live; idx += gridDim.x, ++lt) {
-            QTile t;
-            if (!decode_tile(p, sh, idx, t)) break;
-            const int acc = lt & 1;
-            if (!qwait(&sh.tempty[acc], (((uint32_t)lt >> 1) & 1u) ^ 1u, sh, p.err)) {
-                live = false;
-                break;
-            }
-            tc_fence_after();
-            const int N = max(16, (t.cnt + 15) & ~15);
-            const uint32_t idesc = make_idesc_f16(kTM, N);
-            const uint32_t d = tmem + (uint32_t)(acc * kAccCols);
-            for (int kb = 0; kb < nkb; ++kb, ++it) {
-                const int s = it % kStages;
-                const uint32_t par = (uint32_t)(it / kStages) & 1u;
-                if (!qwait(&sh.full[s], par, sh, p.err) || !qwait(&sh.ldfull[s], par, sh, p.err)) {
+        // ================= MMA issue (one thread of the leader) =================
+        if (leader) {
+            int it = 0, lt = 0;
+            bool live = true;
+            for (int idx = blockIdx.x / CG; live; idx += gridDim.x / CG, ++lt) {
+                QTile t;
+                if (!decode_tile<CG>(p, sh, idx, t)) break;
+                const int acc = lt & 1;
+                if (!qwait<CG>(&sh.tempty[acc], (((uint32_t)lt >> 1) & 1u) ^ 1u, sh, p.err)) {
                     live = false;
                     break;
                 }
                 tc_fence_after();
-                if (lane == 0) {
-                    const uint64_t ad = make_sw128_desc(As + s * kAStage);
-                    const uint64_t bd = make_sw128_desc(Bs + s * kBStage);
+                const int N = max(16, (t.cnt + 15) & ~15);
+                const uint32_t idesc = make_idesc_f16(kTM * CG, N);
+                const uint32_t d = tmem + (uint32_t)(acc * kAccCols);
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % S, a = it % SA;
+                    if (!qwait<CG>(&sh.afull[a], (uint32_t)(it / SA) & 1u, sh, p.err) ||
+                        !qwait<CG>(&sh.bfull[s], (uint32_t)(it / S) & 1u, sh, p.err)) {
+                        live = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint64_t ad = make_sw128_desc(As + a * kAStage);
+                        const uint64_t bd = make_sw128_desc(Bs + s * Cfg::kBStage);
 #pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        umma_f16(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb | k) ? 1u : 0u);
-                    umma_commit(&sh.empty[s]);
+                        for (int k = 0; k < 4; ++k) {
+                            if constexpr (CG == 2)
+                                umma_f16_pair(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc,
+                                              (kb | k) ? 1u : 0u);
+                            else
+                                umma_f16(d, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc,
+                                         (kb | k) ? 1u : 0u);
+                        }
+                        if constexpr (CG == 2) {
+                            umma_commit_pair(&sh.empty[s], 3);
+                            umma_commit_pair(&sh.aempty[a], 3);
+                        } else {
+                            umma_commit(&sh.empty[s]);
+                            umma_commit(&sh.aempty[a]);
+                        }
+                    }
+                    __syncwarp();
+                }
+                if (!live) break;
+                if (lane == 0) {
+                    if constexpr (CG == 2)
+                        umma_commit_pair(&sh.tfull[acc], 3);
+                    else
+                        umma_commit(&sh.tfull[acc]);
                 }
                 __syncwarp();
             }
-            if (!live) break;
-            if (lane == 0) umma_commit(&sh.tfull[acc]);
+            // all issued MMAs retire before TMEM is released
+            if (lane == 0) {
+                if constexpr (CG == 2)
+                    umma_commit_pair(&sh.done, 3);
+                else
+                    umma_commit(&sh.done);
+            }
             __syncwarp();
         }
-        // all issued MMAs retire before TMEM is released
-        if (lane == 0) umma_commit(&sh.done);
-        __syncwarp();
         uint32_t i = 0;
         for (; i < kQSpin; ++i)
             if (mbar_try_wait(&sh.done, 0)) break;
@@ -462,14 +583,14 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
         const int row = ew * 32 + lane;
         const bool gu = gate_up(p.mode);
         int lt = 0;
-        for (int idx = blockIdx.x;; idx += gridDim.x, ++lt) {
+        for (int idx = blockIdx.x / CG;; idx += gridDim.x / CG, ++lt) {
             QTile t;
-            if (!decode_tile(p, sh, idx, t)) break;
+            if (!decode_tile<CG>(p, sh, idx, t)) break;
             const int acc = lt & 1;
-            if (!qwait(&sh.tfull[acc], ((uint32_t)lt >> 1) & 1u, sh, p.err)) break;
+            if (!qwait<CG>(&sh.tfull[acc], ((uint32_t)lt >> 1) & 1u, sh, p.err)) break;
             tc_fence_after();
             const uint32_t tbase = tmem + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * kAccCols);
-            const int f = t.feat0 + (gu ? (row >> 1) : row);
+            const int f = cta_feat0<CG>(p, t, rank) + (gu ? (row >> 1) : row);
             const bool fok = f < p.nfeat;
             for (int cc = 0; cc * 32 < t.cnt; ++cc) {
                 float v[32];
@@ -511,14 +632,20 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&sh.tempty[acc]);
+            if (lane == 0) arrive_leader<CG>(&sh.tempty[acc]);
         }
     }
 
     __syncthreads();
+    // the pair's MMAs have retired (done barrier) and both epilogues are
+    // finished before either CTA frees TMEM or leaves its shared memory
+    if constexpr (CG == 2) cluster_sync_all();
     if (warp == kMmaWarp) {
         tc_fence_after();
-        tmem_dealloc(tmem, kTmemCols);
+        if constexpr (CG == 2)
+            tmem_dealloc_pair(tmem, kTmemCols);
+        else
+            tmem_dealloc(tmem, kTmemCols);
     }
 }
 
@@ -573,18 +700,45 @@ __global__ void reduce_token_major_kernel(const __half* __restrict__ partials, c
     }
 }
 
-tf_status launch_qmm(tf_context* ctx, const QmmParams& p, tf_scale_type st, int grid, cudaStream_t stream,
-                     const char* name) {
-    const void* fn = st == TF_SCALE_BF16 ? reinterpret_cast<const void*>(&qmm_kernel<__nv_bfloat16>)
-                                         : reinterpret_cast<const void*>(&qmm_kernel<__half>);
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kQSmemBytes);
+template <typename ST, int CG>
+tf_status launch_qmm_cg(tf_context* ctx, const QmmParams& p, cudaStream_t stream, const char* name) {
+    const void* fn = reinterpret_cast<const void*>(&qmm_kernel<ST, CG>);
+    const int smem = (int)qsmem_bytes<CG>();
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return cuda_check(ctx, e, name);
-    if (grid <= 0) return TF_OK;
+    // persistent: one CTA (pair) per SM (pair); dense problems never need more
+    // than their tile count
+    long long units = ctx->num_sms / CG;
+    if (p.mode == kDensePlain || p.mode == kDenseGateUp) {
+        const int fpt = (p.mode == kDenseGateUp ? kTM / 2 : kTM) * CG;
+        units = std::min<long long>(units, (long long)((p.T + kTN - 1) / kTN) * ((p.nfeat + fpt - 1) / fpt));
+    }
+    if (units <= 0) return TF_OK;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(units * CG));
+    cfg.blockDim = dim3(kQThreads);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CG;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = CG == 2 ? 1 : 0;
+    return cuda_check(ctx, cudaLaunchKernelEx(&cfg, qmm_kernel<ST, CG>, p), name);
+}
+
+// One SM per tile by default (measured faster on B200: 590 vs 400 TFLOP/s on
+// the 4096 x 2112 x 2816 shape); TFCUDA_QMM_PAIR=1 selects CTA pairs with
+// 2-SM MMAs (same arithmetic).  Read per call.
+tf_status launch_qmm(tf_context* ctx, const QmmParams& p, tf_scale_type st, cudaStream_t stream, const char* name) {
+    const char* env = getenv("TFCUDA_QMM_PAIR");
+    const bool pair = env && env[0] == '1';
     if (st == TF_SCALE_BF16)
-        qmm_kernel<__nv_bfloat16><<<grid, kQThreads, kQSmemBytes, stream>>>(p);
-    else
-        qmm_kernel<__half><<<grid, kQThreads, kQSmemBytes, stream>>>(p);
-    return cuda_check(ctx, cudaGetLastError(), name);
+        return pair ? launch_qmm_cg<__nv_bfloat16, 2>(ctx, p, stream, name)
+                    : launch_qmm_cg<__nv_bfloat16, 1>(ctx, p, stream, name);
+    return pair ? launch_qmm_cg<__half, 2>(ctx, p, stream, name) : launch_qmm_cg<__half, 1>(ctx, p, stream, name);
 }
 
 bool scale_type_ok(tf_scale_type st) { return st == TF_SCALE_BF16 || st == TF_SCALE_F16; }
@@ -634,9 +788,7 @@ tf_status tf_int4_qmm(tf_context* ctx, const void* weights, const void* scales, 
     p.y = static_cast<__half*>(y);
     p.ldy = y_stride;
     p.err = ctx->d_err;
-    const long long tiles = (long long)((t + kTN - 1) / kTN) * ((n + kTM - 1) / kTM);
-    return launch_qmm(ctx, p, st, (int)std::min<long long>(tiles, ctx->num_sms), static_cast<cudaStream_t>(stream),
-                      name);
+    return launch_qmm(ctx, p, st, static_cast<cudaStream_t>(stream), name);
 }
 
 tf_status tf_prefill_shared_expert(tf_context* ctx, const void* x, uint32_t x_stride, const tf_affine_matrix* gate,
@@ -679,8 +831,7 @@ tf_status tf_prefill_shared_expert(tf_context* ctx, const void* x, uint32_t x_st
     p.ldy = f;
     p.round_gu = 1;
     p.err = ctx->d_err;
-    long long tiles = (long long)((t + kTN - 1) / kTN) * ((f + kTM / 2 - 1) / (kTM / 2));
-    tf_status rc = launch_qmm(ctx, p, st, (int)std::min<long long>(tiles, ctx->num_sms), s, name);
+    tf_status rc = launch_qmm(ctx, p, st, s, name);
     if (rc != TF_OK) return rc;
     QmmParams q{};
     q.mode = kDensePlain;
@@ -693,8 +844,7 @@ tf_status tf_prefill_shared_expert(tf_context* ctx, const void* x, uint32_t x_st
     q.y = static_cast<__half*>(y);
     q.ldy = y_stride;
     q.err = ctx->d_err;
-    tiles = (long long)((t + kTN - 1) / kTN) * ((d + kTM - 1) / kTM);
-    return launch_qmm(ctx, q, st, (int)std::min<long long>(tiles, ctx->num_sms), s, name);
+    return launch_qmm(ctx, q, st, s, name);
 }
 
 tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64_t expert_stride, uint32_t num_experts,
@@ -767,9 +917,9 @@ tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64_t expe
         tf_status rc0 = cuda_check(ctx, cudaGetLastError(), name);
         if (rc0 != TF_OK) return rc0;
     }
-    tf_status rc = launch_qmm(ctx, p, st, ctx->num_sms, s, name);
+    tf_status rc = launch_qmm(ctx, p, st, s, name);
     if (rc != TF_OK) return rc;
-    return launch_qmm(ctx, q, st, ctx->num_sms, s, name);
+    return launch_qmm(ctx, q, st, s, name);
 }
 
 tf_status tf_moe_reduce_token_major(tf_context* ctx, const void* route_partials, const void* routing_weights,

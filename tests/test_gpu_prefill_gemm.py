@@ -44,6 +44,38 @@ def test_int4_qmm(cuda, T, N, K, st):
     assert O.rel_error(O.f16_to_f32(f16(y)), y32) < FP16_TOL
 
 
+@pytest.mark.parametrize("T,N,K", [(300, 2112, 2816), (17, 200, 128)])
+def test_int4_qmm_cta_pairs(cuda, T, N, K, monkeypatch):
+    """The 2-SM (CTA pair) variant, selected with TFCUDA_QMM_PAIR=1."""
+    monkeypatch.setenv("TFCUDA_QMM_PAIR", "1")
+    rng = O.seed_tree(T * 7 + N, f"qmm-pair-{K}")
+    W, S, B = rng.synthetic_affine(N, K, 4, 0)
+    X = rng.normal_f16(T * K).reshape(T, K)
+    _, y32 = O.int4_qmm(W, S, B, X, T, N, K, 0)
+    y = torch.empty(T, N, dtype=torch.float16, device="cuda")
+    PrefillInt4QMM().encode(dev(W), dev(S, torch.bfloat16), dev(B, torch.bfloat16), dev(X, torch.float16), y, T, N, K)
+    torch.cuda.synchronize()
+    assert O.rel_error(O.f16_to_f32(f16(y)), y32) < FP16_TOL
+
+
+@pytest.mark.parametrize("pair", ["0", "1"])
+def test_grouped_routed_config1_shapes_both_variants(cuda, pair, monkeypatch):
+    monkeypatch.setenv("TFCUDA_QMM_PAIR", pair)
+    T, K, E, D, F = 48, 8, 16, 2816, 704
+    ex = Experts(E, D, F, 0, "g-variants")
+    idx, w = skewed_routing(T, K, E, 99)
+    X = O.seed_tree(T, "gx-variants").normal_f16(T * D).reshape(T, D)
+    pairs = PrefillRouter.make_token_expert_pairs(idx, w, T, K)
+    ref = O.group_pairs(pairs, T, K, E, 16)
+    part_ref = O.grouped_routed(ex.host.reshape(-1), ex.lay.stride, ex.off, ref["sorted"], X, D, D, F, K, T, 0)
+    routes = route_sort(dev(idx.view(np.int32)), dev(w), T, K, E, 16)
+    act = torch.empty(T * K, F, dtype=torch.float16, device="cuda")
+    part = torch.empty(T * K, D, dtype=torch.float16, device="cuda")
+    PrefillGroupedRoutedMoE().encode(ex.pool(), routes, dev(X, torch.float16), act, part, T, K)
+    torch.cuda.synchronize()
+    assert O.rel_error(O.f16_to_f32(f16(part)), O.f16_to_f32(part_ref)) < FP16_TOL
+
+
 def test_int4_qmm_strided_rows(cuda):
     T, N, K, LX, LY = 40, 256, 256, 320, 272
     rng = O.seed_tree(5, "qmm-strided")
