@@ -46,12 +46,14 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=30)
     ap.add_argument("--ring", type=int, default=8)
-    ap.add_argument("--scale-dtype", choices=["bf16", "f16"], default="bf16")
+    ap.add_argument("--scale-dtype", choices=["bf16", "f16"], default=None,
+                    help="scale/bias storage; default fp16 for config 0 (as BASELINE states it), else bf16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--workload", choices=["decode", "batched", "prefill"], default="decode",
-                    help="decode = config 1 (default, the headline); batched = config 2 (64 tokens); "
-                         "prefill = config 3 (4096 tokens)")
+    ap.add_argument("--workload", choices=["decode", "gemv", "batched", "prefill"], default="decode",
+                    help="decode = config 1 (default, the headline); gemv = config 0 (int4 GEMV 1408x2816 "
+                         "streamed from HBM); batched = config 2 (64 tokens); prefill = config 3 (4096 tokens)")
+    ap.add_argument("--matrices", type=int, default=256, help="gemv: distinct weight matrices per step")
     ap.add_argument("--tokens", type=int, default=0, help="override the chunk's token count (batched/prefill)")
     return ap.parse_args()
 
@@ -162,6 +164,19 @@ def layer_bytes():
 
 def run_reference(a, rank):
     if rank != 0:
+        return
+    if a.workload == "gemv":
+        gps, threads, sample = gemv_cpu_sample(max(5.0, a.cpu_seconds))
+        v = gps * G_BYTES / 1e9
+        print(json.dumps({"metric": "int4 g64 GEMV HBM GB/s (config 0)", "value": v, "unit": "GB/s",
+                          "impl": "reference", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
+                          "ms_per_step": 1e3 * a.matrices / gps, "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "f32-acc/int4", "data": "synthetic (BASELINE config 0)",
+                          "config": {"workload": "config0 int4 GEMV 1408x2816", "matrices": a.matrices},
+                          "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": "port",
+                                           "sample": sample},
+                          "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+              flush=True)
         return
     lps, threads, sample = cpu_sample(max(5.0, a.cpu_seconds), "reference")
     if a.workload != "decode":
@@ -374,6 +389,175 @@ def run_ours(a, rank, world, local_rank):
             "cpu_baseline": cpu,
             "clocks": clk,
             "gpu_launches": launches_per_step * a.steps,
+        }
+        print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------- config 0 GEMV ----
+G_M, G_N = 1408, 2816
+G_BYTES = G_M * G_N // 2 + 2 * G_M * (G_N // 64) * 2 + G_N * 2 + G_M * 2  # 2,238,720 B (W + s/b + x + y)
+
+
+def gemv_cpu_sample(seconds: float):
+    """Oracle port of the reference's int4 GEMV (kernel order) on the host cores."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+    threads = O.lib().orc_max_threads()
+    rng = O.seed_tree(0, "bench-gemv")
+    W, S, B = rng.synthetic_affine(G_M, G_N, 4, 1)
+    x = rng.normal_f16(G_N)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.int4_gemv_kernel_order(W, S, B, x, 1, threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return n / el, threads, f"{n} config-0 GEMVs (1408x2816 int4 g64, fp16 scales) in {el:.1f} s"
+
+
+def run_gemv(a, rank, world, local_rank):
+    """Config 0: the int4 g64 GEMV 1408x2816 over `--matrices` distinct,
+    HBM-resident weight matrices (> L2 in total), one batched launch per step."""
+    import torch
+    import torch.distributed as dist
+
+    from edgeexpert_b200._lib import Context
+    from edgeexpert_b200.format import synthetic_affine
+    from edgeexpert_b200.quant import DequantInt4GEMV, affine_gemv_batched
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    ctx = Context.get(local_rank)
+    sdt = torch.bfloat16 if a.scale_dtype == "bf16" else torch.float16
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(77 + rank)
+    R = a.matrices
+    W, S, B = synthetic_affine(R * G_M, G_N, 4, sdt, dev, gen)
+    x = torch.randn(G_N, device=dev, generator=gen).to(torch.float16)
+    y = torch.empty(R, G_M, dtype=torch.float16, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    wstride, sbstride = G_M * G_N // 2, G_M * (G_N // 64)
+
+    def step(s, xx):
+        affine_gemv_batched(W, S, B, xx, y, bits=4, m=G_M, n=G_N, batch=R, w_stride_bytes=wstride,
+                            sb_stride=sbstride, y_batch_stride=G_M, stream=s, context=ctx)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    x_in = torch.empty_like(x)
+    with torch.cuda.stream(stream):
+        step(stream, x)
+    torch.cuda.synchronize()
+    g, g_in = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        step(stream, x)
+    with torch.cuda.graph(g_in, stream=stream):
+        step(stream, x_in)
+    with torch.cuda.stream(stream):
+        for _ in range(a.warmup):
+            g.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(a.steps):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+    clk = clocks.stop()
+
+    # end to end: x H2D (pinned) and every y D2H each step
+    h_x = torch.empty(G_N, dtype=torch.float16, pin_memory=True)
+    h_x.copy_(x.cpu())
+    h_y = torch.empty(R, G_M, dtype=torch.float16, pin_memory=True)
+    with torch.cuda.stream(stream):
+        for _ in range(a.warmup):
+            x_in.copy_(h_x, non_blocking=True)
+            g_in.replay()
+            h_y.copy_(y, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        f0.record(stream)
+        for _ in range(a.steps):
+            x_in.copy_(h_x, non_blocking=True)
+            g_in.replay()
+            h_y.copy_(y, non_blocking=True)
+        f1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = max_over_ranks(f0.elapsed_time(f1) / a.steps)
+
+    # single-GEMV latency through DequantInt4GEMV.encode (one launch per matrix)
+    q = DequantInt4GEMV(ctx)
+    gs = torch.cuda.CUDAGraph()
+    nl = min(R, 64)
+    with torch.cuda.stream(stream):
+        q.encode(W[:G_M], S[:G_M], B[:G_M], x, y[0], G_M, G_N, stream=stream)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(gs, stream=stream):
+        for i in range(nl):
+            q.encode(W[i * G_M:(i + 1) * G_M], S[i * G_M:(i + 1) * G_M], B[i * G_M:(i + 1) * G_M], x, y[i], G_M, G_N,
+                     stream=stream)
+    with torch.cuda.stream(stream):
+        gs.replay()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        s0.record(stream)
+        gs.replay()
+        s1.record(stream)
+    torch.cuda.synchronize()
+    single_us = s0.elapsed_time(s1) * 1e3 / nl
+    ctx.check_device(stream)
+
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak, src = (peaks["hbm_gbs"], "measured hbm_gbs") if "hbm_gbs" in peaks else (6650.0, "fallback")
+    per_step = R * G_BYTES
+    value = world * per_step / (ms * 1e-3) / 1e9
+    achieved = per_step / (ms * 1e-3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        gps, threads, sample = gemv_cpu_sample(a.cpu_seconds)
+        cpu = {"value": gps * G_BYTES / 1e9, "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample}
+    traffic = None
+    tr = ROOT / "profiles" / "gemv_traffic.json"
+    if tr.exists():
+        traffic = json.loads(tr.read_text()).get("bytes_per_launch")
+    if rank == 0:
+        line = {
+            "metric": "int4 g64 GEMV HBM GB/s (config 0)", "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16-act/int4-w/fp32-acc",
+            "data": "synthetic (BASELINE config-0 distributions, random-init weights)",
+            "config": {"workload": f"config0: int4 g64 GEMV 1408x2816 over {R} distinct HBM-resident matrices "
+                                   "(one batched launch per step)", "matrices": R, "m": G_M, "n": G_N,
+                       "scale_dtype": a.scale_dtype,
+                       "l2": "%.0f MB of weights per step exceed L2 (126 MB); no flush needed" % (per_step / 1e6)},
+            "single_gemv_us": single_us, "single_gemv_gbs": G_BYTES / (single_us * 1e-6) / 1e9,
+            "e2e": {"value": world * per_step / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": G_N * 2,
+                    "d2h_bytes_per_step": R * G_M * 2},
+            "roofline": {"bound": "hbm", "kernel": "engine_kernel<GemvPolicy> (batched)", "achieved": achieved,
+                         "peak": peak, "peak_source": src, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": traffic, "bytes_per_launch": per_step, "us_per_launch": ms * 1e3},
+            "cpu_baseline": cpu, "clocks": clk, "gpu_launches": a.steps,
         }
         print(json.dumps(line), flush=True)
 
@@ -608,6 +792,8 @@ def run_chunk(a, rank, world, local_rank):
 
 def main():
     a = parse()
+    if a.scale_dtype is None:
+        a.scale_dtype = "f16" if a.workload == "gemv" else "bf16"
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -621,6 +807,8 @@ def main():
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     if a.workload == "decode":
         run_ours(a, rank, world, local_rank)
+    elif a.workload == "gemv":
+        run_gemv(a, rank, world, local_rank)
     else:
         run_chunk(a, rank, world, local_rank)
     if world > 1:
