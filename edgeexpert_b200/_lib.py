@@ -121,6 +121,9 @@ _PROTOS = {
     "tf_moe_grouped_routed": ([_P, _P, _U64, _U32, C.POINTER(ExpertOffsets), _P, _P, _P, _P, _U32, _P, _P, _U32,
                                _U32, _U32, _U32, _I, _P], _I),
     "tf_moe_reduce_token_major": ([_P, _P, _P, _P, _U32, _U32, _U32, _P], _I),
+    "tf_ep_send_counts": ([_P, _P, _U32, _U32, _U32, _P, _P], _I),
+    "tf_ep_pack": ([_P, _P, _U32, _P, _U32, _U32, _U32, _U32, _P, _P, _P], _I),
+    "tf_moe_combine_sorted": ([_P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _P], _I),
 }
 
 # Symbols of include/tfcuda.h added by later milestones register here too.

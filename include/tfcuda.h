@@ -304,6 +304,31 @@ TF_API tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64
 TF_API tf_status tf_moe_reduce_token_major(tf_context* ctx, const void* route_partials, const void* routing_weights,
                                            void* h2, uint32_t T, uint32_t top_k, uint32_t d, void* stream);
 
+/* ---- expert parallelism (routed experts sharded over GPUs) ------------------------------ */
+/* No reference counterpart: the reference runs on one Apple GPU and streams
+ * experts from SSD.  Experts are sharded in contiguous id ranges of
+ * experts_per_rank; the exchange itself is the caller's all-to-all (NCCL). */
+
+/* send_counts[r] = sum of counts[e] over the experts rank r owns
+ * (counts: the per-expert output of tf_moe_route_sort).  Device uint32 arrays. */
+TF_API tf_status tf_ep_send_counts(tf_context* ctx, const void* counts, uint32_t num_experts,
+                                   uint32_t experts_per_rank, uint32_t world, void* send_counts, void* stream);
+
+/* The all-to-all send buffer: rows[p] = hidden[pairs[p].token] (fp16 [n][d]) and
+ * local_expert[p] = pairs[p].expert % experts_per_rank, in sorted-pair order,
+ * so each destination's rows are one contiguous range. */
+TF_API tf_status tf_ep_pack(tf_context* ctx, const void* hidden, uint32_t hidden_stride, const void* sorted_pairs,
+                            uint32_t n_pairs, uint32_t d, uint32_t T, uint32_t experts_per_rank, void* rows,
+                            void* local_expert, void* stream);
+
+/* PrefillMoE.encodeReduceTokenMajor (PrefillMoE.swift:11-40; prefill.metal:575-596) over
+ * partials held in sorted-pair order (what the combine all-to-all returns):
+ * h2[t][i] = half(sum_r fma(w[t][r], partials_sorted[pos(t, r)][i])), rank order, where
+ * pos(t, r) is the pair's index in sorted_pairs.  inv_scratch: uint32[T*top_k]. */
+TF_API tf_status tf_moe_combine_sorted(tf_context* ctx, const void* sorted_pairs, const void* partials_sorted,
+                                       const void* routing_weights, void* inv_scratch, void* h2, uint32_t T,
+                                       uint32_t top_k, uint32_t d, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
