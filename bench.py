@@ -50,9 +50,10 @@ def parse():
                     help="scale/bias storage; default fp16 for config 0 (as BASELINE states it), else bf16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--workload", choices=["decode", "gemv", "batched", "prefill"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "gemv", "batched", "prefill", "ep"], default="decode",
                     help="decode = config 1 (default, the headline); gemv = config 0 (int4 GEMV 1408x2816 "
-                         "streamed from HBM); batched = config 2 (64 tokens); prefill = config 3 (4096 tokens)")
+                         "streamed from HBM); batched = config 2 (64 tokens); prefill = config 3 (4096 tokens); "
+                         "ep = config-4 MoE decode batch with the routed experts sharded over the GPUs")
     ap.add_argument("--matrices", type=int, default=256, help="gemv: distinct weight matrices per step")
     ap.add_argument("--tokens", type=int, default=0, help="override the chunk's token count (batched/prefill)")
     return ap.parse_args()
@@ -562,6 +563,109 @@ def run_gemv(a, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------- expert parallel (EP) ----
+def run_ep(a, rank, world, local_rank):
+    """A decode batch of B tokens (default 256, config 4's largest) through
+    one config-1 MoE layer per step, experts sharded E/N per GPU, tokens split
+    B/N per GPU (strong scaling: the job is fixed).  Per rank: batched router
+    on its tokens, expert-parallel routed experts (NCCL all-to-all dispatch
+    and combine), shared expert on its tokens."""
+    import torch
+    import torch.distributed as dist
+
+    from edgeexpert_b200._lib import Context
+    from edgeexpert_b200.ep import ExpertParallelMoE
+    from edgeexpert_b200.format import synthetic_moe_layer
+    from edgeexpert_b200.moe import ExpertPool
+    from edgeexpert_b200.prefill import PrefillRouter, PrefillSharedExpert
+
+    B = a.tokens or 256
+    if B % world:
+        raise SystemExit(f"--tokens {B} must split over {world} GPUs")
+    T = B // world
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    ctx = Context.get(local_rank)
+    sdt = torch.bfloat16 if a.scale_dtype == "bf16" else torch.float16
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2024)  # identical layer on every rank; each keeps its experts
+    nl = 4
+    layers, pools = [], []
+    per = E // world
+    for _ in range(nl):
+        L = synthetic_moe_layer(D, F, FS, E, TOPK, 4, sdt, dev, gen)
+        L.per_expert_scale.copy_((1.0 + 0.3 * torch.randn(E, device=dev, generator=gen)).abs().to(torch.bfloat16))
+        full = L.experts
+        blob = full.blob.view(E, -1)[rank * per:(rank + 1) * per].reshape(-1).clone()
+        pools.append(ExpertPool(blob, full.stride, per, full.offsets, D, F, full.scale_dtype))
+        L.experts = None
+        del full
+        layers.append(L)
+    torch.cuda.empty_cache()
+    g2 = torch.Generator(device=dev)
+    g2.manual_seed(99 + rank)
+    xs = torch.randn(nl, T, D, device=dev, generator=g2).to(torch.float16)
+    idx = torch.empty(T, TOPK, dtype=torch.int32, device=dev)
+    wts = torch.empty(T, TOPK, dtype=torch.float16, device=dev)
+    h2 = torch.empty(T, D, dtype=torch.float16, device=dev)
+    acts = torch.empty(T, FS, dtype=torch.float16, device=dev)
+    ys = torch.empty(T, D, dtype=torch.float16, device=dev)
+    router, shared = PrefillRouter(ctx), PrefillSharedExpert(ctx)
+    eps = [ExpertParallelMoE(pools[i], E, TOPK, context=ctx) for i in range(nl)]
+
+    def step(i):
+        L, x = layers[i % nl], xs[i % nl]
+        router.encode_gemma4_block(L.router_w, L.router_s, L.router_b, x, L.eff_scale, L.per_expert_scale, idx,
+                                   wts, T, E, D, TOPK)
+        eps[i % nl].forward(x, idx, wts, h2)
+        shared.encode(x, L.shared_gate, L.shared_up, L.shared_down, acts, ys, T)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for i in range(a.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(a.steps):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+    clk = clocks.stop()
+    ctx.check_device(None)
+    sent = eps[(a.steps - 1) % nl].last.sent
+    flops = chunk_flops(B)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "MoE decode tok/s, experts sharded over GPUs (config 4 batch)", "value": B * 1e3 / ms,
+            "unit": "tok/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16-act/int4-w/fp32-acc",
+            "data": "synthetic (BASELINE distributions, random-init weights)",
+            "config": {"workload": f"config-4 decode batch of {B} tokens through one config-1 MoE layer, "
+                                   f"{per} routed experts per GPU, {T} tokens per GPU, NCCL all-to-all",
+                       "tokens": B, "experts_per_gpu": per, "parallelism": f"ep{world}", "layer_ring": nl,
+                       "rank0_sent_pairs_per_rank": sent},
+            "tflops": flops / (ms * 1e-3) / 1e12,
+            "e2e": None, "roofline": None, "cpu_baseline": None, "clocks": clk,
+            "gpu_launches": None,
+        }), flush=True)
+
+
 # ------------------------------------------------------ chunk workloads ----
 CHUNK_TOKENS = {"batched": 64, "prefill": 4096}
 
@@ -809,6 +913,8 @@ def main():
         run_ours(a, rank, world, local_rank)
     elif a.workload == "gemv":
         run_gemv(a, rank, world, local_rank)
+    elif a.workload == "ep":
+        run_ep(a, rank, world, local_rank)
     else:
         run_chunk(a, rank, world, local_rank)
     if world > 1:
