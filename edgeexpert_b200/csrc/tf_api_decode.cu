@@ -290,7 +290,7 @@ tf_status tf_router_topk(tf_context* ctx, const void* W, const void* S, const vo
 static tf_status phase1_launch(tf_context* ctx, const ExpertSource& src, const void* x, void* acts, uint32_t d,
                                uint32_t f, uint32_t top_k, const tf_affine_matrix* sg, const tf_affine_matrix* su,
                                void* shared_act, tf_scale_type st, cudaStream_t cs, const char* name,
-                               Phase1Params* build_only = nullptr) {
+                               Phase1Params* build_only = nullptr, bool lazy_ids = false) {
     if (!x || (!acts && top_k)) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null activation pointer", name);
     if (d == 0 || d % 64 || f == 0 || f % 64) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: d and f must be positive multiples of 64", name);
     if (f > (uint32_t)kMaxF * 4) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: f too large", name);
@@ -322,8 +322,13 @@ static tf_status phase1_launch(tf_context* ctx, const ExpertSource& src, const v
     p.x_aligned = aligned16(x);
     p.err = ctx->d_err;
     p.fjobs = (int)f / 8;
-    p.sched = make_sched((int)top_k * p.fjobs, units_for_K((int)d, 4), sg ? (int)sg->rows / 8 : 0,
-                         sg ? units_for_K((int)d, (int)sg->bits) : 1, ctx->num_sms);
+    p.lazy_ids = (lazy_ids && sg && top_k && src.ids != nullptr && !src.ids_in_smem) ? 1 : 0;
+    if (p.lazy_ids)  // shared jobs first: they need no routing
+        p.sched = make_sched((int)sg->rows / 8, units_for_K((int)d, (int)sg->bits), (int)top_k * p.fjobs,
+                             units_for_K((int)d, 4), ctx->num_sms);
+    else
+        p.sched = make_sched((int)top_k * p.fjobs, units_for_K((int)d, 4), sg ? (int)sg->rows / 8 : 0,
+                             sg ? units_for_K((int)d, (int)sg->bits) : 1, ctx->num_sms);
     const int sj = p.sched.S_total;
     if (build_only) {
         *build_only = p;
@@ -542,7 +547,8 @@ tf_status tf_moe_decode_layer(tf_context* ctx, const tf_moe_layer* L, const void
     if (s) return s;
     ExpertSource src = make_source(L->expert_pool, L->expert_stride, L->num_experts, idx, nullptr, &L->offsets, L->top_k);
     s = phase1_launch(ctx, src, x, ctx->d_acts, L->d, L->f, L->top_k, shared ? &L->shared_gate : nullptr,
-                      shared ? &L->shared_up : nullptr, ctx->d_shared_act, L->scale_type, cs, "tf_moe_decode_layer/phase1");
+                      shared ? &L->shared_up : nullptr, ctx->d_shared_act, L->scale_type, cs, "tf_moe_decode_layer/phase1",
+                      nullptr, /*lazy_ids=*/true);
     if (s) return s;
     return phase2_launch(ctx, src, ctx->d_acts, w, residual, y, L->d, L->f, L->top_k,
                          shared ? &L->shared_down : nullptr, ctx->d_shared_act, L->scale_type, cs,

@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda_runtime.h>
 #include <stdarg.h>
+#include <stdlib.h>
 #include <stdio.h>
 #include <string.h>
 
@@ -89,8 +90,22 @@ tf_status launch_engine(tf_context* ctx, const typename Pol::Params& p, size_t x
         configured[dev] = true;
     }
     const int grid = superjobs < ctx->num_sms ? superjobs : ctx->num_sms;
-    engine_kernel<Pol, ST><<<grid, kWarps * 32, smem, stream>>>(p);
-    return cuda_check(ctx, cudaGetLastError(), name);
+    // Programmatic dependent launch (TFCUDA_PDL=0 turns it off): this grid's
+    // launch and set-up overlap the preceding kernel's tail; the kernel waits
+    // (griddepcontrol.wait) before reading anything that kernel produced.
+    const char* pdl_env = getenv("TFCUDA_PDL");
+    const bool pdl = !(pdl_env && pdl_env[0] == '0');
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kWarps * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cuda_check(ctx, cudaLaunchKernelEx(&cfg, engine_kernel<Pol, ST>, p), name);
 }
 
 // ---------------------------------------------------------------------------

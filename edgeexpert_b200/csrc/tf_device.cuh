@@ -290,6 +290,15 @@ __device__ __forceinline__ void stage_words(const __half* __restrict__ x, int x_
     }
 }
 
+// Programmatic dependent launch: wait until the preceding kernel in the
+// stream has completed and its memory is visible (returns at once when this
+// kernel was launched without the attribute), and let the next kernel be
+// scheduled onto SMs this grid leaves.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ float gelu_tanh(float x) {
     // gelu_pytorch_tanh with the inner clamp of moe.metal:53-60.
     const float x3 = x * x * x;

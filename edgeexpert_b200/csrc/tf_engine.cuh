@@ -469,6 +469,13 @@ __device__ __forceinline__ void run_phase(const typename Pol::Params& p, EngineS
     uint8_t* stage = smem + (size_t)warp * kStageBytes;
     uint64_t* bar = es.bar;
 
+    // Weights that depend on no earlier kernel (router, plain GEMV) are put in
+    // flight before waiting for the preceding kernel; expert ids and
+    // activations are read only after the wait.
+    if (!Pol::kWeightsIndependent) {
+        if (!Pol::lazy(p)) griddep_wait();
+        griddep_launch_dependents();
+    }
     Pol::stage_pre(p, threadIdx.x);
     __syncthreads();
 
@@ -499,6 +506,10 @@ __device__ __forceinline__ void run_phase(const typename Pol::Params& p, EngineS
     TF_TW(8);
     if (p.aligned && !es.dead) load_next();
     TF_TW(9);
+    if (Pol::kWeightsIndependent) {
+        griddep_wait();
+        griddep_launch_dependents();
+    }
     Pol::stage_x(p, xarea, threadIdx.x, kWarps * 32);
     __syncthreads();
 

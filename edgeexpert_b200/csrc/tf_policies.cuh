@@ -42,6 +42,8 @@ struct GemvParams {
 template <typename ST>
 struct GemvPolicy {
     using Params = GemvParams;
+    static constexpr bool kWeightsIndependent = true;
+    __device__ static bool lazy(const Params&) { return false; }
     // [ntok][ws] words, [ntok][K/64] sums, [ntok][K/64] folded-offset corrections
     static size_t x_bytes(int K, int ntok) {
         return (size_t)ntok * x_words_stride(K) * 4 + 2 * (size_t)ntok * (K / kGroup) * 4;
@@ -170,6 +172,11 @@ struct Phase1Params {
     AffineMat sg, su;
     __half* shared_act;  // [Fs]
     int aligned, x_aligned;
+    // Decode layer only (its predecessor is the router): the shared expert's
+    // jobs come first and start before the router has finished; a routed
+    // unit waits for it (griddepcontrol.wait) and reads its expert id then;
+    // epilogues write only after the wait.
+    int lazy_ids;
     uint32_t* err;
     Sched sched;
 };
@@ -177,9 +184,23 @@ struct Phase1Params {
 template <typename ST>
 struct Phase1Policy {
     using Params = Phase1Params;
+    static constexpr bool kWeightsIndependent = false;
+    __device__ static bool lazy(const Params& p) { return p.lazy_ids != 0; }
     static size_t x_bytes(int D) { return (size_t)x_words_stride(D) * 4 + 2 * (size_t)(D / kGroup) * 4; }
+    // job -> routed job (>= 0) or shared job (>= 0); shared jobs first in lazy mode
+    __device__ static void split(const Params& p, int job, int* rj, int* sj) {
+        const int rjobs = p.top_k * p.fjobs;
+        if (p.lazy_ids) {
+            const int sjobs = p.has_shared ? p.Fs / 8 : 0;
+            *sj = job < sjobs ? job : -1;
+            *rj = job < sjobs ? -1 : job - sjobs;
+        } else {
+            *rj = job < rjobs ? job : -1;
+            *sj = job < rjobs ? -1 : job - rjobs;
+        }
+    }
     __device__ static void stage_pre(const Params& p, int tid) {
-        stage_ids(p.src, p.top_k, tid);
+        if (!p.lazy_ids) stage_ids(p.src, p.top_k, tid);
         if (!p.aligned) return;
         const bool pool = p.src.ids != nullptr;
         const int nm = p.top_k ? (pool ? 1 : p.top_k) : 0;
@@ -204,10 +225,21 @@ struct Phase1Policy {
         d->ntok = 1;
         d->mult = 1.0f;
         d->K = p.D;
-        const int rjobs = p.top_k * p.fjobs;
-        if (job < rjobs) {
-            const int slot = job / p.fjobs, f0 = (job - slot * p.fjobs) * 8;
-            const uint8_t* b = expert_blob(p.src, slot, p.err);
+        int rj, sjb;
+        split(p, job, &rj, &sjb);
+        if (rj >= 0) {
+            const int slot = rj / p.fjobs, f0 = (rj - slot * p.fjobs) * 8;
+            const uint8_t* b;
+            uint32_t eid = 0;
+            if (p.lazy_ids) {
+                griddep_wait();  // the router that writes the ids has finished
+                eid = __ldcg(p.src.ids + slot);
+                b = eid < (uint32_t)p.src.num_experts ? p.src.pool + (size_t)eid * p.src.stride : nullptr;
+                if (!b && p.err) atomicOr(p.err, kErrBadExpert);
+            } else {
+                b = expert_blob(p.src, slot, p.err);
+                if (p.src.ids != nullptr) eid = ids_smem()[slot];
+            }
             d->bits = 4;
             d->rowA = d->rowB = f0;
             d->nA = d->nB = b ? 8 : 0;
@@ -215,7 +247,7 @@ struct Phase1Policy {
             const bool pool = p.src.ids != nullptr;
             d->mapA = &p.map[pool ? 0 : slot];
             d->mapB = &p.map[pool ? 8 : 8 + slot];
-            d->eA = d->eB = pool ? (int)ids_smem()[slot] : 0;
+            d->eA = d->eB = (pool && b) ? (int)eid : 0;
             d->WA = b + p.src.off[0];
             d->SA = b + p.src.off[1];
             d->BA = b + p.src.off[2];
@@ -223,7 +255,7 @@ struct Phase1Policy {
             d->SB = b + p.src.off[4];
             d->BB = b + p.src.off[5];
         } else {
-            const int f0 = (job - rjobs) * 8;
+            const int f0 = sjb * 8;
             d->bits = p.shared_bits;
             d->rowA = d->rowB = f0;
             d->nA = d->nB = 8;
@@ -242,14 +274,16 @@ struct Phase1Policy {
     }
     __device__ static void epilogue(const Params& p, int job, const float f[4], int lane) {
         const int g = lane >> 2, t = lane & 3;
+        if (p.lazy_ids) griddep_wait();  // outputs are written after the router
         if (t != 0) return;  // token 0 lives in column 0: lanes with t == 0
-        const int rjobs = p.top_k * p.fjobs;
-        if (job < rjobs) {
-            const int slot = job / p.fjobs, f0 = (job - slot * p.fjobs) * 8;
+        int rj, sjb;
+        split(p, job, &rj, &sjb);
+        if (rj >= 0) {
+            const int slot = rj / p.fjobs, f0 = (rj - slot * p.fjobs) * 8;
             // routed: g and u stay fp32 (moe.metal:368)
             p.acts[(size_t)slot * p.F + f0 + g] = __float2half_rn(gelu_tanh(f[0]) * f[2]);
         } else {
-            const int f0 = (job - rjobs) * 8;
+            const int f0 = sjb * 8;
             // shared: g and u rounded to half first (gelu_mul_fp16 on half
             // GEMV outputs, utility.metal:6-18; dequant_int8.metal:150-152)
             const float gh = __half2float(__float2half_rn(f[0]));
@@ -289,6 +323,8 @@ struct Phase2Params {
 template <typename ST>
 struct Phase2Policy {
     using Params = Phase2Params;
+    static constexpr bool kWeightsIndependent = false;
+    __device__ static bool lazy(const Params&) { return false; }
     __host__ __device__ static size_t routed_words(int top_k, int F) { return (size_t)top_k * x_words_stride(F); }
     // routed: [top_k][ws] words, [top_k][F/64] sums, [top_k][F/64] corrections;
     // shared (16-byte aligned): [ws] words, [Fs/64] sums, [Fs/64] corrections
@@ -511,6 +547,8 @@ __device__ __forceinline__ void cta_topk_softmax(const float* logits, int E, int
 template <typename ST>
 struct RouterPolicy {
     using Params = RouterParams;
+    static constexpr bool kWeightsIndependent = true;
+    __device__ static bool lazy(const Params&) { return false; }
     static size_t x_bytes(int D) { return (size_t)2 * x_words_stride(D) * 4 + (size_t)2 * (D / kGroup) * 4; }
     __device__ static void stage_pre(const Params& p, int tid) {
         if (tid == 0 && p.aligned) prefetch_tmap(&p.map);
