@@ -217,13 +217,16 @@ __device__ __forceinline__ void compute_unit_b1(const uint8_t* __restrict__ stag
         // four independent MMA chains (one per k-step), summed after the block
         float c[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
         float c2[4] = {0.f, 0.f, 0.f, 0.f}, c3[4] = {0.f, 0.f, 0.f, 0.f};
+        // this lane's row within the swizzled boxes of the block (2 boxes of 4 groups)
+        const int bbase = ((Gb - G0) >> 2) * kBoxBytes + g * kBox;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const int G = Gb + j;
             if (full_block || G < G1) {
                 const uint4* xp = (g == j) ? reinterpret_cast<const uint4*>(sd.xs + (G * 8 + 2 * t) * 4) : zeros;
                 const uint4 x0 = xp[0], x1 = xp[1];
-                const int o = swz(g, (G - G0) * 32 + t * 8);
+                // swz(g, (G - G0) * 32 + t * 8) with the block's part folded into bbase
+                const int o = bbase + (j >> 2) * kBoxBytes + (((((j & 3) * 2 + (t >> 1)) ^ g) & 7) << 4) + (t & 1) * 8;
                 const uint2 wa = *reinterpret_cast<const uint2*>(halfA + o);
                 const uint2 wb = *reinterpret_cast<const uint2*>(halfB + o);
                 uint32_t pa0[4], pa1[4], pb0[4], pb1[4];
@@ -381,11 +384,12 @@ inline int pick_J(int nj, int U, int ctas) {
     return want < 1 ? 1 : (want > jmax ? jmax : want);
 }
 
-inline Sched make_sched(int nj0, int U0, int nj1 = 0, int U1 = 1, int ctas = 148) {
+// j0 > 0 forces the first class's jobs per super-job.
+inline Sched make_sched(int nj0, int U0, int nj1 = 0, int U1 = 1, int ctas = 148, int j0 = 0) {
     Sched s;
     s.nj[0] = nj0;
     s.U[0] = U0;
-    s.J[0] = pick_J(nj0, U0, ctas);
+    s.J[0] = j0 > 0 ? j0 : pick_J(nj0, U0, ctas);
     s.S[0] = nj0 > 0 ? (nj0 + s.J[0] - 1) / s.J[0] : 0;
     s.nj[1] = nj1;
     s.U[1] = U1;
