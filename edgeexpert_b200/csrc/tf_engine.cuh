@@ -483,13 +483,13 @@ __device__ __forceinline__ void run_phase(const typename Pol::Params& p, EngineS
     Pol::stage_pre(p, threadIdx.x);
     __syncthreads();
 
-    const int S = p.sched.S_total;
+    const int S = Pol::superjobs(p);
 
     // Load cursor: same unit sequence as the compute loop below.
     int l_sj = blockIdx.x, l_i = 0;
     auto load_next = [&]() -> void {
         while (l_sj < S) {
-            const SuperJob sj = decode_superjob(p.sched, l_sj);
+            const SuperJob sj = Pol::superjob(p, l_sj);
             const int v = warp_unit(sj, warp, l_i);
             if (v < 0) {
                 l_sj += gridDim.x;
@@ -518,7 +518,11 @@ __device__ __forceinline__ void run_phase(const typename Pol::Params& p, EngineS
     __syncthreads();
 
     for (int sjx = blockIdx.x; sjx < S; sjx += gridDim.x) {
-        const SuperJob sj = decode_superjob(p.sched, sjx);
+        const SuperJob sj = Pol::superjob(p, sjx);
+        if (Pol::kStagePerSuperjob) {  // activations differ per super-job (grouped experts)
+            Pol::stage_x_sj(p, sj, xarea, threadIdx.x, kWarps * 32);
+            __syncthreads();
+        }
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         for (int i = 0;; ++i) {
             const int v = warp_unit(sj, warp, i);

@@ -43,6 +43,11 @@ template <typename ST>
 struct GemvPolicy {
     using Params = GemvParams;
     static constexpr bool kWeightsIndependent = true;
+    // engine hooks: schedule from the host Sched, activations staged once per CTA
+    static constexpr bool kStagePerSuperjob = false;
+    __device__ static int superjobs(const Params& p) { return p.sched.S_total; }
+    __device__ static SuperJob superjob(const Params& p, int sjx) { return decode_superjob(p.sched, sjx); }
+    __device__ static void stage_x_sj(const Params&, const SuperJob&, uint8_t*, int, int) {}
     __device__ static bool lazy(const Params&) { return false; }
     // [ntok][ws] words, [ntok][K/64] sums, [ntok][K/64] folded-offset corrections
     static size_t x_bytes(int K, int ntok) {
@@ -185,6 +190,11 @@ template <typename ST>
 struct Phase1Policy {
     using Params = Phase1Params;
     static constexpr bool kWeightsIndependent = false;
+    // engine hooks: schedule from the host Sched, activations staged once per CTA
+    static constexpr bool kStagePerSuperjob = false;
+    __device__ static int superjobs(const Params& p) { return p.sched.S_total; }
+    __device__ static SuperJob superjob(const Params& p, int sjx) { return decode_superjob(p.sched, sjx); }
+    __device__ static void stage_x_sj(const Params&, const SuperJob&, uint8_t*, int, int) {}
     __device__ static bool lazy(const Params& p) { return p.lazy_ids != 0; }
     static size_t x_bytes(int D) { return (size_t)x_words_stride(D) * 4 + 2 * (size_t)(D / kGroup) * 4; }
     // job -> routed job (>= 0) or shared job (>= 0); shared jobs first in lazy mode
@@ -324,6 +334,11 @@ template <typename ST>
 struct Phase2Policy {
     using Params = Phase2Params;
     static constexpr bool kWeightsIndependent = false;
+    // engine hooks: schedule from the host Sched, activations staged once per CTA
+    static constexpr bool kStagePerSuperjob = false;
+    __device__ static int superjobs(const Params& p) { return p.sched.S_total; }
+    __device__ static SuperJob superjob(const Params& p, int sjx) { return decode_superjob(p.sched, sjx); }
+    __device__ static void stage_x_sj(const Params&, const SuperJob&, uint8_t*, int, int) {}
     __device__ static bool lazy(const Params&) { return false; }
     __host__ __device__ static size_t routed_words(int top_k, int F) { return (size_t)top_k * x_words_stride(F); }
     // routed: [top_k][ws] words, [top_k][F/64] sums, [top_k][F/64] corrections;
@@ -548,6 +563,11 @@ template <typename ST>
 struct RouterPolicy {
     using Params = RouterParams;
     static constexpr bool kWeightsIndependent = true;
+    // engine hooks: schedule from the host Sched, activations staged once per CTA
+    static constexpr bool kStagePerSuperjob = false;
+    __device__ static int superjobs(const Params& p) { return p.sched.S_total; }
+    __device__ static SuperJob superjob(const Params& p, int sjx) { return decode_superjob(p.sched, sjx); }
+    __device__ static void stage_x_sj(const Params&, const SuperJob&, uint8_t*, int, int) {}
     __device__ static bool lazy(const Params&) { return false; }
     static size_t x_bytes(int D) { return (size_t)2 * x_words_stride(D) * 4 + (size_t)2 * (D / kGroup) * 4; }
     __device__ static void stage_pre(const Params& p, int tid) {
@@ -631,6 +651,248 @@ struct RouterPolicy {
             __threadfence();
             warp_topk_softmax(p.logits, p.E, p.top_k, p.per_expert_scale, p.out_idx, p.out_w, lane);
             if (lane == 0) *p.ticket = 0u;
+        }
+    }
+};
+
+
+// ===========================================================================
+// Grouped routed experts on the streaming engine (small token counts per
+// expert: batched decode).  The device grouping (tf_moe_route_sort) gives,
+// per non-empty expert, a contiguous range of sorted pairs; the range is cut
+// into passes of at most `nt` tokens and each (group, pass) is one super-job
+// whose token rows are staged once (kStagePerSuperjob).  MODE 0: gate/up rows
+// of the expert with GELU(g)*u per token -> acts[pair][f] (sorted-pair order);
+// MODE 1: down rows -> route_partials[(token*top_k + rank)][d].  Same
+// arithmetic as prefill_grouped_routed_moe_batched_phase1/_down
+// (prefill.metal:336-440, 598-670): g and u fp32, act and partial rounded to
+// fp16.
+// ===========================================================================
+struct GroupedParams {
+    CUtensorMap map[3];  // gate_w, up_w, down_w of all experts: [E][rows][row_bytes]
+    const uint8_t* pool;
+    unsigned long long stride;
+    uint32_t off[9];
+    int E, D, F, top_k, nt;  // nt: tokens per pass
+    const tf_moe_group* groups;
+    const uint32_t* n_groups;
+    const tf_token_expert_pair* pairs;
+    const __half* hidden;  // MODE 0 input rows, gathered through the pairs
+    int hstride;
+    __half* acts;      // [pairs][F] sorted order (MODE 0 out, MODE 1 in)
+    __half* partials;  // [T*top_k][D] (MODE 1 out)
+    int aligned;
+    uint32_t* err;
+    Sched sched;  // unused: the schedule comes from the device groups
+};
+
+struct GroupTab {
+    int ng, passes, staged_pass;
+    int prefix[257];  // passes before group g
+    int start[256], count[256], expert[256];
+};
+__device__ __forceinline__ GroupTab& group_tab() {
+    __shared__ GroupTab t;
+    return t;
+}
+
+// Work decomposition: pass = (group, up to nt of its tokens); each pass has
+// jobs_per row jobs (8 gate+up rows, or 16 down rows) cut into chunks of
+// kWarps / U jobs, so a super-job's units fit the engine's one-round
+// reduction.  Super-jobs are numbered so that a CTA's consecutive super-jobs
+// are consecutive chunks (usually of one pass): the pass's token rows are
+// staged once per CTA per pass.
+template <typename ST, int MODE>
+struct GroupedPolicy {
+    using Params = GroupedParams;
+    static constexpr bool kWeightsIndependent = false;
+    __device__ static bool lazy(const Params&) { return false; }
+    static constexpr bool kStagePerSuperjob = true;
+    __host__ __device__ static int kdim(const Params& p) { return MODE == 0 ? p.D : p.F; }
+    __host__ __device__ static int jobs_per(const Params& p) { return MODE == 0 ? p.F / 8 : (p.D + 15) / 16; }
+    __host__ __device__ static int units(const Params& p) { return units_for_K(kdim(p), 4); }
+    __host__ __device__ static int chunk_jobs(const Params& p) { return max(1, kWarps / units(p)); }
+    __host__ __device__ static int chunks(const Params& p) {
+        return (jobs_per(p) + chunk_jobs(p) - 1) / chunk_jobs(p);
+    }
+    static size_t x_bytes(int K, int ntok) {
+        return (size_t)ntok * x_words_stride(K) * 4 + 2 * (size_t)ntok * (K / kGroup) * 4;
+    }
+    __device__ static void stage_pre(const Params& p, int tid) {
+        GroupTab& tb = group_tab();
+        if (tid < 32) {
+            const int lane = tid;
+            const int ng = min((int)__ldcg(p.n_groups), 256);
+            int cnt[8], run = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int g = lane * 8 + j;
+                int ps = 0;
+                if (g < ng) {
+                    const tf_moe_group gr = p.groups[g];
+                    tb.start[g] = (int)gr.pair_start;
+                    tb.count[g] = (int)gr.pair_count;
+                    tb.expert[g] = (int)gr.expert;
+                    if (gr.expert < (uint32_t)p.E)
+                        ps = ((int)gr.pair_count + p.nt - 1) / p.nt;
+                    else if (p.err)
+                        atomicOr(p.err, kErrBadExpert);
+                }
+                cnt[j] = ps;
+                run += ps;
+            }
+            int incl = run;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            int acc = incl - run;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int g = lane * 8 + j;
+                if (g <= ng) tb.prefix[g] = acc;
+                acc += cnt[j];
+            }
+            if (lane == 31) {
+                tb.passes = incl;
+                if (ng == 256) tb.prefix[256] = incl;
+            }
+            if (lane == 0) {
+                tb.ng = ng;
+                tb.staged_pass = -1;
+            }
+        } else if (p.aligned && tid == 32) {
+            prefetch_tmap(&p.map[MODE == 0 ? 0 : 2]);
+            if (MODE == 0) prefetch_tmap(&p.map[1]);
+        }
+    }
+    __device__ static void stage_x(const Params&, uint8_t*, int, int) {}  // per pass instead
+    __device__ static int per_cta(const Params& p) {
+        const int W = group_tab().passes * chunks(p);
+        return (W + (int)gridDim.x - 1) / (int)gridDim.x;
+    }
+    __device__ static int superjobs(const Params& p) { return per_cta(p) * (int)gridDim.x; }
+    // engine index sjx (CTA sjx % grid, its (sjx / grid)-th super-job) ->
+    // CTA-contiguous work index -> (pass, chunk); jobs are numbered
+    // pass * jobs_per + row job.  J = 0 marks an index past the work.
+    __device__ static SuperJob superjob(const Params& p, int sjx) {
+        SuperJob s;
+        s.U = units(p);
+        const int G = (int)gridDim.x;
+        const int L = (sjx % G) * per_cta(p) + sjx / G;
+        const int C = chunks(p), CJ = chunk_jobs(p), JP = jobs_per(p);
+        if (L >= group_tab().passes * C) {
+            s.j0 = s.j1 = 0;
+            s.J = 0;
+            return s;
+        }
+        const int pass = L / C, ch = L - pass * C;
+        const int l0 = ch * CJ, l1 = min(JP, l0 + CJ);
+        s.j0 = pass * JP + l0;
+        s.j1 = pass * JP + l1;
+        s.J = l1 - l0;
+        return s;
+    }
+    // pass -> expert, first pair, tokens of the pass
+    __device__ static void locate(const Params& p, int pass, int* e, int* pair0, int* ntok) {
+        const GroupTab& tb = group_tab();
+        int lo = 0, hi = tb.ng - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (tb.prefix[mid] <= pass) lo = mid; else hi = mid - 1;
+        }
+        const int k = pass - tb.prefix[lo];
+        *e = tb.expert[lo];
+        *pair0 = tb.start[lo] + k * p.nt;
+        *ntok = min(p.nt, tb.count[lo] - k * p.nt);
+    }
+    __device__ static void stage_x_sj(const Params& p, const SuperJob& sj, uint8_t* xa, int tid, int nt) {
+        if (sj.J == 0) return;
+        GroupTab& tb = group_tab();
+        const int pass = sj.j0 / jobs_per(p);
+        if (pass == tb.staged_pass) return;  // uniform: written only after the barrier below
+        int e, p0, ntok;
+        locate(p, pass, &e, &p0, &ntok);
+        const int K = kdim(p), ws = x_words_stride(K);
+        uint32_t* xs = reinterpret_cast<uint32_t*>(xa);
+        float* xsum = reinterpret_cast<float*>(xs + p.nt * ws);
+        float* xcorr = xsum + p.nt * (K / kGroup);
+        if (MODE == 0) {
+            for (int t = 0; t < ntok; ++t) {
+                const uint32_t row = p.pairs[p0 + t].token;
+                stage_words(p.hidden + (size_t)row * p.hstride, p.hstride, 1, K, xs + t * ws, true, false, tid, nt);
+            }
+        } else {
+            stage_words(p.acts + (size_t)p0 * p.F, p.F, ntok, K, xs, true, false, tid, nt);
+        }
+        __syncthreads();
+        stage_xsum_smem(xs, ws, ntok, K, xsum, xcorr, false, tid, nt);
+        if (tid == 0) tb.staged_pass = pass;
+    }
+    __device__ static bool unit(const Params& p, int job, int u, SegDesc* d, int* chunk) {
+        const int JP = jobs_per(p);
+        const int pass = job / JP, local = job - pass * JP;
+        int e, p0, ntok;
+        locate(p, pass, &e, &p0, &ntok);
+        const uint8_t* b = p.pool + (size_t)e * p.stride;
+        const int K = kdim(p);
+        d->K = K;
+        d->bits = 4;
+        d->eA = d->eB = e;
+        if (MODE == 0) {
+            d->rowA = d->rowB = local * 8;
+            d->nA = d->nB = 8;
+            d->mapA = &p.map[0];
+            d->mapB = &p.map[1];
+            d->WA = b + p.off[0];
+            d->SA = b + p.off[1];
+            d->BA = b + p.off[2];
+            d->WB = b + p.off[3];
+            d->SB = b + p.off[4];
+            d->BB = b + p.off[5];
+        } else {
+            d->rowA = local * 16;
+            d->rowB = d->rowA + 8;
+            d->nA = max(0, min(8, p.D - d->rowA));
+            d->nB = max(0, min(8, p.D - d->rowB));
+            d->mapA = d->mapB = &p.map[2];
+            d->WA = d->WB = b + p.off[6];
+            d->SA = d->SB = b + p.off[7];
+            d->BA = d->BB = b + p.off[8];
+        }
+        const uint32_t* xs = reinterpret_cast<const uint32_t*>(engine_xarea());
+        const int ws = x_words_stride(K);
+        d->xs = xs;
+        d->xsum = reinterpret_cast<const float*>(xs + p.nt * ws);
+        d->xcorr = d->xsum + p.nt * (K / kGroup);
+        d->xfold = 0;
+        d->xws = ws;
+        d->ntok = ntok;
+        d->mult = 1.0f;
+        *chunk = u;
+        return true;
+    }
+    __device__ static void epilogue(const Params& p, int job, const float f[4], int lane) {
+        const int JP = jobs_per(p);
+        const int pass = job / JP, local = job - pass * JP;
+        int e, p0, ntok;
+        locate(p, pass, &e, &p0, &ntok);
+        const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int tok = 2 * t + j;
+            if (tok >= ntok) continue;
+            if (MODE == 0) {
+                // rows A = gate f0+g, rows B = up f0+g; g and u stay fp32
+                p.acts[(size_t)(p0 + tok) * p.F + local * 8 + g] = __float2half_rn(gelu_tanh(f[j]) * f[2 + j]);
+            } else {
+                const tf_token_expert_pair pr = p.pairs[p0 + tok];
+                __half* out = p.partials + ((size_t)pr.token * p.top_k + pr.rank) * p.D;
+                const int r0 = local * 16 + g, r1 = r0 + 8;
+                if (r0 < p.D) out[r0] = __float2half_rn(f[j]);
+                if (r1 < p.D) out[r1] = __float2half_rn(f[2 + j]);
+            }
         }
     }
 };

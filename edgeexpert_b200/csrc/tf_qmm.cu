@@ -760,6 +760,31 @@ bool dense_weights(QmmParams& p, CUtensorMap* m, const void* w, uint32_t rows, u
 
 }  // namespace
 
+namespace {
+
+// Grouped routed experts on the streaming engine (few tokens per expert):
+// gate/up (MODE 0) then down (MODE 1), one super-job per (expert, token pass).
+template <typename ST>
+tf_status grouped_gemv(tf_context* ctx, GroupedParams p, cudaStream_t s, const char* name) {
+    auto launch = [&](auto pol_tag) -> tf_status {
+        using Pol = decltype(pol_tag);
+        const int K = Pol::kdim(p);
+        const size_t limit = engine_smem_limit<Pol, ST>(ctx);
+        int nt = 8;
+        while (nt > 1 && engine_fixed_smem() + Pol::x_bytes(K, nt) + 1024 > limit) --nt;
+        if (engine_fixed_smem() + Pol::x_bytes(K, nt) + 1024 > limit)
+            return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: hidden size too large for the engine", name);
+        GroupedParams q = p;
+        q.nt = nt;
+        return launch_engine<Pol, ST>(ctx, q, Pol::x_bytes(K, nt), ctx->num_sms, s, name);
+    };
+    tf_status rc = launch(GroupedPolicy<ST, 0>{});
+    if (rc != TF_OK) return rc;
+    return launch(GroupedPolicy<ST, 1>{});
+}
+
+}  // namespace
+
 extern "C" {
 
 tf_status tf_int4_qmm(tf_context* ctx, const void* weights, const void* scales, const void* biases, const void* x,
@@ -872,6 +897,37 @@ tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64_t expe
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const uint32_t P = t * top_k;
     const uint8_t* pb = static_cast<const uint8_t*>(pool);
+    // Few tokens per expert (batched decode): the streaming engine reads each
+    // hit expert's weights once with up to 8 tokens per MMA column block; many
+    // (prefill): the tcgen05 GEMMs.  TFCUDA_GROUPED=gemv|gemm forces one.
+    const char* env = getenv("TFCUDA_GROUPED");
+    bool gemv = (uint64_t)P <= 12ull * num_experts;
+    if (env && env[0] == 'g' && env[1] == 'e' && env[2] == 'm') gemv = env[3] == 'v';
+    if (gemv) {
+        GroupedParams g{};
+        bool ok = make_weight_map(&g.map[0], pb + off->gate_w, d / 2, f, num_experts, expert_stride) &&
+                  make_weight_map(&g.map[1], pb + off->up_w, d / 2, f, num_experts, expert_stride) &&
+                  make_weight_map(&g.map[2], pb + off->down_w, f / 2, d, num_experts, expert_stride);
+        g.aligned = ok ? 1 : 0;
+        g.pool = pb;
+        g.stride = expert_stride;
+        const uint32_t o9[9] = {off->gate_w, off->gate_s, off->gate_b, off->up_w, off->up_s,
+                                off->up_b,   off->down_w, off->down_s, off->down_b};
+        for (int i = 0; i < 9; ++i) g.off[i] = o9[i];
+        g.E = (int)num_experts;
+        g.D = (int)d;
+        g.F = (int)f;
+        g.top_k = (int)top_k;
+        g.groups = static_cast<const tf_moe_group*>(groups);
+        g.n_groups = static_cast<const uint32_t*>(n_groups);
+        g.pairs = static_cast<const tf_token_expert_pair*>(sorted_pairs);
+        g.hidden = static_cast<const __half*>(hidden);
+        g.hstride = (int)hidden_stride;
+        g.acts = static_cast<__half*>(act_scratch);
+        g.partials = static_cast<__half*>(route_partials);
+        g.err = ctx->d_err;
+        return st == TF_SCALE_BF16 ? grouped_gemv<__nv_bfloat16>(ctx, g, s, name) : grouped_gemv<__half>(ctx, g, s, name);
+    }
     QmmParams p{};
     p.mode = kGroupedGateUp;
     p.K = (int)d;
