@@ -41,7 +41,8 @@ D, F, FS, E, TOPK = 2816, 704, 2112, 128, 8
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=0,
+                    help="timed steps (default per workload: a timed region of about half a second)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=30)
@@ -76,7 +77,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except (OSError, FileNotFoundError):
@@ -894,8 +895,13 @@ def run_chunk(a, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
+DEFAULT_STEPS = {"decode": 400, "gemv": 3000, "batched": 1000, "prefill": 300, "ep": 200}
+
+
 def main():
     a = parse()
+    if a.steps <= 0:
+        a.steps = DEFAULT_STEPS[a.workload]
     if a.scale_dtype is None:
         a.scale_dtype = "f16" if a.workload == "gemv" else "bf16"
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -41,13 +41,28 @@ __global__ void __launch_bounds__(kRtThreads) prefill_router_kernel(
     const int ntok = min(kRtTok, T - t0);
 
     // stage hi/lo (columns 2t, 2t+1) in octet-pair order
+    const bool hvec = ((reinterpret_cast<uintptr_t>(H) | reinterpret_cast<uintptr_t>(es)) & 15u) == 0 &&
+                      (hstride & 7) == 0;
     for (int i = tid; i < kRtTok * (D / 8); i += blockDim.x) {
         const int t = i / (D / 8), q = i - t * (D / 8);
+        __half hv[8];
+        __nv_bfloat16 ev[8];
+        if (t < ntok && hvec) {
+            const uint4 hr = __ldg(reinterpret_cast<const uint4*>(H + (size_t)(t0 + t) * hstride + q * 8));
+            const uint4 er = __ldg(reinterpret_cast<const uint4*>(es + q * 8));
+            memcpy(hv, &hr, 16);
+            memcpy(ev, &er, 16);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                hv[j] = t < ntok ? H[(size_t)(t0 + t) * hstride + q * 8 + j] : __float2half(0.f);
+                ev[j] = es[q * 8 + j];
+            }
+        }
         __half hi[8], lo[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            const int k = q * 8 + j;
-            const float xt = t < ntok ? __half2float(H[(size_t)(t0 + t) * hstride + k]) * __bfloat162float(es[k]) : 0.f;
+            const float xt = t < ntok ? __half2float(hv[j]) * __bfloat162float(ev[j]) : 0.f;
             hi[j] = __float2half_rn(xt);
             lo[j] = __float2half_rn(xt - __half2float(hi[j]));
         }
@@ -81,18 +96,28 @@ __global__ void __launch_bounds__(kRtThreads) prefill_router_kernel(
         float accA[kRtCG], accB[kRtCG];  // (row g, token 4c+t), (row g+8, token 4c+t)
 #pragma unroll
         for (int c = 0; c < kRtCG; ++c) accA[c] = accB[c] = 0.f;
+        // software pipeline: the next group's weights and scales are loaded
+        // (from L2) while the current group's MMAs run
+        auto ldw = [&](int G, uint4& qa, uint4& qb, float sc[4]) {
+            qa = __ldg(reinterpret_cast<const uint4*>(wA + G * 64 + t * 16));
+            qb = __ldg(reinterpret_cast<const uint4*>(wB + G * 64 + t * 16));
+            sc[0] = va ? scale_to_float(S[(size_t)rA * ng + G]) : 0.f;
+            sc[1] = va ? scale_to_float(B[(size_t)rA * ng + G]) : 0.f;
+            sc[2] = vb ? scale_to_float(S[(size_t)rB * ng + G]) : 0.f;
+            sc[3] = vb ? scale_to_float(B[(size_t)rB * ng + G]) : 0.f;
+        };
+        uint4 qa, qb;
+        float sc[4];
+        ldw(0, qa, qb, sc);
         for (int G = 0; G < ng; ++G) {
-            const uint4 qa = __ldg(reinterpret_cast<const uint4*>(wA + G * 64 + t * 16));
-            const uint4 qb = __ldg(reinterpret_cast<const uint4*>(wB + G * 64 + t * 16));
+            uint4 nqa = qa, nqb = qb;
+            float nsc[4] = {0.f, 0.f, 0.f, 0.f};
+            if (G + 1 < ng) ldw(G + 1, nqa, nqb, nsc);
             uint32_t pa0[4], pa1[4], pb0[4], pb1[4];
             dq8(qa.x, qa.y, pa0);
             dq8(qa.z, qa.w, pa1);
             dq8(qb.x, qb.y, pb0);
             dq8(qb.z, qb.w, pb1);
-            const float sa = va ? scale_to_float(S[(size_t)rA * ng + G]) : 0.f;
-            const float ba = va ? scale_to_float(B[(size_t)rA * ng + G]) : 0.f;
-            const float sb = vb ? scale_to_float(S[(size_t)rB * ng + G]) : 0.f;
-            const float bb = vb ? scale_to_float(B[(size_t)rB * ng + G]) : 0.f;
 #pragma unroll
             for (int cg = 0; cg < kRtCG; ++cg) {
                 // B fragment: column g of group cg = token 4cg + g/2, part g%2
@@ -105,11 +130,15 @@ __global__ void __launch_bounds__(kRtThreads) prefill_router_kernel(
                 mma16816(cb, pa1[2], pb1[2], pa1[3], pb1[3], x1.z, x1.w);
                 const float xsm = xsum[(4 * cg + t) * ng + G];
                 // columns 2t (hi) and 2t+1 (lo) of this lane are token 4cg + t
-                accA[cg] = fmaf(sa, (c[0] + cb[0]) + (c[1] + cb[1]), accA[cg]);
-                accA[cg] = fmaf(ba, xsm, accA[cg]);
-                accB[cg] = fmaf(sb, (c[2] + cb[2]) + (c[3] + cb[3]), accB[cg]);
-                accB[cg] = fmaf(bb, xsm, accB[cg]);
+                accA[cg] = fmaf(sc[0], (c[0] + cb[0]) + (c[1] + cb[1]), accA[cg]);
+                accA[cg] = fmaf(sc[1], xsm, accA[cg]);
+                accB[cg] = fmaf(sc[2], (c[2] + cb[2]) + (c[3] + cb[3]), accB[cg]);
+                accB[cg] = fmaf(sc[3], xsm, accB[cg]);
             }
+            qa = nqa;
+            qb = nqb;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sc[i] = nsc[i];
         }
 #pragma unroll
         for (int cg = 0; cg < kRtCG; ++cg) {
