@@ -114,6 +114,14 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU arm ---
+def host_threads() -> int:
+    """All host threads this process may use (torchrun sets OMP_NUM_THREADS=1
+    per rank; the CPU baseline passes its thread count explicitly instead)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
 def cpu_sample(seconds: float, label: str = "cpu"):
     """Oracle port of the reference CPU math on the host cores: router + top-8
     + 8 routed experts + shared expert for one token of one config-1 layer,
@@ -122,7 +130,7 @@ def cpu_sample(seconds: float, label: str = "cpu"):
     import numpy as np
 
     import oracle as O
-    threads = O.lib().orc_max_threads()
+    threads = host_threads()
     rng = O.seed_tree(0, f"bench-{label}")
     W8, S8, B8 = rng.synthetic_affine(E, D, 8, 0)
     es = O.bf16_bits(np.full(D, D ** -0.5, np.float32))
@@ -404,7 +412,7 @@ def gemv_cpu_sample(seconds: float):
     """Oracle port of the reference's int4 GEMV (kernel order) on the host cores."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle as O
-    threads = O.lib().orc_max_threads()
+    threads = host_threads()
     rng = O.seed_tree(0, "bench-gemv")
     W, S, B = rng.synthetic_affine(G_M, G_N, 4, 1)
     x = rng.normal_f16(G_N)

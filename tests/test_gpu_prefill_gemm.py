@@ -212,3 +212,28 @@ def test_grouped_routed_empty_routes(cuda, path, monkeypatch):
                                      act, part, 0, K)
     torch.cuda.synchronize()
     assert bool((part == 3.0).all())
+
+
+def test_prefill_argument_validation(cuda):
+    """Contract violations return a status (the reference traps); nothing launches."""
+    from edgeexpert_b200._lib import TFError
+    W = torch.zeros(128, 64, dtype=torch.uint8, device="cuda")
+    S = torch.zeros(128, 2, dtype=torch.bfloat16, device="cuda")
+    X = torch.zeros(4, 128, dtype=torch.float16, device="cuda")
+    Y = torch.zeros(4, 128, dtype=torch.float16, device="cuda")
+    q = PrefillInt4QMM()
+    with pytest.raises(TFError) as ei:
+        q.encode(W, S, S, X, Y, 4, 128, 100)  # k % 64 != 0
+    assert ei.value.status == 3
+    with pytest.raises(TFError) as ei:
+        q.encode(W, S, S, X, Y, 4, 128, 128, x_stride=100)  # stride not a multiple of 8
+    assert ei.value.status == 3
+    Xu = torch.zeros(4 * 128 + 1, dtype=torch.float16, device="cuda")[1:].view(4, 128)  # 2-byte aligned only
+    with pytest.raises(TFError) as ei:
+        q.encode(W, S, S, Xu, Y, 4, 128, 128)
+    assert ei.value.status == 2
+    # T = 0: nothing to do
+    q.encode(W, S, S, X, Y, 0, 128, 128)
+    with pytest.raises(TFError) as ei:
+        PrefillMoE.encode_reduce_token_major(Y, Y, Y, 4, 8, 100)  # d % 8 != 0
+    assert ei.value.status == 3
