@@ -290,6 +290,60 @@ __device__ __forceinline__ void stage_words(const __half* __restrict__ x, int x_
     }
 }
 
+// ---- integer activation layout for the batch-1 int4 path ---------------------
+// One token row staged for mma.sync m16n8k32 u8 x s8: per 64-group g,
+// m = max|x|, X = rint(x * 16383 / m) (15 bits), X = 128*hi + lo with
+// hi in [-128, 127], lo in [0, 127]; xsc[g] = m / 16383, xsum[g] = sum x.
+// Bytes of group g at xs + 128 g: four 32-byte lane blocks t' (elements
+// 16t'..16t'+15), each [hi W0 W1 W2 W3][lo W0 W1 W2 W3] with
+// W0 = elements 16t'+{0,2,4,6}, W1 = +{1,3,5,7}, W2 = +{8,10,12,14},
+// W3 = +{9,11,13,15}: the B-fragment order that matches weight bytes
+// unpacked as (w & 0x0F0F0F0F, (w >> 4) & 0x0F0F0F0F).
+__device__ __forceinline__ int x8_offset(int e) {
+    const int tq = e >> 4, w = e & 15;
+    const int word = (w >= 8 ? 2 : 0) + (w & 1), byte = (w & 7) >> 1;
+    return tq * 32 + word * 4 + byte;
+}
+
+__device__ __forceinline__ void stage_x_int(const __half* __restrict__ x, int K, uint32_t* xs, float* xsum, float* xsc,
+                                            int tid, int nthreads) {
+    const int ng = K / kGroup;
+    const int warp = tid >> 5, lane = tid & 31, nw = nthreads >> 5;
+    uint8_t* xb = reinterpret_cast<uint8_t*>(xs);
+    for (int g = warp; g < ng; g += nw) {
+        const float a = __half2float(__ldcg(x + g * 64 + 2 * lane));
+        const float b = __half2float(__ldcg(x + g * 64 + 2 * lane + 1));
+        float m = fmaxf(fabsf(a), fabsf(b)), sum = a + b;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        }
+        const float q = m > 0.f ? 16383.0f / m : 0.f;
+        const int XA = __float2int_rn(a * q), XB = __float2int_rn(b * q);
+        uint8_t* gb = xb + g * 128;
+        const int e0 = 2 * lane, e1 = e0 + 1;
+        gb[x8_offset(e0)] = (uint8_t)(XA >> 7);
+        gb[x8_offset(e0) + 16] = (uint8_t)(XA & 127);
+        gb[x8_offset(e1)] = (uint8_t)(XB >> 7);
+        gb[x8_offset(e1) + 16] = (uint8_t)(XB & 127);
+        if (lane == 0) {
+            xsum[g] = sum;
+            xsc[g] = m / 16383.0f;
+        }
+    }
+}
+
+// D += A(u8, 16x32) * B(s8, 32x8), int32 accumulate
+__device__ __forceinline__ void imma16832(int c[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                          uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 // Programmatic dependent launch: wait until the preceding kernel in the
 // stream has completed and its memory is visible (returns at once when this
 // kernel was launched without the attribute), and let the next kernel be

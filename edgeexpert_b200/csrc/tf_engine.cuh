@@ -69,7 +69,8 @@ struct SegDesc {
     const uint32_t* xs;  // staged activation (octet-pair layout), token 0
     const float* xsum;   // per-group sums, token 0
     const float* xcorr;  // folded staging: 1024 * sum of staged values per group
-    int xfold;           // xs staged with odd pairs divided by 16 (stage_words fold)
+    int xfold;           // 1: xs staged with odd pairs divided by 16 (stage_words fold);
+                         // 2: integer layout (stage_x_int), xcorr holds the per-group x scale
     int xws;             // words between tokens in xs
     int ntok;            // tokens (MMA columns) carried by xs
     float mult;          // multiplier applied to this seg's contribution
@@ -250,6 +251,78 @@ __device__ __forceinline__ void compute_unit_b1(const uint8_t* __restrict__ stag
                 const float corr = sd.xcorr[G], xsm = sd.xsum[G];
                 if (va) accA += scale_to_float(sA[G]) * (c[h] - corr) + scale_to_float(bA[G]) * xsm;
                 if (vb) accB += scale_to_float(sB[G]) * (c[2 + h] - corr) + scale_to_float(bB[G]) * xsm;
+            }
+        }
+    };
+    int Gb = G0;
+    for (; Gb + 8 <= G1; Gb += 8) block(Gb, true);
+    if (Gb < G1) block(Gb, false);
+    accA += __shfl_xor_sync(0xffffffffu, accA, 1);
+    accA += __shfl_xor_sync(0xffffffffu, accA, 2);
+    accB += __shfl_xor_sync(0xffffffffu, accB, 1);
+    accB += __shfl_xor_sync(0xffffffffu, accB, 2);
+    out[0] = accA;
+    out[1] = 0.f;
+    out[2] = accB;
+    out[3] = 0.f;
+}
+
+// Batch-1 int4 path on the integer tensor path: weight codes unpacked to
+// bytes (w & 0x0F0F0F0F, (w >> 4) & 0x0F0F0F0F) times the 15-bit activation
+// split in two int8 halves, exact int32 sums per group; groups in the MMA N
+// dimension as in compute_unit_b1.  y = sum_g s_g * xsc_g * (128 hi + lo) + b_g * xsum_g.
+template <typename ST>
+__device__ __forceinline__ void compute_unit_b1_int(const uint8_t* __restrict__ stage, const SegDesc& sd, int chunk,
+                                                    float out[4], int lane, const uint4* zeros) {
+    const int g = lane >> 2, t = lane & 3;
+    const int ngK = sd.K / kGroup;
+    constexpr int kGPU = kMaxBoxes * kBox / 32;  // 24 groups per unit
+    const int G0 = chunk * kGPU;
+    const int G1 = min(ngK, G0 + kGPU);
+    const bool va = g < sd.nA, vb = g < sd.nB;
+    const bool full = ngK <= kMaxScaleGroups;
+    const int sstride = full ? ngK : kGPU;
+    const int sbase = full ? 0 : G0;
+    const ST* scl = reinterpret_cast<const ST*>(stage + 2 * kHalfBytes) - sbase;
+    const ST* sA = scl + g * sstride;
+    const ST* bA = scl + kScaleArr / 2 + g * sstride;
+    const ST* sB = scl + 2 * (kScaleArr / 2) + g * sstride;
+    const ST* bB = scl + 3 * (kScaleArr / 2) + g * sstride;
+    const uint8_t* halfA = stage;
+    const uint8_t* halfB = stage + kHalfBytes;
+    const uint8_t* xb = reinterpret_cast<const uint8_t*>(sd.xs);
+    constexpr uint32_t kLo = 0x0F0F0F0Fu;
+    float accA = 0.f, accB = 0.f;
+    auto block = [&](const int Gb, const bool full_block) {
+        int h0[4] = {0, 0, 0, 0}, h1[4] = {0, 0, 0, 0}, l0[4] = {0, 0, 0, 0}, l1[4] = {0, 0, 0, 0};
+        const int bbase = ((Gb - G0) >> 2) * kBoxBytes + g * kBox;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int G = Gb + j;
+            if (full_block || G < G1) {
+                const uint4* xp = (g == j) ? reinterpret_cast<const uint4*>(xb + (G * 4 + t) * 32) : zeros;
+                const uint4 xh = xp[0], xl = xp[1];
+                const int o = bbase + (j >> 2) * kBoxBytes + (((((j & 3) * 2 + (t >> 1)) ^ g) & 7) << 4) + (t & 1) * 8;
+                const uint2 wa = *reinterpret_cast<const uint2*>(halfA + o);
+                const uint2 wb = *reinterpret_cast<const uint2*>(halfB + o);
+                const uint32_t a0 = wa.x & kLo, a1 = (wa.x >> 4) & kLo, a2 = wa.y & kLo, a3 = (wa.y >> 4) & kLo;
+                const uint32_t b0 = wb.x & kLo, b1 = (wb.x >> 4) & kLo, b2 = wb.y & kLo, b3 = (wb.y >> 4) & kLo;
+                imma16832(h0, a0, b0, a1, b1, xh.x, xh.y);
+                imma16832(h1, a2, b2, a3, b3, xh.z, xh.w);
+                imma16832(l0, a0, b0, a1, b1, xl.x, xl.y);
+                imma16832(l1, a2, b2, a3, b3, xl.z, xl.w);
+            }
+        }
+        // this lane's columns: groups Gb + 2t (elements 0, 2) and Gb + 2t + 1 (1, 3)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int G = Gb + 2 * t + h;
+            if (full_block || G < G1) {
+                const float xsc = sd.xcorr[G], xsm = sd.xsum[G];
+                const int dA = 128 * (h0[h] + h1[h]) + (l0[h] + l1[h]);
+                const int dB = 128 * (h0[2 + h] + h1[2 + h]) + (l0[2 + h] + l1[2 + h]);
+                if (va) accA += scale_to_float(sA[G]) * ((float)dA * xsc) + scale_to_float(bA[G]) * xsm;
+                if (vb) accB += scale_to_float(sB[G]) * ((float)dB * xsc) + scale_to_float(bB[G]) * xsm;
             }
         }
     };
@@ -542,7 +615,10 @@ __device__ __forceinline__ void run_phase(const typename Pol::Params& p, EngineS
             }
             if (ready) {
                 float u[4];
-                if (sd.bits == 4 && sd.ntok == 1 && sd.xfold)
+                if (sd.bits == 4 && sd.ntok == 1 && sd.xfold == 2)
+                    compute_unit_b1_int<ST>(stage, sd, chunk, u, lane,
+                                            reinterpret_cast<const uint4*>(xarea) - 2);  // 32 zero bytes before x
+                else if (sd.bits == 4 && sd.ntok == 1 && sd.xfold)
                     compute_unit_b1<ST>(stage, sd, chunk, u, lane,
                                         reinterpret_cast<const uint4*>(xarea) - 2);  // 32 zero bytes before x
                 else if (sd.bits == 4)

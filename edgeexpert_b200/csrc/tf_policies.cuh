@@ -35,6 +35,7 @@ struct GemvParams {
     int y_row_stride;     // elements between tokens of y
     long long y_bstride;  // elements between matrices of y
     int aligned, x_aligned;
+    int xint;  // batch-1 int4: activation staged for the integer tensor path
     uint32_t* err;
     Sched sched;
 };
@@ -60,6 +61,10 @@ struct GemvPolicy {
         uint32_t* xs = reinterpret_cast<uint32_t*>(xa);
         float* xsum = reinterpret_cast<float*>(xs + p.ntok * x_words_stride(p.K));
         float* xcorr = xsum + p.ntok * (p.K / kGroup);
+        if (p.xint) {
+            stage_x_int(p.x, p.K, xs, xsum, xcorr, tid, nt);
+            return;
+        }
         const bool fold = p.ntok == 1;
         stage_words(p.x, p.x_row_stride, p.ntok, p.K, xs, p.x_aligned, fold, tid, nt);
         __syncthreads();
@@ -85,7 +90,7 @@ struct GemvPolicy {
         d->xs = xs;
         d->xsum = reinterpret_cast<const float*>(xs + p.ntok * x_words_stride(p.K));
         d->xcorr = d->xsum + p.ntok * (p.K / kGroup);
-        d->xfold = p.ntok == 1;
+        d->xfold = p.xint ? 2 : (p.ntok == 1 ? 1 : 0);
         d->xws = x_words_stride(p.K);
         d->ntok = p.ntok;
         d->mult = 1.0f;
@@ -182,6 +187,7 @@ struct Phase1Params {
     // unit waits for it (griddepcontrol.wait) and reads its expert id then;
     // epilogues write only after the wait.
     int lazy_ids;
+    int xint;  // every consumer is int4: x staged for the integer tensor path
     uint32_t* err;
     Sched sched;
 };
@@ -221,6 +227,10 @@ struct Phase1Policy {
     __device__ static void stage_x(const Params& p, uint8_t* xa, int tid, int nt) {
         uint32_t* xs = reinterpret_cast<uint32_t*>(xa);
         float* xsum = reinterpret_cast<float*>(xs + x_words_stride(p.D));
+        if (p.xint) {
+            stage_x_int(p.x, p.D, xs, xsum, xsum + p.D / kGroup, tid, nt);
+            return;
+        }
         stage_words(p.x, p.D, 1, p.D, xs, p.x_aligned, true, tid, nt);
         __syncthreads();
         stage_xsum_smem(xs, x_words_stride(p.D), 1, p.D, xsum, xsum + p.D / kGroup, true, tid, nt);
@@ -230,7 +240,7 @@ struct Phase1Policy {
         d->xs = xs;
         d->xsum = reinterpret_cast<const float*>(xs + x_words_stride(p.D));
         d->xcorr = d->xsum + p.D / kGroup;
-        d->xfold = 1;
+        d->xfold = p.xint ? 2 : 1;
         d->xws = x_words_stride(p.D);
         d->ntok = 1;
         d->mult = 1.0f;
@@ -325,6 +335,7 @@ struct Phase2Params {
     AffineMat sd;
     const __half* shared_act;  // [Fs]
     int rw_in_smem;            // fused layer: routing weights in rw_smem()
+    int xint;                  // every consumer is int4: acts staged for the integer tensor path
     int aligned;
     uint32_t* err;
     Sched sched;
@@ -361,6 +372,14 @@ struct Phase2Policy {
         float* xsum = reinterpret_cast<float*>(xs + routed_words(p.top_k, p.F));
         uint32_t* xss = reinterpret_cast<uint32_t*>(xa + shared_off(p.top_k, p.F));
         float* xsums = reinterpret_cast<float*>(xss + x_words_stride(p.Fs));
+        if (p.xint) {
+            const int ngF = p.F / kGroup;
+            for (int sl = 0; sl < p.top_k; ++sl)
+                stage_x_int(p.acts + (size_t)sl * p.F, p.F, xs + (size_t)sl * x_words_stride(p.F), xsum + sl * ngF,
+                            xsum + p.top_k * ngF + sl * ngF, tid, nt);
+            if (p.has_shared) stage_x_int(p.shared_act, p.Fs, xss, xsums, xsums + p.Fs / kGroup, tid, nt);
+            return;
+        }
         if (p.top_k) stage_words(p.acts, p.F, p.top_k, p.F, xs, true, true, tid, nt);
         if (p.has_shared) stage_words(p.shared_act, p.Fs, 1, p.Fs, xss, true, true, tid, nt);
         __syncthreads();
@@ -397,7 +416,7 @@ struct Phase2Policy {
             d->xs = xs + (size_t)s * x_words_stride(p.F);
             d->xsum = reinterpret_cast<const float*>(xs + routed_words(p.top_k, p.F)) + s * (p.F / kGroup);
             d->xcorr = d->xsum + p.top_k * (p.F / kGroup);
-            d->xfold = 1;
+            d->xfold = p.xint ? 2 : 1;
             d->xws = x_words_stride(p.F);
             d->mult = __half2float(p.rw_in_smem ? rw_smem()[s] : p.routing_w[s]);
         } else {
@@ -415,7 +434,7 @@ struct Phase2Policy {
             d->xs = xss;
             d->xsum = reinterpret_cast<const float*>(xss + x_words_stride(p.Fs));
             d->xcorr = d->xsum + p.Fs / kGroup;
-            d->xfold = 1;
+            d->xfold = p.xint ? 2 : 1;
             d->xws = x_words_stride(p.Fs);
             d->mult = 1.0f;
         }

@@ -82,9 +82,13 @@ def test_int4_gemv_sweep(cuda, m, n):
     assert O.rel_error(y, ref) < FP16_TOL
 
 
+@pytest.mark.parametrize("xint", ["", "0"])
 @pytest.mark.parametrize("scale_type", [0, 1])
-def test_int4_gemv_config0(cuda, scale_type):
-    # 1408 x 2816, q ~ U{0..15}, |N(0,0.02)| scales, x ~ N(0,1)
+def test_int4_gemv_config0(cuda, scale_type, xint, monkeypatch):
+    # 1408 x 2816, q ~ U{0..15}, |N(0,0.02)| scales, x ~ N(0,1);
+    # default integer tensor path and the fp16 path (TFCUDA_XINT=0)
+    if xint:
+        monkeypatch.setenv("TFCUDA_XINT", xint)
     W, S, B, x = make_gemv(1408, 2816, 4, scale_type, f"cfg0-{scale_type}")
     y = run_gemv(W, S, B, x, 1408, 2816, 4, scale_type)
     ref = O.affine_gemv_ref(W, S, B, O.f16_to_f32(x), 4, scale_type)
@@ -289,13 +293,16 @@ def test_shared_expert(cuda, bits, D, Fs):
     assert O.rel_error(O.f16_to_f32(f16(y)), y32_ref) < FP16_TOL
 
 
+@pytest.mark.parametrize("xint", ["", "1"])
 @pytest.mark.parametrize("fused", [False, True])
-def test_moe_decode_layer_config1(cuda, fused, monkeypatch):
+def test_moe_decode_layer_config1(cuda, fused, xint, monkeypatch):
     """BASELINE config 1 at full shape: router int8 128x2816 -> top-8 -> routed
     gate/up/down (F=704) + shared int4 (Fs=2112).  Routing bit-exact (or a
     near tie), output within 2e-3 of the oracle layer.  Both the default
     three-launch path and the single cooperative launch (TFCUDA_FUSED=1)."""
     monkeypatch.setenv("TFCUDA_FUSED", "1" if fused else "0")
+    if xint:  # batch-1 phases on the integer tensor path (u8 codes x 15-bit activation)
+        monkeypatch.setenv("TFCUDA_XINT", xint)
     from edgeexpert_b200.moe import (ExpertPool, MoELayerWeights, SharedExpertProjection, moe_decode_layer)
     E, D, F, Fs = 128, 2816, 704, 2112
     ex = Experts(E, D, F, 0, "layer-cfg1")
