@@ -5,6 +5,7 @@
 
 #include "tf_context.cuh"
 #include "tf_fused.cuh"
+#include "tf_gemv_tc.cuh"
 
 using namespace tf;
 
@@ -88,6 +89,19 @@ tf_status gemv_common(tf_context* ctx, uint32_t bits, const void* W, const void*
     if (ntok > 8) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: at most 8 tokens per call, got %u", name, ntok);
     if (!aligned2(W) || !aligned2(S) || !aligned2(B) || !aligned2(x) || !aligned2(y))
         return fail(ctx, TF_ERR_MISALIGNED, "%s: buffers must be 2-byte aligned", name);
+    // One token of int4 on the tcgen05 GEMV (tf_gemv_tc.cu) when TFCUDA_GEMV=tc
+    // (read per call).  Opt-in: its i8 MMAs with the codes as the 128-row A
+    // operand cost a fixed ~140 cycles each, which holds it at ~0.61 of HBM
+    // while the streaming engine's integer path reaches ~0.65.
+    if (bits == 4 && ntok == 1) {
+        const char* env = getenv("TFCUDA_GEMV");
+        if (env && strcmp(env, "tc") == 0) {
+            bool used = false;
+            tf_status rc = gemv_tc_try(ctx, W, S, B, wbs, sbs, batch, x, y, ybs, m, n, st,
+                                       static_cast<cudaStream_t>(stream), 1, &used, name);
+            if (rc || used) return rc;
+        }
+    }
     GemvParams p;
     memset(&p, 0, sizeof(p));
     p.W = static_cast<const uint8_t*>(W);

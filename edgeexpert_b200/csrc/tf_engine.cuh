@@ -24,6 +24,8 @@
 #pragma once
 #include <cuda.h>
 
+#include <type_traits>
+
 #include "tf_device.cuh"
 
 namespace tf {
@@ -269,8 +271,12 @@ __device__ __forceinline__ void compute_unit_b1(const uint8_t* __restrict__ stag
 
 // Batch-1 int4 path on the integer tensor path: weight codes unpacked to
 // bytes (w & 0x0F0F0F0F, (w >> 4) & 0x0F0F0F0F) times the 15-bit activation
-// split in two int8 halves, exact int32 sums per group; groups in the MMA N
-// dimension as in compute_unit_b1.  y = sum_g s_g * xsc_g * (128 hi + lo) + b_g * xsum_g.
+// split in two int8 halves (X = 128 hi + lo), exact int32 sums per group.
+// The 8 MMA columns hold 4 groups x {hi, lo}: column 2j + h carries half h of
+// group j of a 4-group block and is zero for the other groups' k-steps, so one
+// m16n8k32 per 32 codes serves both halves.  Lane t then holds group t of the
+// block: c[0] = hi, c[1] = lo of row g; c[2], c[3] of row g + 8.
+// y = sum_g s_g * xsc_g * (128 hi + lo) + b_g * xsum_g.
 template <typename ST>
 __device__ __forceinline__ void compute_unit_b1_int(const uint8_t* __restrict__ stage, const SegDesc& sd, int chunk,
                                                     float out[4], int lane, const uint4* zeros) {
@@ -293,42 +299,52 @@ __device__ __forceinline__ void compute_unit_b1_int(const uint8_t* __restrict__ 
     const uint8_t* xb = reinterpret_cast<const uint8_t*>(sd.xs);
     constexpr uint32_t kLo = 0x0F0F0F0Fu;
     float accA = 0.f, accB = 0.f;
-    auto block = [&](const int Gb, const bool full_block) {
-        int h0[4] = {0, 0, 0, 0}, h1[4] = {0, 0, 0, 0}, l0[4] = {0, 0, 0, 0}, l1[4] = {0, 0, 0, 0};
-        const int bbase = ((Gb - G0) >> 2) * kBoxBytes + g * kBox;
+    // NB blocks of 4 groups (one 128-byte box column of the stage each), their
+    // MMA chains interleaved
+    auto blocks = [&](const int Gb, const bool full_block, auto nb_tag) {
+        constexpr int NB = decltype(nb_tag)::value;
+        int c[NB][2][4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int G = Gb + j;
-            if (full_block || G < G1) {
-                const uint4* xp = (g == j) ? reinterpret_cast<const uint4*>(xb + (G * 4 + t) * 32) : zeros;
-                const uint4 xh = xp[0], xl = xp[1];
-                const int o = bbase + (j >> 2) * kBoxBytes + (((((j & 3) * 2 + (t >> 1)) ^ g) & 7) << 4) + (t & 1) * 8;
-                const uint2 wa = *reinterpret_cast<const uint2*>(halfA + o);
-                const uint2 wb = *reinterpret_cast<const uint2*>(halfB + o);
-                const uint32_t a0 = wa.x & kLo, a1 = (wa.x >> 4) & kLo, a2 = wa.y & kLo, a3 = (wa.y >> 4) & kLo;
-                const uint32_t b0 = wb.x & kLo, b1 = (wb.x >> 4) & kLo, b2 = wb.y & kLo, b3 = (wb.y >> 4) & kLo;
-                imma16832(h0, a0, b0, a1, b1, xh.x, xh.y);
-                imma16832(h1, a2, b2, a3, b3, xh.z, xh.w);
-                imma16832(l0, a0, b0, a1, b1, xl.x, xl.y);
-                imma16832(l1, a2, b2, a3, b3, xl.z, xl.w);
+        for (int k = 0; k < NB; ++k)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) c[k][0][i] = c[k][1][i] = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+#pragma unroll
+            for (int k = 0; k < NB; ++k) {
+                const int G = Gb + 4 * k + j;
+                if (full_block || G < G1) {
+                    const int bbase = ((Gb + 4 * k - G0) >> 2) * kBoxBytes + g * kBox;
+                    // this lane's column 2j + h: half h = g & 1 of group j
+                    const uint4* xp = ((g >> 1) == j)
+                                          ? reinterpret_cast<const uint4*>(xb + (G * 4 + t) * 32) + (g & 1)
+                                          : zeros;
+                    const uint4 xv = xp[0];
+                    const int o = bbase + ((((j * 2 + (t >> 1)) ^ g) & 7) << 4) + (t & 1) * 8;
+                    const uint2 wa = *reinterpret_cast<const uint2*>(halfA + o);
+                    const uint2 wb = *reinterpret_cast<const uint2*>(halfB + o);
+                    const uint32_t a0 = wa.x & kLo, a1 = (wa.x >> 4) & kLo, a2 = wa.y & kLo, a3 = (wa.y >> 4) & kLo;
+                    const uint32_t b0 = wb.x & kLo, b1 = (wb.x >> 4) & kLo, b2 = wb.y & kLo, b3 = (wb.y >> 4) & kLo;
+                    imma16832(c[k][0], a0, b0, a1, b1, xv.x, xv.y);
+                    imma16832(c[k][1], a2, b2, a3, b3, xv.z, xv.w);
+                }
             }
         }
-        // this lane's columns: groups Gb + 2t (elements 0, 2) and Gb + 2t + 1 (1, 3)
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int G = Gb + 2 * t + h;
+        for (int k = 0; k < NB; ++k) {
+            const int G = Gb + 4 * k + t;
             if (full_block || G < G1) {
                 const float xsc = sd.xcorr[G], xsm = sd.xsum[G];
-                const int dA = 128 * (h0[h] + h1[h]) + (l0[h] + l1[h]);
-                const int dB = 128 * (h0[2 + h] + h1[2 + h]) + (l0[2 + h] + l1[2 + h]);
+                const int dA = 128 * (c[k][0][0] + c[k][1][0]) + (c[k][0][1] + c[k][1][1]);
+                const int dB = 128 * (c[k][0][2] + c[k][1][2]) + (c[k][0][3] + c[k][1][3]);
                 if (va) accA += scale_to_float(sA[G]) * ((float)dA * xsc) + scale_to_float(bA[G]) * xsm;
                 if (vb) accB += scale_to_float(sB[G]) * ((float)dB * xsc) + scale_to_float(bB[G]) * xsm;
             }
         }
     };
     int Gb = G0;
-    for (; Gb + 8 <= G1; Gb += 8) block(Gb, true);
-    if (Gb < G1) block(Gb, false);
+    for (; Gb + 8 <= G1; Gb += 8) blocks(Gb, true, std::integral_constant<int, 2>{});
+    for (; Gb < G1; Gb += 4) blocks(Gb, Gb + 4 <= G1, std::integral_constant<int, 1>{});
     accA += __shfl_xor_sync(0xffffffffu, accA, 1);
     accA += __shfl_xor_sync(0xffffffffu, accA, 2);
     accB += __shfl_xor_sync(0xffffffffu, accB, 1);
