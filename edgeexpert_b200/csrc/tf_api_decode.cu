@@ -77,6 +77,11 @@ static bool xint_enabled(bool default_on) {
     return default_on;
 }
 
+static bool helpers_enabled() {
+    const char* e = getenv("TFCUDA_HELPERS");
+    return !(e && e[0] == '0');
+}
+
 tf_status gemv_common(tf_context* ctx, uint32_t bits, const void* W, const void* S, const void* B, uint64_t wbs,
                       uint64_t sbs, uint32_t batch, const void* x, uint32_t ntok, uint32_t xrs, void* y, uint32_t yrs,
                       uint64_t ybs, uint32_t m, uint32_t n, tf_scale_type st, void* stream, const char* name) {
@@ -89,16 +94,20 @@ tf_status gemv_common(tf_context* ctx, uint32_t bits, const void* W, const void*
     if (ntok > 8) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: at most 8 tokens per call, got %u", name, ntok);
     if (!aligned2(W) || !aligned2(S) || !aligned2(B) || !aligned2(x) || !aligned2(y))
         return fail(ctx, TF_ERR_MISALIGNED, "%s: buffers must be 2-byte aligned", name);
-    // One token of int4 on the tcgen05 GEMV (tf_gemv_tc.cu) when TFCUDA_GEMV=tc
-    // (read per call).  Opt-in: its i8 MMAs with the codes as the 128-row A
-    // operand cost a fixed ~140 cycles each, which holds it at ~0.61 of HBM
-    // while the streaming engine's integer path reaches ~0.65.
-    if (bits == 4 && ntok == 1) {
+    // One token of int4 over at least one 128-row tile per SM: the ring-streamed
+    // integer GEMV (tf_gemv_tc.cu).  TFCUDA_GEMV (read per call): "engine"
+    // keeps the streaming engine, "stream" / "tc" force the integer / the
+    // tcgen05 ring kernel for any tile count.
+    if (bits == 4 && ntok == 1 && xint_enabled(true)) {
         const char* env = getenv("TFCUDA_GEMV");
-        if (env && strcmp(env, "tc") == 0) {
+        const bool eng = env && strcmp(env, "engine") == 0;
+        const bool tc = env && strcmp(env, "tc") == 0;
+        const bool forced = tc || (env && strcmp(env, "stream") == 0);
+        if (!eng) {
             bool used = false;
             tf_status rc = gemv_tc_try(ctx, W, S, B, wbs, sbs, batch, x, y, ybs, m, n, st,
-                                       static_cast<cudaStream_t>(stream), 1, &used, name);
+                                       static_cast<cudaStream_t>(stream), tc ? kGemvTensorCore : kGemvStream,
+                                       forced ? 1 : 0, &used, name);
             if (rc || used) return rc;
         }
     }
@@ -143,7 +152,11 @@ tf_status gemv_common(tf_context* ctx, uint32_t bits, const void* W, const void*
             q.xint = (q.bits == 4 && q.ntok == 1 && xint_enabled(true)) ? 1 : 0;
             q.x = p.x + (size_t)t0 * xrs;
             q.y = p.y + (size_t)t0 * yrs;
-            tf_status rc = launch_engine<Pol, ST>(ctx, q, Pol::x_bytes((int)n, q.ntok), sj, cs, name);
+            // one token on the integer path: a helper warp per stage
+            // (TFCUDA_HELPERS=0 turns it off; read per call)
+            tf_status rc = (q.xint && q.aligned && helpers_enabled())
+                               ? launch_engine<Pol, ST, 1>(ctx, q, Pol::x_bytes((int)n, q.ntok), sj, cs, name)
+                               : launch_engine<Pol, ST>(ctx, q, Pol::x_bytes((int)n, q.ntok), sj, cs, name);
             if (rc) return rc;
         }
         return TF_OK;

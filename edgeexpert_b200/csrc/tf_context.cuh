@@ -60,12 +60,12 @@ inline bool aligned2(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 1
 inline bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
 
 // Largest dynamic shared memory an engine launch may request.
-template <class Pol, typename ST>
+template <class Pol, typename ST, int H = 0>
 size_t engine_smem_limit(tf_context* ctx) {
     static size_t static_smem = (size_t)-1;
     if (static_smem == (size_t)-1) {
         cudaFuncAttributes fa;
-        if (cudaFuncGetAttributes(&fa, engine_kernel<Pol, ST>) != cudaSuccess) return 0;
+        if (cudaFuncGetAttributes(&fa, engine_kernel<Pol, ST, H>) != cudaSuccess) return 0;
         static_smem = fa.sharedSizeBytes;
     }
     return ctx->max_smem_optin - static_smem;
@@ -73,18 +73,18 @@ size_t engine_smem_limit(tf_context* ctx) {
 
 // Launch one engine instantiation: sets the dynamic shared-memory attribute
 // once per instantiation and device, sizes the grid to min(super-jobs, SMs)
-// (one kWarps-warp CTA per SM).
-template <class Pol, typename ST>
+// (one CTA of kWarps warps, or 2 * kWarps with helper warps, per SM).
+template <class Pol, typename ST, int H = 0>
 tf_status launch_engine(tf_context* ctx, const typename Pol::Params& p, size_t x_bytes, int superjobs,
                         cudaStream_t stream, const char* name) {
     if (superjobs <= 0) return TF_OK;
-    const size_t limit = engine_smem_limit<Pol, ST>(ctx);
-    const size_t smem = engine_fixed_smem() + x_bytes + 1024;  // + slack for 1 KB alignment
+    const size_t limit = engine_smem_limit<Pol, ST, H>(ctx);
+    const size_t smem = engine_fixed_smem(H) + x_bytes + 1024;  // + slack for 1 KB alignment
     if (smem > limit) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: activation too large for shared memory", name);
     static bool configured[64] = {};  // per instantiation, per device
     const int dev = ctx->device & 63;
     if (!configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(engine_kernel<Pol, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(engine_kernel<Pol, ST, H>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)limit);
         if (e != cudaSuccess) return cuda_check(ctx, e, name);
         configured[dev] = true;
@@ -97,7 +97,7 @@ tf_status launch_engine(tf_context* ctx, const typename Pol::Params& p, size_t x
     const bool pdl = !(pdl_env && pdl_env[0] == '0');
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(kWarps * 32);
+    cfg.blockDim = dim3(kWarps * 32 * (1 + H));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -105,7 +105,7 @@ tf_status launch_engine(tf_context* ctx, const typename Pol::Params& p, size_t x
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cuda_check(ctx, cudaLaunchKernelEx(&cfg, engine_kernel<Pol, ST>, p), name);
+    return cuda_check(ctx, cudaLaunchKernelEx(&cfg, engine_kernel<Pol, ST, H>, p), name);
 }
 
 // ---------------------------------------------------------------------------

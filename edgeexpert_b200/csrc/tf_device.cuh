@@ -39,7 +39,7 @@ constexpr int kMaxScaleGroups = 64;             // full-row scale copies up to K
 constexpr int kScaleArr = kBoxRows * kMaxScaleGroups * 2;
 // Stage: [half A: rows 0-7][half B: rows 8-15][scales A][biases A][scales B][biases B]
 constexpr int kStageBytes = 2 * kHalfBytes + 4 * kScaleArr;  // 16 KB
-constexpr uint32_t kSpinLimit = 1u << 22;  // bounded mbarrier wait (error flag after)
+constexpr uint32_t kSpinLimit = 1u << 20;  // bounded mbarrier wait (error flag after)
 
 // Error bits written to the context's device status word.
 enum : uint32_t { kErrMbarTimeout = 1u, kErrBadExpert = 2u, kErrAlign = 4u };
@@ -103,11 +103,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread for up to `ns`
+// nanoseconds (or until the phase completes) instead of returning at once, so
+// a waiting warp does not take issue slots from the warps that compute.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait: returns false (and records the error) if the phase never
 // completes; the caller then skips the work instead of hanging the GPU.
+// Each try suspends for at most 1 us, so the bound is about kSpinLimit us.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t* err) {
     for (uint32_t i = 0; i < kSpinLimit; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
     if (err) atomicOr(err, kErrMbarTimeout);
     return false;
 }

@@ -277,18 +277,24 @@ __device__ __forceinline__ void compute_unit_b1(const uint8_t* __restrict__ stag
 // m16n8k32 per 32 codes serves both halves.  Lane t then holds group t of the
 // block: c[0] = hi, c[1] = lo of row g; c[2], c[3] of row g + 8.
 // y = sum_g s_g * xsc_g * (128 hi + lo) + b_g * xsum_g.
+// `part` 0/1 of `nparts` 2 covers the first / second half of the unit's groups
+// (split at a multiple of 4) when two warps share the stage; nparts 1 = all.
 template <typename ST>
 __device__ __forceinline__ void compute_unit_b1_int(const uint8_t* __restrict__ stage, const SegDesc& sd, int chunk,
-                                                    float out[4], int lane, const uint4* zeros) {
+                                                    float out[4], int lane, const uint4* zeros, int part = 0,
+                                                    int nparts = 1) {
     const int g = lane >> 2, t = lane & 3;
     const int ngK = sd.K / kGroup;
     constexpr int kGPU = kMaxBoxes * kBox / 32;  // 24 groups per unit
-    const int G0 = chunk * kGPU;
-    const int G1 = min(ngK, G0 + kGPU);
+    const int U0 = chunk * kGPU;                 // the unit's groups: [U0, U1)
+    const int U1 = min(ngK, U0 + kGPU);
+    const int mid = nparts == 1 ? U1 : min(U1, U0 + ((U1 - U0 + 7) >> 3) * 4);
+    const int G0 = part == 0 ? U0 : mid;         // this call's groups: [G0, G1)
+    const int G1 = part == 0 ? mid : U1;
     const bool va = g < sd.nA, vb = g < sd.nB;
     const bool full = ngK <= kMaxScaleGroups;
     const int sstride = full ? ngK : kGPU;
-    const int sbase = full ? 0 : G0;
+    const int sbase = full ? 0 : U0;
     const ST* scl = reinterpret_cast<const ST*>(stage + 2 * kHalfBytes) - sbase;
     const ST* sA = scl + g * sstride;
     const ST* bA = scl + kScaleArr / 2 + g * sstride;
@@ -314,7 +320,7 @@ __device__ __forceinline__ void compute_unit_b1_int(const uint8_t* __restrict__ 
             for (int k = 0; k < NB; ++k) {
                 const int G = Gb + 4 * k + j;
                 if (full_block || G < G1) {
-                    const int bbase = ((Gb + 4 * k - G0) >> 2) * kBoxBytes + g * kBox;
+                    const int bbase = ((Gb + 4 * k - U0) >> 2) * kBoxBytes + g * kBox;
                     // this lane's column 2j + h: half h = g & 1 of group j
                     const uint4* xp = ((g >> 1) == j)
                                           ? reinterpret_cast<const uint4*>(xb + (G * 4 + t) * 32) + (g & 1)
@@ -512,11 +518,12 @@ __device__ __forceinline__ int warp_unit(const SuperJob& s, int w, int i) {
     return v;
 }
 
-// Shared-memory layout of the engine (bytes):
-//   [stages: kWarps * kStageBytes (1 KB aligned)][red: 2 * kWarps * 32 * 4 floats]
+// Shared-memory layout of the engine (bytes), H = helper warps per stage (0/1):
+//   [stages: kWarps * kStageBytes (1 KB aligned)][red: 2 * (1 + H) * kWarps * 32 * 4 floats]
 //   [bars: kWarps u64][32 zero bytes][x area: Pol::x_bytes(p)]
-__host__ __device__ inline size_t engine_fixed_smem() {
-    return (size_t)kWarps * kStageBytes + 2 * kWarps * 32 * 4 * sizeof(float) + kWarps * 8 + 32;
+__host__ __device__ inline size_t engine_red_floats(int H) { return (size_t)2 * (1 + H) * kWarps * 32 * 4; }
+__host__ __device__ inline size_t engine_fixed_smem(int H = 0) {
+    return (size_t)kWarps * kStageBytes + engine_red_floats(H) * sizeof(float) + kWarps * 8 + 32;
 }
 
 // Dynamic shared memory rounded up to a 1 KB boundary (the 128-byte TMA
@@ -530,36 +537,49 @@ __device__ __forceinline__ uint8_t* engine_smem_base() {
 // Per-CTA engine state that persists across the phases of a fused kernel.
 struct EngineState {
     uint8_t* smem;      // 1 KB aligned base
-    uint64_t* bar;      // this warp's stage mbarrier
+    uint8_t* xarea;     // staged activations
+    uint64_t* bar;      // this warp's stage mbarrier (a helper warp: its owner's)
     int seq;            // units consumed by this warp (mbarrier phase)
     int parity_buf;     // reduction buffer in use
     bool dead;          // a bounded wait gave up: skip further waits
 };
 
-__device__ __forceinline__ void engine_init(EngineState& es) {
+__device__ __forceinline__ void engine_init(EngineState& es, int H = 0) {
     es.smem = engine_smem_base();
+    es.xarea = es.smem + engine_fixed_smem(H);
     float* red = reinterpret_cast<float*>(es.smem + (size_t)kWarps * kStageBytes);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(red + 2 * kWarps * 32 * 4);
-    es.bar = bars + (threadIdx.x >> 5);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(red + engine_red_floats(H));
+    es.bar = bars + (threadIdx.x >> 5) % kWarps;
     es.seq = 0;
     es.parity_buf = 0;
     es.dead = false;
-    if ((threadIdx.x & 31) == 0) mbar_init(es.bar, 1);
+    if ((threadIdx.x & 31) == 0 && (threadIdx.x >> 5) < kWarps) mbar_init(es.bar, 1);
     if (threadIdx.x < 8) reinterpret_cast<uint32_t*>(bars + kWarps)[threadIdx.x] = 0u;  // zero x fragment
     fence_mbar_init();
 }
 
-__device__ __forceinline__ uint8_t* engine_xarea_of(const EngineState& es) { return es.smem + engine_fixed_smem(); }
+__device__ __forceinline__ uint8_t* engine_xarea_of(const EngineState& es) { return es.xarea; }
+
+// Two warps that share a stage meet at named barrier 1 + stage index.
+__device__ __forceinline__ void stage_pair_sync(int stage_idx) {
+    asm volatile("bar.sync %0, 64;" ::"r"(1 + stage_idx) : "memory");
+}
 
 // One phase: all jobs of policy `Pol`, distributed over the grid's CTAs.
 // Every thread of the CTA must call it (it contains CTA barriers).
-template <class Pol, typename ST>
+// H = 1: kWarps helper warps, helper w + kWarps computes the second half of
+// the groups of every unit of stage w (batch-1 int4 integer path only; the
+// host launches H = 1 only for such phases, with TMA-aligned weights).
+template <class Pol, typename ST, int H = 0>
 __device__ __forceinline__ void run_phase(const typename Pol::Params& p, EngineState& es) {
+    constexpr int kW = kWarps * (1 + H);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int owner = warp % kWarps;
+    const bool helper = H && warp >= kWarps;
     uint8_t* smem = es.smem;
     float* red = reinterpret_cast<float*>(smem + (size_t)kWarps * kStageBytes);
     uint8_t* xarea = engine_xarea_of(es);
-    uint8_t* stage = smem + (size_t)warp * kStageBytes;
+    uint8_t* stage = smem + (size_t)owner * kStageBytes;
     uint64_t* bar = es.bar;
 
     // Weights that depend on no earlier kernel (router, plain GEMV) are put in
@@ -579,7 +599,7 @@ __device__ __forceinline__ void run_phase(const typename Pol::Params& p, EngineS
     auto load_next = [&]() -> void {
         while (l_sj < S) {
             const SuperJob sj = Pol::superjob(p, l_sj);
-            const int v = warp_unit(sj, warp, l_i);
+            const int v = warp_unit(sj, owner, l_i);
             if (v < 0) {
                 l_sj += gridDim.x;
                 l_i = 0;
@@ -597,24 +617,24 @@ __device__ __forceinline__ void run_phase(const typename Pol::Params& p, EngineS
     // Weight tiles do not depend on the activations: put the first unit of
     // every warp in flight before staging the activations.
     TF_TW(8);
-    if (p.aligned && !es.dead) load_next();
+    if (p.aligned && !es.dead && !helper) load_next();
     TF_TW(9);
     if (Pol::kWeightsIndependent) {
         griddep_wait();
         griddep_launch_dependents();
     }
-    Pol::stage_x(p, xarea, threadIdx.x, kWarps * 32);
+    Pol::stage_x(p, xarea, threadIdx.x, kW * 32);
     __syncthreads();
 
     for (int sjx = blockIdx.x; sjx < S; sjx += gridDim.x) {
         const SuperJob sj = Pol::superjob(p, sjx);
         if (Pol::kStagePerSuperjob) {  // activations differ per super-job (grouped experts)
-            Pol::stage_x_sj(p, sj, xarea, threadIdx.x, kWarps * 32);
+            Pol::stage_x_sj(p, sj, xarea, threadIdx.x, kW * 32);
             __syncthreads();
         }
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         for (int i = 0;; ++i) {
-            const int v = warp_unit(sj, warp, i);
+            const int v = warp_unit(sj, owner, i);
             if (v < 0) break;
             SegDesc sd;
             int chunk;
@@ -631,7 +651,10 @@ __device__ __forceinline__ void run_phase(const typename Pol::Params& p, EngineS
             }
             if (ready) {
                 float u[4];
-                if (sd.bits == 4 && sd.ntok == 1 && sd.xfold == 2)
+                if constexpr (H != 0)
+                    compute_unit_b1_int<ST>(stage, sd, chunk, u, lane, reinterpret_cast<const uint4*>(xarea) - 2,
+                                            helper ? 1 : 0, 2);
+                else if (sd.bits == 4 && sd.ntok == 1 && sd.xfold == 2)
                     compute_unit_b1_int<ST>(stage, sd, chunk, u, lane,
                                             reinterpret_cast<const uint4*>(xarea) - 2);  // 32 zero bytes before x
                 else if (sd.bits == 4 && sd.ntok == 1 && sd.xfold)
@@ -646,27 +669,31 @@ __device__ __forceinline__ void run_phase(const typename Pol::Params& p, EngineS
                 if (i == 0) TF_TW(11);
             }
             __syncwarp();
+            if constexpr (H != 0) stage_pair_sync(owner);  // both halves read before the stage is refilled
             if (p.aligned) ++es.seq;
-            if (p.aligned && !es.dead) load_next();
+            if (p.aligned && !es.dead && !helper) load_next();
         }
-        float* rb = red + (size_t)es.parity_buf * kWarps * 32 * 4;
+        float* rb = red + (size_t)es.parity_buf * kW * 32 * 4;
         *reinterpret_cast<float4*>(rb + (warp * 32 + lane) * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
         __syncthreads();
         // Leaders: for J > 1 warp jj*U reduces job jj over warps jj*U..jj*U+U-1;
         // for J == 1 warp 0 reduces warps 0..min(U,kWarps)-1.
         const int njobs = sj.j1 - sj.j0;
         const int lead_stride = sj.J > 1 ? sj.U : kWarps;
-        if (warp % lead_stride == 0 && warp / lead_stride < njobs) {
+        if (!helper && warp % lead_stride == 0 && warp / lead_stride < njobs) {
             const int jj = warp / lead_stride;
             const int w0 = sj.J > 1 ? jj * sj.U : 0;
             const int wn = sj.J > 1 ? sj.U : min(sj.U, kWarps);
             float f[4] = {0.f, 0.f, 0.f, 0.f};
             for (int w = w0; w < w0 + wn; ++w) {
-                const float4 q = *reinterpret_cast<const float4*>(rb + (w * 32 + lane) * 4);
-                f[0] += q.x;
-                f[1] += q.y;
-                f[2] += q.z;
-                f[3] += q.w;
+#pragma unroll
+                for (int h = 0; h <= H; ++h) {
+                    const float4 q = *reinterpret_cast<const float4*>(rb + ((w + h * kWarps) * 32 + lane) * 4);
+                    f[0] += q.x;
+                    f[1] += q.y;
+                    f[2] += q.z;
+                    f[3] += q.w;
+                }
             }
             Pol::epilogue(p, sj.j0 + jj, f, lane);
         }
@@ -674,12 +701,13 @@ __device__ __forceinline__ void run_phase(const typename Pol::Params& p, EngineS
     }
 }
 
-template <class Pol, typename ST>
-__global__ void __launch_bounds__(kWarps * 32, 1) engine_kernel(const __grid_constant__ typename Pol::Params p) {
+template <class Pol, typename ST, int H = 0>
+__global__ void __launch_bounds__(kWarps * 32 * (1 + H), 1)
+    engine_kernel(const __grid_constant__ typename Pol::Params p) {
     EngineState es;
     TF_T(0);
-    engine_init(es);
-    run_phase<Pol, ST>(p, es);
+    engine_init(es, H);
+    run_phase<Pol, ST, H>(p, es);
     TF_T(6);
 }
 

@@ -115,14 +115,68 @@ __device__ __forceinline__ int gt_bpos(int G, int e, int h) {
            ((((kb >> 4) ^ n) & 7) << 4) + (kb & 15);
 }
 
-__device__ __forceinline__ bool gwait(uint64_t* bar, uint32_t parity, GtShared& sh, uint32_t* err) {
+__device__ __forceinline__ bool gwait(uint64_t* bar, uint32_t parity, int& abort_flag, uint32_t* err) {
     for (uint32_t i = 0; i < kGtSpin; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 255u) == 255u && *reinterpret_cast<volatile int*>(&sh.abort_flag)) return false;
+        if ((i & 255u) == 255u && *reinterpret_cast<volatile int*>(&abort_flag)) return false;
     }
-    sh.abort_flag = 1;
+    abort_flag = 1;
     if (err) atomicOr(err, kErrMbarTimeout);
     return false;
+}
+__device__ __forceinline__ bool gwait(uint64_t* bar, uint32_t parity, GtShared& sh, uint32_t* err) {
+    return gwait(bar, parity, sh.abort_flag, err);
+}
+
+// The loader role of both GEMV kernels (one thread): per job (matrix b, rows
+// row0..row0+127) the scale and bias block -- one contiguous run of
+// rows * K/64 elements each, bulk-copied in 16-byte multiples, the < 16 ragged
+// bytes of a short last tile by plain loads -- into job slot jl % 2, then the
+// job's stages of 8 groups (two TMA boxes of 128 rows x 128 B; the second is
+// skipped when it starts past the row) into the ring.
+struct GtRing {
+    uint8_t* ring;
+    uint8_t* scl;
+    uint32_t sslot;
+    uint64_t* full;
+    uint64_t* empty;
+    uint64_t* sfull;
+    uint64_t* sempty;
+    int* abort_flag;
+};
+
+__device__ __forceinline__ void gt_load_jobs(const GtParams& p, const GtRing& r) {
+    const int ngK = p.K >> 6, nst = (ngK + 7) >> 3, R = p.R;
+    uint32_t q = 0;
+    int jl = 0;
+    for (int job = blockIdx.x; job < p.jobs; job += gridDim.x, ++jl) {
+        const int b = job / p.tiles, row0 = (job - b * p.tiles) * kGtRows;
+        const int rows = min(kGtRows, p.M - row0);
+        const int js = jl & 1;
+        if (!gwait(&r.sempty[js], ((jl >> 1) & 1) ^ 1, *r.abort_flag, p.err)) return;
+        const uint32_t nbytes = (uint32_t)rows * ngK * 2, bulk = nbytes & ~15u;
+        const size_t off = (size_t)b * p.sb_bstride + (size_t)row0 * ngK * 2;
+        uint8_t* ds = r.scl + (2 * js) * r.sslot;
+        uint8_t* db = ds + r.sslot;
+        for (uint32_t i = bulk; i < nbytes; i += 2) {
+            *reinterpret_cast<uint16_t*>(ds + i) = __ldg(reinterpret_cast<const uint16_t*>(p.S + off + i));
+            *reinterpret_cast<uint16_t*>(db + i) = __ldg(reinterpret_cast<const uint16_t*>(p.B + off + i));
+        }
+        mbar_arrive_expect_tx(&r.sfull[js], 2 * bulk);
+        if (bulk) {
+            bulk_g2s(ds, p.S + off, bulk, &r.sfull[js]);
+            bulk_g2s(db, p.B + off, bulk, &r.sfull[js]);
+        }
+        for (int st = 0; st < nst; ++st, ++q) {
+            const int slot = (int)(q % (uint32_t)R);
+            if (!gwait(&r.empty[slot], ((q / R) & 1) ^ 1, *r.abort_flag, p.err)) return;
+            const int x0 = st * 256;
+            const bool two = x0 + 128 < p.K / 2;
+            mbar_arrive_expect_tx(&r.full[slot], two ? 2 * kGtBox : kGtBox);
+            tma_load_3d(r.ring + slot * kGtStage, &p.wmap, x0, row0, b, &r.full[slot]);
+            if (two) tma_load_3d(r.ring + slot * kGtStage + kGtBox, &p.wmap, x0 + 128, row0, b, &r.full[slot]);
+        }
+    }
 }
 
 template <typename ST>
@@ -200,37 +254,8 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemv_tc_kernel(const __grid_con
     if (warp == 0) {
         // ================= loader =================
         if (lane == 0) {
-            uint32_t q = 0;
-            int jl = 0;
-            bool ok = true;
-            for (int job = blockIdx.x; ok && job < p.jobs; job += gridDim.x, ++jl) {
-                const int b = job / p.tiles, row0 = (job - b * p.tiles) * kGtRows;
-                const int rows = min(kGtRows, p.M - row0);
-                const int js = jl & 1;
-                if (!(ok = gwait(&sh.sempty[js], ((jl >> 1) & 1) ^ 1, sh, p.err))) break;
-                const uint32_t nbytes = (uint32_t)rows * ngK * 2, bulk = nbytes & ~15u;
-                const size_t off = (size_t)b * p.sb_bstride + (size_t)row0 * ngK * 2;
-                uint8_t* ds = scl + (2 * js) * L.sslot;
-                uint8_t* db = ds + L.sslot;
-                for (uint32_t i = bulk; i < nbytes; i += 2) {  // < 16 ragged bytes of a short last tile
-                    *reinterpret_cast<uint16_t*>(ds + i) = __ldg(reinterpret_cast<const uint16_t*>(p.S + off + i));
-                    *reinterpret_cast<uint16_t*>(db + i) = __ldg(reinterpret_cast<const uint16_t*>(p.B + off + i));
-                }
-                mbar_arrive_expect_tx(&sh.sfull[js], 2 * bulk);
-                if (bulk) {
-                    bulk_g2s(ds, p.S + off, bulk, &sh.sfull[js]);
-                    bulk_g2s(db, p.B + off, bulk, &sh.sfull[js]);
-                }
-                for (int st = 0; st < nst; ++st, ++q) {
-                    const int slot = (int)(q % (uint32_t)R);
-                    if (!(ok = gwait(&sh.empty[slot], ((q / R) & 1) ^ 1, sh, p.err))) break;
-                    const int x0 = st * 256;
-                    const bool two = x0 + 128 < p.K / 2;
-                    mbar_arrive_expect_tx(&sh.full[slot], two ? 2 * kGtBox : kGtBox);
-                    tma_load_3d(ring + slot * kGtStage, &p.wmap, x0, row0, b, &sh.full[slot]);
-                    if (two) tma_load_3d(ring + slot * kGtStage + kGtBox, &p.wmap, x0 + 128, row0, b, &sh.full[slot]);
-                }
-            }
+            const GtRing r{ring, scl, L.sslot, sh.full, sh.empty, sh.sfull, sh.sempty, &sh.abort_flag};
+            gt_load_jobs(p, r);
         }
     } else if (warp == 1) {
         // ================= MMA issue =================
@@ -348,6 +373,195 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemv_tc_kernel(const __grid_con
     }
 }
 
+// ---------------------------------------------------------------------------
+// Streaming GEMV on the integer mma.sync path (the default for many 128-row
+// tiles).  Same loader and ring as above; 8 consumer warps, warp w owning rows
+// 16w..16w+15 of the job, read the raw stage directly: a lane loads 8 code
+// bytes of row g and of row g + 8 (the 128-byte swizzle of the TMA box is the
+// engine's swizzle of an 8-row box), unpacks them to u8 (w & 0x0F0F0F0F,
+// (w >> 4) & 0x0F0F0F0F) and runs m16n8k32 against the activation staged as
+// in the engine's integer path (stage_x_int): the 8 MMA columns are 4 groups x
+// {hi, lo}, so lane t ends a 4-group block holding group t's two int32 dots.
+// The warp keeps its rows' fp32 sums for the whole job in registers.
+// ---------------------------------------------------------------------------
+// SPLIT = 2: 16 consumers, the warps w and w + 8 of a row tile take the
+// stage's first and second TMA box (groups 0-3 / 4-7) and add their row sums
+// through shared memory at the job's end.
+template <int SPLIT>
+struct GsCfg {
+    static constexpr int kConsumers = 8 * SPLIT;
+    static constexpr int kThreads = 32 * (1 + kConsumers);
+};
+
+struct GsShared {
+    uint64_t full[kGtMaxR], empty[kGtMaxR];
+    uint64_t sfull[2], sempty[2];
+    uint64_t pdone[8];       // SPLIT = 2: row tile w's second-half sums written
+    float part[2][kGtRows];  // SPLIT = 2: second-half row sums, by job parity
+    int abort_flag;
+};
+
+struct GsLayout {
+    uint32_t scl, sslot, xs, xsum, xsc, sh, total;
+};
+
+// [ring: R stages][scale/bias job slots: 4 x sslot][16 zero bytes + pad][xs: K/64 x 128 B]
+// [xsum, xsc: K/64 floats each][barriers]
+__host__ __device__ inline GsLayout gs_layout(int K, int R) {
+    const int ngK = K / 64;
+    GsLayout L;
+    L.scl = (uint32_t)R * kGtStage;
+    L.sslot = (uint32_t)((kGtRows * ngK * 2 + 15) & ~15);
+    L.xs = L.scl + 4 * L.sslot + 32;
+    L.xsum = L.xs + (uint32_t)ngK * 128;
+    L.xsc = L.xsum + (uint32_t)ngK * 4;
+    L.sh = (L.xsc + (uint32_t)ngK * 4 + 15) & ~15u;
+    L.total = L.sh + (uint32_t)sizeof(GsShared) + 1024;
+    return L;
+}
+
+template <typename ST, int SPLIT>
+__global__ void __launch_bounds__(GsCfg<SPLIT>::kThreads, 1) gemv_stream_kernel(const __grid_constant__ GtParams p) {
+    constexpr int kConsumers = GsCfg<SPLIT>::kConsumers;
+    constexpr int kThreads = GsCfg<SPLIT>::kThreads;
+    extern __shared__ uint8_t gs_smem_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gs_smem_raw) + 1023) & ~uintptr_t(1023));
+    const GsLayout L = gs_layout(p.K, p.R);
+    uint8_t* ring = sm;
+    uint8_t* scl = sm + L.scl;
+    uint8_t* xb = sm + L.xs;
+    float* xsum = reinterpret_cast<float*>(sm + L.xsum);
+    float* xsc = reinterpret_cast<float*>(sm + L.xsc);
+    GsShared& sh = *reinterpret_cast<GsShared*>(sm + L.sh);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ngK = p.K >> 6, nst = (ngK + 7) >> 3, R = p.R;
+
+    if (tid == 0) {
+        for (int s = 0; s < R; ++s) {
+            mbar_init(&sh.full[s], 1);
+            mbar_init(&sh.empty[s], kConsumers);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&sh.sfull[a], 1);
+            mbar_init(&sh.sempty[a], kConsumers);
+        }
+        for (int a = 0; a < 8; ++a) mbar_init(&sh.pdone[a], 1);
+        sh.abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tmap(&p.wmap);
+    }
+    if (tid < 8) reinterpret_cast<uint32_t*>(xb - 32)[tid] = 0u;  // zero activation fragment
+    stage_x_int(p.x, p.K, reinterpret_cast<uint32_t*>(xb), xsum, xsc, tid, kThreads);
+    __syncthreads();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const GtRing r{ring, scl, L.sslot, sh.full, sh.empty, sh.sfull, sh.sempty, &sh.abort_flag};
+            gt_load_jobs(p, r);
+        }
+    } else {
+        const int w = (warp - 1) & 7, half = (warp - 1) >> 3;
+        const int k0 = SPLIT == 2 ? half : 0, k1 = SPLIT == 2 ? half + 1 : 2;  // this warp's boxes
+        const int g = lane >> 2, t = lane & 3;
+        const uint4* zeros = reinterpret_cast<const uint4*>(xb - 32);
+        constexpr uint32_t kLo = 0x0F0F0F0Fu;
+        uint32_t q = 0;
+        int jl = 0;
+        bool ok = true;
+        for (int job = blockIdx.x; ok && job < p.jobs; job += gridDim.x, ++jl) {
+            const int b = job / p.tiles, row0 = (job - b * p.tiles) * kGtRows;
+            const int js = jl & 1;
+            if (!(ok = gwait(&sh.sfull[js], (jl >> 1) & 1, sh.abort_flag, p.err))) break;
+            const ST* sA = reinterpret_cast<const ST*>(scl + (2 * js) * L.sslot) + (16 * w + g) * ngK;
+            const ST* bA = reinterpret_cast<const ST*>(scl + (2 * js + 1) * L.sslot) + (16 * w + g) * ngK;
+            const ST* sB = sA + 8 * ngK;
+            const ST* bB = bA + 8 * ngK;
+            float accA = 0.f, accB = 0.f;
+            for (int st = 0; st < nst; ++st, ++q) {
+                const int slot = (int)(q % (uint32_t)R);
+                if (!(ok = gwait(&sh.full[slot], (q / R) & 1u, sh.abort_flag, p.err))) break;
+                const uint8_t* rowA = ring + slot * kGtStage + (16 * w + g) * 128;
+                const int ng = min(8, ngK - 8 * st);
+                // the stage's 2 blocks of 4 groups (one TMA box each), MMA chains interleaved
+                int c[2][2][4];
+#pragma unroll
+                for (int k = 0; k < 2; ++k)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) c[k][0][i] = c[k][1][i] = 0;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+#pragma unroll
+                    for (int k = 0; k < 2; ++k) {
+                        const int gl = 4 * k + j;
+                        if (k >= k0 && k < k1 && gl < ng) {
+                            const int G = 8 * st + gl;
+                            const uint4* xp = ((g >> 1) == j)
+                                                  ? reinterpret_cast<const uint4*>(xb + (G * 4 + t) * 32) + (g & 1)
+                                                  : zeros;
+                            const uint4 xv = xp[0];
+                            const int o = k * kGtBox + ((((j * 2 + (t >> 1)) ^ g) & 7) << 4) + (t & 1) * 8;
+                            const uint2 wa = *reinterpret_cast<const uint2*>(rowA + o);
+                            const uint2 wb = *reinterpret_cast<const uint2*>(rowA + 8 * 128 + o);
+                            const uint32_t a0 = wa.x & kLo, a1 = (wa.x >> 4) & kLo;
+                            const uint32_t a2 = wa.y & kLo, a3 = (wa.y >> 4) & kLo;
+                            const uint32_t b0 = wb.x & kLo, b1 = (wb.x >> 4) & kLo;
+                            const uint32_t b2 = wb.y & kLo, b3 = (wb.y >> 4) & kLo;
+                            imma16832(c[k][0], a0, b0, a1, b1, xv.x, xv.y);
+                            imma16832(c[k][1], a2, b2, a3, b3, xv.z, xv.w);
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sh.empty[slot]);  // codes are in registers
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    if (k >= k0 && k < k1 && 4 * k + t < ng) {
+                        const int G = 8 * st + 4 * k + t;
+                        const float xc = xsc[G], xm = xsum[G];
+                        const int dA = 128 * (c[k][0][0] + c[k][1][0]) + (c[k][0][1] + c[k][1][1]);
+                        const int dB = 128 * (c[k][0][2] + c[k][1][2]) + (c[k][0][3] + c[k][1][3]);
+                        accA += scale_to_float(sA[G]) * ((float)dA * xc) + scale_to_float(bA[G]) * xm;
+                        accB += scale_to_float(sB[G]) * ((float)dB * xc) + scale_to_float(bB[G]) * xm;
+                    }
+                }
+            }
+            if (!ok) break;
+            accA += __shfl_xor_sync(0xffffffffu, accA, 1);
+            accA += __shfl_xor_sync(0xffffffffu, accA, 2);
+            accB += __shfl_xor_sync(0xffffffffu, accB, 1);
+            accB += __shfl_xor_sync(0xffffffffu, accB, 2);
+            if constexpr (SPLIT == 2) {
+                // the second-half warp hands its row sums over; the slot of
+                // job jl is rewritten only after both warps released job jl's
+                // scales (sempty), i.e. after the first-half warp read it
+                float* part = sh.part[jl & 1];
+                if (half == 1) {
+                    if (t == 0) {
+                        part[16 * w + g] = accA;
+                        part[16 * w + 8 + g] = accB;
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&sh.pdone[w]);
+                        mbar_arrive(&sh.sempty[js]);
+                    }
+                    continue;
+                }
+                if (!(ok = gwait(&sh.pdone[w], jl & 1, sh.abort_flag, p.err))) break;
+                accA += part[16 * w + g];
+                accB += part[16 * w + 8 + g];
+            }
+            const int rA = row0 + 16 * w + g;
+            __half* yb = p.y + (long long)b * p.y_bstride;
+            if (t == 0 && rA < p.M) yb[rA] = __float2half_rn(accA);
+            if (t == 1 && rA + 8 < p.M) yb[rA + 8] = __float2half_rn(accB);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.sempty[js]);
+        }
+    }
+    __syncthreads();
+}
+
 // uint8 [depth][rows][row_bytes] in boxes of 128 B x 128 rows, 128-byte swizzle.
 bool make_gt_map(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows, uint64_t depth,
                  uint64_t depth_stride) {
@@ -371,6 +585,31 @@ int gt_ring_stages(int K) {
     return (int)std::min<long long>(kGtMaxR, left / kGtStage);
 }
 
+int gs_ring_stages(int K) {
+    const GsLayout L0 = gs_layout(K, 0);
+    const long long left = (long long)kGtSmemLimit - (long long)L0.total;
+    return (int)std::min<long long>(kGtMaxR, left / kGtStage);
+}
+
+template <typename ST, int SPLIT>
+tf_status launch_gemv_stream_split(tf_context* ctx, const GtParams& p, cudaStream_t stream, const char* name) {
+    const GsLayout L = gs_layout(p.K, p.R);
+    const void* fn = reinterpret_cast<const void*>(&gemv_stream_kernel<ST, SPLIT>);
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
+    if (e != cudaSuccess) return cuda_check(ctx, e, name);
+    const int grid = std::min(ctx->num_sms, p.jobs);
+    gemv_stream_kernel<ST, SPLIT><<<grid, GsCfg<SPLIT>::kThreads, L.total, stream>>>(p);
+    return cuda_check(ctx, cudaGetLastError(), name);
+}
+
+// TFCUDA_GEMV_SPLIT=1 selects 8 consumer warps instead of 16 (read per call).
+template <typename ST>
+tf_status launch_gemv_stream(tf_context* ctx, const GtParams& p, cudaStream_t stream, const char* name) {
+    const char* e = getenv("TFCUDA_GEMV_SPLIT");
+    if (e && e[0] == '1') return launch_gemv_stream_split<ST, 1>(ctx, p, stream, name);
+    return launch_gemv_stream_split<ST, 2>(ctx, p, stream, name);
+}
+
 template <typename ST>
 tf_status launch_gemv_tc(tf_context* ctx, const GtParams& p, cudaStream_t stream, const char* name) {
     const GtLayout L = gt_layout(p.K, p.R);
@@ -388,7 +627,7 @@ namespace tf {
 
 tf_status gemv_tc_try(tf_context* ctx, const void* W, const void* S, const void* B, uint64_t wbs, uint64_t sbs,
                       uint32_t batch, const void* x, void* y, uint64_t ybs, uint32_t m, uint32_t n,
-                      tf_scale_type st, cudaStream_t stream, int force, bool* used, const char* name) {
+                      tf_scale_type st, cudaStream_t stream, int kind, int force, bool* used, const char* name) {
     *used = false;
     if (n % 64 || n / 2 % 16) return TF_OK;
     if (st != TF_SCALE_BF16 && st != TF_SCALE_F16) return TF_OK;
@@ -397,7 +636,7 @@ tf_status gemv_tc_try(tf_context* ctx, const void* W, const void* S, const void*
     const long long jobs = (long long)tiles * batch;
     if (jobs > (1ll << 30)) return TF_OK;
     if (!force && jobs < ctx->num_sms) return TF_OK;  // too few tiles to fill the GPU: the engine splits K
-    const int R = gt_ring_stages((int)n);
+    const int R = kind == kGemvTensorCore ? gt_ring_stages((int)n) : gs_ring_stages((int)n);
     if (R < 2) return TF_OK;
     GtParams p;
     memset(&p, 0, sizeof(p));
@@ -416,8 +655,11 @@ tf_status gemv_tc_try(tf_context* ctx, const void* W, const void* S, const void*
     p.R = R;
     p.err = ctx->d_err;
     *used = true;
-    return st == TF_SCALE_BF16 ? launch_gemv_tc<__nv_bfloat16>(ctx, p, stream, name)
-                               : launch_gemv_tc<__half>(ctx, p, stream, name);
+    if (kind == kGemvTensorCore)
+        return st == TF_SCALE_BF16 ? launch_gemv_tc<__nv_bfloat16>(ctx, p, stream, name)
+                                   : launch_gemv_tc<__half>(ctx, p, stream, name);
+    return st == TF_SCALE_BF16 ? launch_gemv_stream<__nv_bfloat16>(ctx, p, stream, name)
+                               : launch_gemv_stream<__half>(ctx, p, stream, name);
 }
 
 }  // namespace tf

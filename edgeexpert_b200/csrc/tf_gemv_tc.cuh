@@ -8,13 +8,16 @@ struct tf_context;
 
 namespace tf {
 
-// Launches the tcgen05 GEMV for `batch` int4 matrices [m][n] sharing one fp16
-// activation vector when the shapes, alignments and shared memory allow it and
-// (unless `force`) there are at least as many 128-row tiles as SMs.  Sets
-// *used; returns TF_OK without launching when the path does not apply.
-// Selected by tf_int4_gemv / tf_affine_gemv_batched only under TFCUDA_GEMV=tc.
+enum : int { kGemvStream = 0, kGemvTensorCore = 1 };
+
+// Launches a ring-streamed GEMV for `batch` int4 matrices [m][n] sharing one
+// fp16 activation vector: kind kGemvStream = integer mma.sync consumers,
+// kGemvTensorCore = tcgen05 kind::i8 with the codes in TMEM.  Only when the
+// shapes, alignments and shared memory allow it and (unless `force`) there are
+// at least as many 128-row tiles as SMs.  Sets *used; returns TF_OK without
+// launching when the path does not apply.
 tf_status gemv_tc_try(tf_context* ctx, const void* W, const void* S, const void* B, uint64_t wbs, uint64_t sbs,
                       uint32_t batch, const void* x, void* y, uint64_t ybs, uint32_t m, uint32_t n,
-                      tf_scale_type st, cudaStream_t stream, int force, bool* used, const char* name);
+                      tf_scale_type st, cudaStream_t stream, int kind, int force, bool* used, const char* name);
 
 }  // namespace tf

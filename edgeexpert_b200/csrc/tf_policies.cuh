@@ -13,7 +13,10 @@
 
 namespace tf {
 
-__device__ __forceinline__ const uint8_t* engine_xarea() { return engine_smem_base() + engine_fixed_smem(); }
+// (a CTA wider than kWarps warps carries helper warps and a larger reduction area)
+__device__ __forceinline__ const uint8_t* engine_xarea() {
+    return engine_smem_base() + engine_fixed_smem(blockDim.x > kWarps * 32 ? 1 : 0);
+}
 
 // ===========================================================================
 // Plain affine GEMV, Y[tok][row] = sum_k W[row][k] * X[tok][k]

@@ -1,8 +1,9 @@
-"""GPU parity of the tensor-core one-token int4 GEMV (tf_gemv_tc.cu) against the oracle.
+"""GPU parity of the ring-streamed one-token int4 GEMVs (tf_gemv_tc.cu) against the oracle.
 
-The path is reached through the public entry points tf_int4_gemv and
-tf_affine_gemv_batched under TFCUDA_GEMV=tc (the streaming engine is the
-default for one token).
+Both kernels are reached through the public entry points tf_int4_gemv and
+tf_affine_gemv_batched: the integer mma.sync kernel ("stream", the default
+when a call has at least one 128-row tile per SM) and the tcgen05 kernel
+("tc", opt-in).  TFCUDA_GEMV forces either for any tile count.
 Tolerance: max relative error (RelError) <= 2e-3 for fp16 outputs, the
 reference's own kernel-vs-CPU bar (Tolerances.swift:4-21).
 """
@@ -48,25 +49,28 @@ def single(m, n, scale_type, label, uniform=False):
 
 @pytest.mark.parametrize("m,n", [(128, 128), (1024, 2816), (64, 64), (1408, 2816), (2816, 2112), (704, 2816),
                                  (2816, 704)])
-def test_tc_gemv_shapes(cuda, m, n, monkeypatch):
-    monkeypatch.setenv("TFCUDA_GEMV", "tc")
+@pytest.mark.parametrize("kind", ["stream", "tc"])
+def test_ring_gemv_shapes(cuda, m, n, kind, monkeypatch):
+    monkeypatch.setenv("TFCUDA_GEMV", kind)
     y, ref = single(m, n, 0, f"tc-{m}-{n}", uniform=True)
     assert O.rel_error(y, ref) < FP16_TOL
 
 
 @pytest.mark.parametrize("m", [1, 65, 129, 200])
 @pytest.mark.parametrize("n", [64, 192, 448, 512, 576, 1088])
-def test_tc_gemv_ragged(cuda, m, n, monkeypatch):
+@pytest.mark.parametrize("kind", ["stream", "tc"])
+def test_ring_gemv_ragged(cuda, m, n, kind, monkeypatch):
     # partial 128-row tiles (scale blocks that are not a multiple of 16 bytes),
     # stages with fewer than 8 groups, a second TMA box outside the row
-    monkeypatch.setenv("TFCUDA_GEMV", "tc")
+    monkeypatch.setenv("TFCUDA_GEMV", kind)
     y, ref = single(m, n, 0, f"tc-ragged-{m}-{n}", uniform=True)
     assert O.rel_error(y, ref) < FP16_TOL
 
 
+@pytest.mark.parametrize("kind", ["stream", "tc"])
 @pytest.mark.parametrize("scale_type", [0, 1])
-def test_tc_gemv_config0(cuda, scale_type, monkeypatch):
-    monkeypatch.setenv("TFCUDA_GEMV", "tc")
+def test_ring_gemv_config0(cuda, scale_type, kind, monkeypatch):
+    monkeypatch.setenv("TFCUDA_GEMV", kind)
     y, ref = single(1408, 2816, scale_type, f"tc-cfg0-{scale_type}")
     assert O.rel_error(y, ref) < FP16_TOL
 
@@ -98,20 +102,27 @@ def batched(batch, m, n, scale_type, label, pad_w=0, pad_s=0):
     return Yh
 
 
-def test_tc_gemv_batched_many_tiles(cuda, monkeypatch):
-    # 160 tiles: more jobs than SMs, each CTA runs several (persistent loop)
-    monkeypatch.setenv("TFCUDA_GEMV", "tc")
+@pytest.mark.parametrize("kind", ["", "tc"])
+def test_ring_gemv_batched_many_tiles(cuda, kind, monkeypatch):
+    # 160 tiles: more jobs than SMs, each CTA runs several (persistent loop);
+    # "" = the default selection (the integer ring kernel)
+    if kind:
+        monkeypatch.setenv("TFCUDA_GEMV", kind)
+    else:
+        monkeypatch.delenv("TFCUDA_GEMV", raising=False)
     batched(160, 128, 2816, 1, "tc-batched-auto")
 
 
+@pytest.mark.parametrize("kind", ["stream", "tc"])
 @pytest.mark.parametrize("pad_w,pad_s", [(0, 0), (48, 8), (4096, 24)])
-def test_tc_gemv_batched_strides(cuda, pad_w, pad_s, monkeypatch):
-    monkeypatch.setenv("TFCUDA_GEMV", "tc")
+def test_ring_gemv_batched_strides(cuda, pad_w, pad_s, kind, monkeypatch):
+    monkeypatch.setenv("TFCUDA_GEMV", kind)
     batched(5, 200, 1088, 0, f"tc-batched-{pad_w}-{pad_s}", pad_w, pad_s)
 
 
-def test_tc_gemv_matches_engine_and_is_deterministic(cuda, monkeypatch):
-    monkeypatch.setenv("TFCUDA_GEMV", "tc")
+@pytest.mark.parametrize("kind", ["stream", "tc"])
+def test_ring_gemv_matches_engine_and_is_deterministic(cuda, kind, monkeypatch):
+    monkeypatch.setenv("TFCUDA_GEMV", kind)
     a, _ = single(1408, 2816, 1, "tc-det")
     b, _ = single(1408, 2816, 1, "tc-det")
     assert np.array_equal(a, b)
