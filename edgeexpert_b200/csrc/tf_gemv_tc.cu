@@ -460,8 +460,7 @@ __global__ void __launch_bounds__(GsCfg<SPLIT>::kThreads, 1) gemv_stream_kernel(
             gt_load_jobs(p, r);
         }
     } else {
-        const int w = (warp - 1) & 7, half = (warp - 1) >> 3;
-        const int k0 = SPLIT == 2 ? half : 0, k1 = SPLIT == 2 ? half + 1 : 2;  // this warp's boxes
+        const int w = (warp - 1) & 7, half = (warp - 1) >> 3;  // row tile; box of the stage (SPLIT = 2)
         const int g = lane >> 2, t = lane & 3;
         const uint4* zeros = reinterpret_cast<const uint4*>(xb - 32);
         constexpr uint32_t kLo = 0x0F0F0F0Fu;
@@ -482,18 +481,13 @@ __global__ void __launch_bounds__(GsCfg<SPLIT>::kThreads, 1) gemv_stream_kernel(
                 if (!(ok = gwait(&sh.full[slot], (q / R) & 1u, sh.abort_flag, p.err))) break;
                 const uint8_t* rowA = ring + slot * kGtStage + (16 * w + g) * 128;
                 const int ng = min(8, ngK - 8 * st);
-                // the stage's 2 blocks of 4 groups (one TMA box each), MMA chains interleaved
-                int c[2][2][4];
+                // one block of 4 groups = one TMA box (k): two interleaved MMA
+                // chains; lane t ends with group t's dots
+                auto block = [&](const int k, int c[2][4]) {
 #pragma unroll
-                for (int k = 0; k < 2; ++k)
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) c[k][0][i] = c[k][1][i] = 0;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-#pragma unroll
-                    for (int k = 0; k < 2; ++k) {
+                    for (int j = 0; j < 4; ++j) {
                         const int gl = 4 * k + j;
-                        if (k >= k0 && k < k1 && gl < ng) {
+                        if (gl < ng) {
                             const int G = 8 * st + gl;
                             const uint4* xp = ((g >> 1) == j)
                                                   ? reinterpret_cast<const uint4*>(xb + (G * 4 + t) * 32) + (g & 1)
@@ -506,23 +500,35 @@ __global__ void __launch_bounds__(GsCfg<SPLIT>::kThreads, 1) gemv_stream_kernel(
                             const uint32_t a2 = wa.y & kLo, a3 = (wa.y >> 4) & kLo;
                             const uint32_t b0 = wb.x & kLo, b1 = (wb.x >> 4) & kLo;
                             const uint32_t b2 = wb.y & kLo, b3 = (wb.y >> 4) & kLo;
-                            imma16832(c[k][0], a0, b0, a1, b1, xv.x, xv.y);
-                            imma16832(c[k][1], a2, b2, a3, b3, xv.z, xv.w);
+                            imma16832(c[0], a0, b0, a1, b1, xv.x, xv.y);
+                            imma16832(c[1], a2, b2, a3, b3, xv.z, xv.w);
                         }
                     }
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&sh.empty[slot]);  // codes are in registers
-#pragma unroll
-                for (int k = 0; k < 2; ++k) {
-                    if (k >= k0 && k < k1 && 4 * k + t < ng) {
+                };
+                auto finish = [&](const int k, const int c[2][4]) {
+                    if (4 * k + t < ng) {
                         const int G = 8 * st + 4 * k + t;
                         const float xc = xsc[G], xm = xsum[G];
-                        const int dA = 128 * (c[k][0][0] + c[k][1][0]) + (c[k][0][1] + c[k][1][1]);
-                        const int dB = 128 * (c[k][0][2] + c[k][1][2]) + (c[k][0][3] + c[k][1][3]);
+                        const int dA = 128 * (c[0][0] + c[1][0]) + (c[0][1] + c[1][1]);
+                        const int dB = 128 * (c[0][2] + c[1][2]) + (c[0][3] + c[1][3]);
                         accA += scale_to_float(sA[G]) * ((float)dA * xc) + scale_to_float(bA[G]) * xm;
                         accB += scale_to_float(sB[G]) * ((float)dB * xc) + scale_to_float(bB[G]) * xm;
                     }
+                };
+                if constexpr (SPLIT == 2) {
+                    int c[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+                    block(half, c);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sh.empty[slot]);  // codes are in registers
+                    finish(half, c);
+                } else {
+                    int c0[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}}, c1[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+                    block(0, c0);
+                    block(1, c1);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sh.empty[slot]);
+                    finish(0, c0);
+                    finish(1, c1);
                 }
             }
             if (!ok) break;
