@@ -251,7 +251,9 @@ tf_status tf_context_check_device(tf_context* ctx, void* stream, uint32_t* flags
     if (e == cudaSuccess) e = cudaStreamSynchronize(cs);
     if (e != cudaSuccess) return cuda_check(ctx, e, "tf_context_check_device");
     if (flags_out) *flags_out = flags;
-    if (flags & kErrMbarTimeout) return fail(ctx, TF_ERR_TIMEOUT, "a bounded device wait gave up (flags=0x%x)", flags);
+    if (flags & kErrMbarTimeout)
+        return fail(ctx, TF_ERR_TIMEOUT, "a bounded device wait gave up (flags=0x%x, site %u, info 0x%08x)", flags,
+                    words[1], words[2]);
     if (flags & kErrBadExpert) return fail(ctx, TF_ERR_INVALID_ARG, "an expert id was out of range (flags=0x%x)", flags);
     if (flags & kErrAlign)
         return fail(ctx, TF_ERR_MISALIGNED, "misaligned access skipped at site %u, address 0x%08x%08x", words[1],

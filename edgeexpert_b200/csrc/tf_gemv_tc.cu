@@ -115,14 +115,23 @@ __device__ __forceinline__ int gt_bpos(int G, int e, int h) {
            ((((kb >> 4) ^ n) & 7) << 4) + (kb & 15);
 }
 
-__device__ __forceinline__ bool gwait(uint64_t* bar, uint32_t parity, int& abort_flag, uint32_t* err) {
+// Bounded wait; the first wait of the launch to give up records its source
+// line and (CTA << 20 | job << 10 | stage & 1023) in the status words 1-2.
+__device__ __forceinline__ bool gwait(uint64_t* bar, uint32_t parity, int& abort_flag, uint32_t* err, uint32_t site = 0,
+                                      uint32_t info = 0) {
     for (uint32_t i = 0; i < kGtSpin; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 255u) == 255u && *reinterpret_cast<volatile int*>(&abort_flag)) return false;
     }
     abort_flag = 1;
-    if (err) atomicOr(err, kErrMbarTimeout);
+    if (err && atomicOr(err, kErrMbarTimeout) == 0) {
+        err[1] = site;
+        err[2] = info;
+    }
     return false;
+}
+__device__ __forceinline__ uint32_t gt_info(int jl, uint32_t q) {
+    return (blockIdx.x << 20) | ((uint32_t)(jl & 1023) << 10) | (q & 1023u);
 }
 __device__ __forceinline__ bool gwait(uint64_t* bar, uint32_t parity, GtShared& sh, uint32_t* err) {
     return gwait(bar, parity, sh.abort_flag, err);
@@ -153,7 +162,7 @@ __device__ __forceinline__ void gt_load_jobs(const GtParams& p, const GtRing& r)
         const int b = job / p.tiles, row0 = (job - b * p.tiles) * kGtRows;
         const int rows = min(kGtRows, p.M - row0);
         const int js = jl & 1;
-        if (!gwait(&r.sempty[js], ((jl >> 1) & 1) ^ 1, *r.abort_flag, p.err)) return;
+        if (!gwait(&r.sempty[js], ((jl >> 1) & 1) ^ 1, *r.abort_flag, p.err, __LINE__, gt_info(jl, q))) return;
         const uint32_t nbytes = (uint32_t)rows * ngK * 2, bulk = nbytes & ~15u;
         const size_t off = (size_t)b * p.sb_bstride + (size_t)row0 * ngK * 2;
         uint8_t* ds = r.scl + (2 * js) * r.sslot;
@@ -169,7 +178,7 @@ __device__ __forceinline__ void gt_load_jobs(const GtParams& p, const GtRing& r)
         }
         for (int st = 0; st < nst; ++st, ++q) {
             const int slot = (int)(q % (uint32_t)R);
-            if (!gwait(&r.empty[slot], ((q / R) & 1) ^ 1, *r.abort_flag, p.err)) return;
+            if (!gwait(&r.empty[slot], ((q / R) & 1) ^ 1, *r.abort_flag, p.err, __LINE__, gt_info(jl, q))) return;
             const int x0 = st * 256;
             const bool two = x0 + 128 < p.K / 2;
             mbar_arrive_expect_tx(&r.full[slot], two ? 2 * kGtBox : kGtBox);
@@ -397,7 +406,8 @@ struct GsShared {
     uint64_t full[kGtMaxR], empty[kGtMaxR];
     uint64_t sfull[2], sempty[2];
     uint64_t pdone[8];       // SPLIT = 2: row tile w's second-half sums written
-    float part[2][kGtRows];  // SPLIT = 2: second-half row sums, by job parity
+    uint64_t pfree[8];       // SPLIT = 2: ... and read by the first-half warp
+    float part[kGtRows];     // SPLIT = 2: second-half row sums of the current job
     int abort_flag;
 };
 
@@ -445,7 +455,10 @@ __global__ void __launch_bounds__(GsCfg<SPLIT>::kThreads, 1) gemv_stream_kernel(
             mbar_init(&sh.sfull[a], 1);
             mbar_init(&sh.sempty[a], kConsumers);
         }
-        for (int a = 0; a < 8; ++a) mbar_init(&sh.pdone[a], 1);
+        for (int a = 0; a < 8; ++a) {
+            mbar_init(&sh.pdone[a], 1);
+            mbar_init(&sh.pfree[a], 1);
+        }
         sh.abort_flag = 0;
         fence_mbar_init();
         prefetch_tmap(&p.wmap);
@@ -470,7 +483,7 @@ __global__ void __launch_bounds__(GsCfg<SPLIT>::kThreads, 1) gemv_stream_kernel(
         for (int job = blockIdx.x; ok && job < p.jobs; job += gridDim.x, ++jl) {
             const int b = job / p.tiles, row0 = (job - b * p.tiles) * kGtRows;
             const int js = jl & 1;
-            if (!(ok = gwait(&sh.sfull[js], (jl >> 1) & 1, sh.abort_flag, p.err))) break;
+            if (!(ok = gwait(&sh.sfull[js], (jl >> 1) & 1, sh.abort_flag, p.err, __LINE__, gt_info(jl, q)))) break;
             const ST* sA = reinterpret_cast<const ST*>(scl + (2 * js) * L.sslot) + (16 * w + g) * ngK;
             const ST* bA = reinterpret_cast<const ST*>(scl + (2 * js + 1) * L.sslot) + (16 * w + g) * ngK;
             const ST* sB = sA + 8 * ngK;
@@ -478,7 +491,7 @@ __global__ void __launch_bounds__(GsCfg<SPLIT>::kThreads, 1) gemv_stream_kernel(
             float accA = 0.f, accB = 0.f;
             for (int st = 0; st < nst; ++st, ++q) {
                 const int slot = (int)(q % (uint32_t)R);
-                if (!(ok = gwait(&sh.full[slot], (q / R) & 1u, sh.abort_flag, p.err))) break;
+                if (!(ok = gwait(&sh.full[slot], (q / R) & 1u, sh.abort_flag, p.err, __LINE__, gt_info(jl, q)))) break;
                 const uint8_t* rowA = ring + slot * kGtStage + (16 * w + g) * 128;
                 const int ng = min(8, ngK - 8 * st);
                 // one block of 4 groups = one TMA box (k): two interleaved MMA
@@ -537,11 +550,15 @@ __global__ void __launch_bounds__(GsCfg<SPLIT>::kThreads, 1) gemv_stream_kernel(
             accB += __shfl_xor_sync(0xffffffffu, accB, 1);
             accB += __shfl_xor_sync(0xffffffffu, accB, 2);
             if constexpr (SPLIT == 2) {
-                // the second-half warp hands its row sums over; the slot of
-                // job jl is rewritten only after both warps released job jl's
-                // scales (sempty), i.e. after the first-half warp read it
-                float* part = sh.part[jl & 1];
+                // the second-half warp hands its row sums over (pdone) and
+                // writes the next job's only after the first-half warp read
+                // them (pfree): with jobs shorter than the ring a warp can run
+                // two jobs ahead of its partner, so a one-way barrier's parity
+                // would wrap
+                float* part = sh.part;
                 if (half == 1) {
+                    if (!(ok = gwait(&sh.pfree[w], (jl & 1) ^ 1, sh.abort_flag, p.err, __LINE__, gt_info(jl, q))))
+                        break;
                     if (t == 0) {
                         part[16 * w + g] = accA;
                         part[16 * w + 8 + g] = accB;
@@ -553,9 +570,11 @@ __global__ void __launch_bounds__(GsCfg<SPLIT>::kThreads, 1) gemv_stream_kernel(
                     }
                     continue;
                 }
-                if (!(ok = gwait(&sh.pdone[w], jl & 1, sh.abort_flag, p.err))) break;
+                if (!(ok = gwait(&sh.pdone[w], jl & 1, sh.abort_flag, p.err, __LINE__, gt_info(jl, q)))) break;
                 accA += part[16 * w + g];
                 accB += part[16 * w + 8 + g];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sh.pfree[w]);
             }
             const int rA = row0 + 16 * w + g;
             __half* yb = p.y + (long long)b * p.y_bstride;

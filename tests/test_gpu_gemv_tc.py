@@ -132,3 +132,13 @@ def test_ring_gemv_matches_engine_and_is_deterministic(cuda, kind, monkeypatch):
     # differ only in fp32 summation order
     assert O.rel_error(a, e) < 1e-3
     assert O.rel_error(e, ref) < FP16_TOL
+
+
+@pytest.mark.parametrize("batch,m,n", [(300, 128, 2816), (100, 200, 1088), (149, 1408, 704)])
+def test_stream_gemv_many_jobs_per_cta(cuda, batch, m, n, monkeypatch):
+    # several jobs per CTA, some shorter than the stage ring (K = 704: two
+    # stages), so a consumer warp can run jobs ahead of its partner
+    monkeypatch.delenv("TFCUDA_GEMV", raising=False)
+    a = batched(batch, m, n, 1, f"many-{batch}-{m}-{n}")
+    b = batched(batch, m, n, 1, f"many-{batch}-{m}-{n}")
+    assert np.array_equal(a, b)
