@@ -564,7 +564,7 @@ def run_gemv(a, rank, world, local_rank):
             "single_gemv_us": single_us, "single_gemv_gbs": G_BYTES / (single_us * 1e-6) / 1e9,
             "e2e": {"value": world * per_step / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": G_N * 2,
                     "d2h_bytes_per_step": R * G_M * 2},
-            "roofline": {"bound": "hbm", "kernel": "engine_kernel<GemvPolicy> (batched)", "achieved": achieved,
+            "roofline": {"bound": "hbm", "kernel": "gemv_stream_kernel (ring-streamed integer GEMV, 16 mma.sync consumer warps)", "achieved": achieved,
                          "peak": peak, "peak_source": src, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": traffic, "bytes_per_launch": per_step, "us_per_launch": ms * 1e3},
             "cpu_baseline": cpu, "clocks": clk, "gpu_launches": a.steps,
