@@ -284,24 +284,45 @@ __device__ __forceinline__ void stage_words(const __half* __restrict__ x, int x_
                                             uint32_t* xs, bool vec, bool fold, int tid, int nthreads) {
     const int octets = K / 8;
     const int ws = x_words_stride(K);
+    const int n = ntok * octets;
     const __half2 sixteenth = __float2half2_rn(0.0625f);
-    for (int i = tid; i < ntok * octets; i += nthreads) {
-        const int t = i / octets, q = i - t * octets;
-        const __half* src = x + (size_t)t * x_row_stride + q * 8;
-        __half h[8];
-        if (vec) {
-            const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(src));  // L2: may be another CTA's output
-            memcpy(h, &raw, 16);
-        } else {
+    // up to U octets per thread: every load of the round is issued before the
+    // first is used, so the round costs one L2 latency
+    constexpr int U = 4;
+    for (int base = tid; base < n; base += U * nthreads) {
+        uint4 raw[U];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) h[j] = __ldcg(src + j);
+        for (int u = 0; u < U; ++u) {
+            const int i = base + u * nthreads;
+            raw[u] = make_uint4(0u, 0u, 0u, 0u);
+            if (i < n) {
+                const int t = i / octets, q = i - t * octets;
+                const __half* src = x + (size_t)t * x_row_stride + q * 8;
+                if (vec) {
+                    raw[u] = __ldcg(reinterpret_cast<const uint4*>(src));  // L2: may be another CTA's output
+                } else {
+                    __half h[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) h[j] = __ldcg(src + j);
+                    memcpy(&raw[u], h, 16);
+                }
+            }
         }
-        uint32_t* dst = xs + t * ws + q * 4;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            __half2 p = __halves2half2(h[j], h[j + 4]);
-            if (fold && (j & 1)) p = __hmul2(p, sixteenth);
-            dst[j] = *reinterpret_cast<uint32_t*>(&p);
+        for (int u = 0; u < U; ++u) {
+            const int i = base + u * nthreads;
+            if (i < n) {
+                const int t = i / octets, q = i - t * octets;
+                __half h[8];
+                memcpy(h, &raw[u], 16);
+                uint32_t* dst = xs + t * ws + q * 4;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    __half2 p = __halves2half2(h[j], h[j + 4]);
+                    if (fold && (j & 1)) p = __hmul2(p, sixteenth);
+                    dst[j] = *reinterpret_cast<uint32_t*>(&p);
+                }
+            }
         }
     }
 }
@@ -321,33 +342,59 @@ __device__ __forceinline__ int x8_offset(int e) {
     return tq * 32 + word * 4 + byte;
 }
 
-__device__ __forceinline__ void stage_x_int(const __half* __restrict__ x, int K, uint32_t* xs, float* xsum, float* xsc,
-                                            int tid, int nthreads) {
-    const int ng = K / kGroup;
+// `nrows` rows x + r * x_rs, row r to xs + r * xs_rw words with its group
+// sums / scales at xsum / xsc + r * K/64.  Up to U groups per warp per round,
+// all their loads issued before the first is used.
+__device__ __forceinline__ void stage_x_int_rows(const __half* __restrict__ x, int x_rs, int nrows, int K, uint32_t* xs,
+                                                 int xs_rw, float* xsum, float* xsc, int tid, int nthreads) {
+    const int ng = K / kGroup, total = nrows * ng;
     const int warp = tid >> 5, lane = tid & 31, nw = nthreads >> 5;
-    uint8_t* xb = reinterpret_cast<uint8_t*>(xs);
-    for (int g = warp; g < ng; g += nw) {
-        const float a = __half2float(__ldcg(x + g * 64 + 2 * lane));
-        const float b = __half2float(__ldcg(x + g * 64 + 2 * lane + 1));
-        float m = fmaxf(fabsf(a), fabsf(b)), sum = a + b;
+    constexpr int U = 4;
+    for (int base = warp; base < total; base += U * nw) {
+        float va[U], vb[U];
 #pragma unroll
-        for (int o = 16; o; o >>= 1) {
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        for (int u = 0; u < U; ++u) {
+            const int i = base + u * nw;
+            va[u] = vb[u] = 0.f;
+            if (i < total) {
+                const int r = i / ng, g = i - r * ng;
+                const __half* src = x + (size_t)r * x_rs + g * 64 + 2 * lane;
+                va[u] = __half2float(__ldcg(src));
+                vb[u] = __half2float(__ldcg(src + 1));
+            }
         }
-        const float q = m > 0.f ? 16383.0f / m : 0.f;
-        const int XA = __float2int_rn(a * q), XB = __float2int_rn(b * q);
-        uint8_t* gb = xb + g * 128;
-        const int e0 = 2 * lane, e1 = e0 + 1;
-        gb[x8_offset(e0)] = (uint8_t)(XA >> 7);
-        gb[x8_offset(e0) + 16] = (uint8_t)(XA & 127);
-        gb[x8_offset(e1)] = (uint8_t)(XB >> 7);
-        gb[x8_offset(e1) + 16] = (uint8_t)(XB & 127);
-        if (lane == 0) {
-            xsum[g] = sum;
-            xsc[g] = m / 16383.0f;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int i = base + u * nw;
+            if (i < total) {  // warp-uniform
+                const int r = i / ng, g = i - r * ng;
+                const float a = va[u], b = vb[u];
+                float m = fmaxf(fabsf(a), fabsf(b)), sum = a + b;
+#pragma unroll
+                for (int o = 16; o; o >>= 1) {
+                    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+                }
+                const float q = m > 0.f ? 16383.0f / m : 0.f;
+                const int XA = __float2int_rn(a * q), XB = __float2int_rn(b * q);
+                uint8_t* gb = reinterpret_cast<uint8_t*>(xs + (size_t)r * xs_rw) + g * 128;
+                const int e0 = 2 * lane, e1 = e0 + 1;
+                gb[x8_offset(e0)] = (uint8_t)(XA >> 7);
+                gb[x8_offset(e0) + 16] = (uint8_t)(XA & 127);
+                gb[x8_offset(e1)] = (uint8_t)(XB >> 7);
+                gb[x8_offset(e1) + 16] = (uint8_t)(XB & 127);
+                if (lane == 0) {
+                    xsum[r * ng + g] = sum;
+                    xsc[r * ng + g] = m / 16383.0f;
+                }
+            }
         }
     }
+}
+
+__device__ __forceinline__ void stage_x_int(const __half* __restrict__ x, int K, uint32_t* xs, float* xsum, float* xsc,
+                                            int tid, int nthreads) {
+    stage_x_int_rows(x, 0, 1, K, xs, 0, xsum, xsc, tid, nthreads);
 }
 
 // D += A(u8, 16x32) * B(s8, 32x8), int32 accumulate

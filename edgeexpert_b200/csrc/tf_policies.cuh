@@ -377,9 +377,9 @@ struct Phase2Policy {
         float* xsums = reinterpret_cast<float*>(xss + x_words_stride(p.Fs));
         if (p.xint) {
             const int ngF = p.F / kGroup;
-            for (int sl = 0; sl < p.top_k; ++sl)
-                stage_x_int(p.acts + (size_t)sl * p.F, p.F, xs + (size_t)sl * x_words_stride(p.F), xsum + sl * ngF,
-                            xsum + p.top_k * ngF + sl * ngF, tid, nt);
+            if (p.top_k)
+                stage_x_int_rows(p.acts, p.F, p.top_k, p.F, xs, x_words_stride(p.F), xsum, xsum + p.top_k * ngF, tid,
+                                 nt);
             if (p.has_shared) stage_x_int(p.shared_act, p.Fs, xss, xsums, xsums + p.Fs / kGroup, tid, nt);
             return;
         }
