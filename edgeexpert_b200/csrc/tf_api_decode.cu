@@ -66,10 +66,10 @@ tf_status check_source(tf_context* ctx, const void* pool, const void* ids, const
 }
 
 // Batch-1 int4 work on the integer tensor path (activation as a 15-bit
-// per-group integer in two int8 halves, mma.sync u8 x s8).  Measured on
-// B200: +1.4 % for the plain GEMV, -3 % for the decode phases (their
-// staging is on the critical path), so the default is on for the GEMV and
-// off for the phases; TFCUDA_XINT=1 / 0 forces it everywhere.
+// per-group integer in two int8 halves, mma.sync u8 x s8, 4 groups x {hi, lo}
+// per 8 MMA columns).  The default for the GEMV and, with a helper warp per
+// stage and load-batched staging, for the decode phases (measured faster on
+// B200 than the fp16 path for both); TFCUDA_XINT=0 / 1 forces it off / on.
 static bool xint_enabled(bool default_on) {
     const char* e = getenv("TFCUDA_XINT");
     if (e && e[0] == '1') return true;
@@ -366,7 +366,7 @@ static tf_status phase1_launch(tf_context* ctx, const ExpertSource& src, const v
     p.err = ctx->d_err;
     p.fjobs = (int)f / 8;
     p.lazy_ids = (lazy_ids && sg && top_k && src.ids != nullptr && !src.ids_in_smem) ? 1 : 0;
-    p.xint = ((!sg || sg->bits == 4) && xint_enabled(false)) ? 1 : 0;
+    p.xint = ((!sg || sg->bits == 4) && xint_enabled(true)) ? 1 : 0;
     if (p.lazy_ids)  // shared jobs first: they need no routing
         p.sched = make_sched((int)sg->rows / 8, units_for_K((int)d, (int)sg->bits), (int)top_k * p.fjobs,
                              units_for_K((int)d, 4), ctx->num_sms);
@@ -380,6 +380,11 @@ static tf_status phase1_launch(tf_context* ctx, const ExpertSource& src, const v
     }
     return dispatch_scale(st, [&](auto tag) {
         using ST = decltype(tag);
+        // integer path: a helper warp per stage halves each unit's latency
+        const size_t xb1 = Phase1Policy<ST>::x_bytes((int)d);
+        if (p.xint && p.aligned && helpers_enabled() &&
+            engine_fixed_smem(1) + xb1 + 1024 <= engine_smem_limit<Phase1Policy<ST>, ST, 1>(ctx))
+            return launch_engine<Phase1Policy<ST>, ST, 1>(ctx, p, xb1, sj, cs, name);
         return launch_engine<Phase1Policy<ST>, ST>(ctx, p, Phase1Policy<ST>::x_bytes((int)d), sj, cs, name);
     });
 }
@@ -415,7 +420,7 @@ static tf_status phase2_launch(tf_context* ctx, const ExpertSource& src, const v
         if (!aligned16(shared_act)) return fail(ctx, TF_ERR_MISALIGNED, "%s: shared act must be 16-byte aligned", name);
     }
     p.aligned = aligned;
-    p.xint = ((!sdn || sdn->bits == 4) && xint_enabled(false)) ? 1 : 0;
+    p.xint = ((!sdn || sdn->bits == 4) && xint_enabled(true)) ? 1 : 0;
     p.err = ctx->d_err;
     const int U = (int)top_k * units_for_K((int)f, 4) + (sdn ? units_for_K((int)sdn->cols, (int)sdn->bits) : 0);
     p.upf = units_for_K((int)f, 4);
@@ -428,6 +433,10 @@ static tf_status phase2_launch(tf_context* ctx, const ExpertSource& src, const v
     return dispatch_scale(st, [&](auto tag) {
         using ST = decltype(tag);
         xb = Phase2Policy<ST>::x_bytes((int)top_k, (int)f, sdn ? (int)sdn->cols : 0);
+        // (when the activations still fit beside the helpers' larger reduction area)
+        if (p.xint && p.aligned && helpers_enabled() &&
+            engine_fixed_smem(1) + xb + 1024 <= engine_smem_limit<Phase2Policy<ST>, ST, 1>(ctx))
+            return launch_engine<Phase2Policy<ST>, ST, 1>(ctx, p, xb, sj, cs, name);
         return launch_engine<Phase2Policy<ST>, ST>(ctx, p, xb, sj, cs, name);
     });
 }

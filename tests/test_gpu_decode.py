@@ -293,7 +293,7 @@ def test_shared_expert(cuda, bits, D, Fs):
     assert O.rel_error(O.f16_to_f32(f16(y)), y32_ref) < FP16_TOL
 
 
-@pytest.mark.parametrize("xint", ["", "1"])
+@pytest.mark.parametrize("xint", ["", "0"])
 @pytest.mark.parametrize("fused", [False, True])
 def test_moe_decode_layer_config1(cuda, fused, xint, monkeypatch):
     """BASELINE config 1 at full shape: router int8 128x2816 -> top-8 -> routed
@@ -301,7 +301,7 @@ def test_moe_decode_layer_config1(cuda, fused, xint, monkeypatch):
     near tie), output within 2e-3 of the oracle layer.  Both the default
     three-launch path and the single cooperative launch (TFCUDA_FUSED=1)."""
     monkeypatch.setenv("TFCUDA_FUSED", "1" if fused else "0")
-    if xint:  # batch-1 phases on the integer tensor path (u8 codes x 15-bit activation)
+    if xint:  # "0": batch-1 phases on the fp16 path instead of the integer default
         monkeypatch.setenv("TFCUDA_XINT", xint)
     from edgeexpert_b200.moe import (ExpertPool, MoELayerWeights, SharedExpertProjection, moe_decode_layer)
     E, D, F, Fs = 128, 2816, 704, 2112
