@@ -519,9 +519,11 @@ __device__ __forceinline__ int warp_unit(const SuperJob& s, int w, int i) {
 }
 
 // Shared-memory layout of the engine (bytes), H = helper warps per stage (0/1):
-//   [stages: kWarps * kStageBytes (1 KB aligned)][red: 2 * (1 + H) * kWarps * 32 * 4 floats]
+//   [stages: kWarps * kStageBytes (1 KB aligned)][red: 2 * (1 + H) * kWarps * 32 * (H ? 2 : 4) floats]
 //   [bars: kWarps u64][32 zero bytes][x area: Pol::x_bytes(p)]
-__host__ __device__ inline size_t engine_red_floats(int H) { return (size_t)2 * (1 + H) * kWarps * 32 * 4; }
+// (with helper warps only the batch-1 integer path runs, whose lanes hold two
+// non-zero partial sums, so a slot is a float2)
+__host__ __device__ inline size_t engine_red_floats(int H) { return (size_t)2 * (1 + H) * kWarps * 32 * (H ? 2 : 4); }
 __host__ __device__ inline size_t engine_fixed_smem(int H = 0) {
     return (size_t)kWarps * kStageBytes + engine_red_floats(H) * sizeof(float) + kWarps * 8 + 32;
 }
@@ -673,8 +675,12 @@ __device__ __forceinline__ void run_phase(const typename Pol::Params& p, EngineS
             if (p.aligned) ++es.seq;
             if (p.aligned && !es.dead && !helper) load_next();
         }
-        float* rb = red + (size_t)es.parity_buf * kW * 32 * 4;
-        *reinterpret_cast<float4*>(rb + (warp * 32 + lane) * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        constexpr int kSlot = H ? 2 : 4;  // floats per lane slot
+        float* rb = red + (size_t)es.parity_buf * kW * 32 * kSlot;
+        if constexpr (H != 0)
+            *reinterpret_cast<float2*>(rb + (warp * 32 + lane) * 2) = make_float2(acc[0], acc[2]);
+        else
+            *reinterpret_cast<float4*>(rb + (warp * 32 + lane) * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
         __syncthreads();
         // Leaders: for J > 1 warp jj*U reduces job jj over warps jj*U..jj*U+U-1;
         // for J == 1 warp 0 reduces warps 0..min(U,kWarps)-1.
@@ -688,11 +694,17 @@ __device__ __forceinline__ void run_phase(const typename Pol::Params& p, EngineS
             for (int w = w0; w < w0 + wn; ++w) {
 #pragma unroll
                 for (int h = 0; h <= H; ++h) {
-                    const float4 q = *reinterpret_cast<const float4*>(rb + ((w + h * kWarps) * 32 + lane) * 4);
-                    f[0] += q.x;
-                    f[1] += q.y;
-                    f[2] += q.z;
-                    f[3] += q.w;
+                    if constexpr (H != 0) {
+                        const float2 q = *reinterpret_cast<const float2*>(rb + ((w + h * kWarps) * 32 + lane) * 2);
+                        f[0] += q.x;
+                        f[2] += q.y;
+                    } else {
+                        const float4 q = *reinterpret_cast<const float4*>(rb + (w * 32 + lane) * 4);
+                        f[0] += q.x;
+                        f[1] += q.y;
+                        f[2] += q.z;
+                        f[3] += q.w;
+                    }
                 }
             }
             Pol::epilogue(p, sj.j0 + jj, f, lane);
