@@ -50,11 +50,14 @@ def parse():
     ap.add_argument("--scale-dtype", choices=["bf16", "f16"], default=None,
                     help="scale/bias storage; default fp16 for config 0 (as BASELINE states it), else bf16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemv", action="store_true", help="decode: skip the config-0 GEMV sub-record")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--workload", choices=["decode", "gemv", "batched", "prefill", "ep"], default="decode",
-                    help="decode = config 1 (default, the headline); gemv = config 0 (int4 GEMV 1408x2816 "
-                         "streamed from HBM); batched = config 2 (64 tokens); prefill = config 3 (4096 tokens); "
-                         "ep = config-4 MoE decode batch with the routed experts sharded over the GPUs")
+    ap.add_argument("--workload", choices=["moe", "decode", "gemv", "batched", "prefill", "ep"], default="moe",
+                    help="moe (default) = config-4 MoE decode step at batch 256/32/1 through 30 layers, experts "
+                         "sharded over the GPUs (plus, on one GPU, the batch-1 roofline and the config-0 GEMV); "
+                         "decode = config 1 (batch 1, GB/s); gemv = config 0 (int4 GEMV 1408x2816 streamed from "
+                         "HBM); batched = config 2 (64 tokens); prefill = config 3 (4096 tokens); ep = one layer "
+                         "of the expert-parallel batch")
     ap.add_argument("--matrices", type=int, default=256, help="gemv: distinct weight matrices per step")
     ap.add_argument("--tokens", type=int, default=0, help="override the chunk's token count (batched/prefill)")
     return ap.parse_args()
@@ -122,7 +125,18 @@ def host_threads() -> int:
     except (AttributeError, OSError):
         return os.cpu_count() or 1
 
-def cpu_sample(seconds: float, label: str = "cpu"):
+def cpu_model() -> str:
+    """The host CPU's model name (the `lscpu` "Model name" line)."""
+    try:
+        for ln in Path("/proc/cpuinfo").read_text().splitlines():
+            if ln.startswith("model name"):
+                return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_sample(seconds: float, label: str = "cpu", threads: int | None = None):
     """Oracle port of the reference CPU math on the host cores: router + top-8
     + 8 routed experts + shared expert for one token of one config-1 layer,
     repeated for ~`seconds`.  Returns (layer-tokens/s, threads, sample text)."""
@@ -130,7 +144,7 @@ def cpu_sample(seconds: float, label: str = "cpu"):
     import numpy as np
 
     import oracle as O
-    threads = host_threads()
+    threads = threads or host_threads()
     rng = O.seed_tree(0, f"bench-{label}")
     W8, S8, B8 = rng.synthetic_affine(E, D, 8, 0)
     es = O.bf16_bits(np.full(D, D ** -0.5, np.float32))
@@ -188,6 +202,23 @@ def run_reference(a, rank):
                           "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
               flush=True)
         return
+    if a.workload == "moe":
+        rec = cpu_baseline_record(lambda sec, th: cpu_sample(sec, "reference", th), 1e9 / a.layers,
+                                  max(10.0, a.cpu_seconds), unit="tok/s")
+        v = rec["value"]
+        B = a.tokens or MOE_BATCHES[0]
+        rec["sample"] += f"; tok/s = layer-tokens/s / {a.layers} layers"
+        print(json.dumps({
+            "metric": METRIC, "value": v, "unit": "tok/s", "impl": "reference", "n_gpus": a.gpus, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": B / v * 1e3, "tok_s": v, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32-acc/int4",
+            "data": "synthetic (BASELINE config-1 distributions, SplitMix64 seed 0)",
+            "config": {"workload": f"config-4 MoE decode step: batch {B} through {a.layers} config-1 MoE layers "
+                                   "(the reference's per-token CPU math, oracle port)", "global_batch": B,
+                       "layers": a.layers},
+            "cpu_baseline": rec,
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
+        return
     lps, threads, sample = cpu_sample(max(5.0, a.cpu_seconds), "reference")
     if a.workload != "decode":
         T = a.tokens or CHUNK_TOKENS[a.workload]
@@ -224,7 +255,9 @@ def run_reference(a, rank):
 
 
 # ---------------------------------------------------------------- GPU arm ---
-def run_ours(a, rank, world, local_rank):
+def run_ours(a, rank, world, local_rank, emit: bool = True, layers=None):
+    """Config 1: batch-1 decode through `--layers` distinct MoE layers (GB/s).
+    `layers` reuses already-built layer weights."""
     import torch
     import torch.distributed as dist
 
@@ -238,9 +271,10 @@ def run_ours(a, rank, world, local_rank):
     sdt = torch.bfloat16 if a.scale_dtype == "bf16" else torch.float16
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
-    layers = [synthetic_moe_layer(D, F, FS, E, TOPK, 4, sdt, dev, gen) for _ in range(a.layers)]
+    if layers is None:
+        layers = [synthetic_moe_layer(D, F, FS, E, TOPK, 4, sdt, dev, gen) for _ in range(a.layers)]
     c_layers = [L.as_c() for L in layers]
-    L, R = a.layers, a.ring
+    L, R = len(layers), a.ring
     x_ring = torch.randn(R, L, D, device=dev, generator=gen).to(torch.float16)
     y = torch.empty(L, D, dtype=torch.float16, device=dev)
     ids = torch.empty(L, TOPK, dtype=torch.int32, device=dev)
@@ -374,9 +408,8 @@ def run_ours(a, rank, world, local_rank):
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        lps, threads, sample = cpu_sample(a.cpu_seconds)
-        cpu = {"value": lps * layer_bytes() / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": sample}
+        cpu = cpu_baseline_record(lambda sec, th: cpu_sample(sec, "cpu", th), layer_bytes(),
+                                  a.cpu_seconds if emit else min(a.cpu_seconds, 8.0))
 
     if rank == 0:
         line = {
@@ -400,7 +433,9 @@ def run_ours(a, rank, world, local_rank):
             "clocks": clk,
             "gpu_launches": launches_per_step * a.steps,
         }
-        print(json.dumps(line), flush=True)
+        if emit:
+            print(json.dumps(line), flush=True)
+        return line
 
 
 # --------------------------------------------------------- config 0 GEMV ----
@@ -408,11 +443,11 @@ G_M, G_N = 1408, 2816
 G_BYTES = G_M * G_N // 2 + 2 * G_M * (G_N // 64) * 2 + G_N * 2 + G_M * 2  # 2,238,720 B (W + s/b + x + y)
 
 
-def gemv_cpu_sample(seconds: float):
+def gemv_cpu_sample(seconds: float, threads: int | None = None):
     """Oracle port of the reference's int4 GEMV (kernel order) on the host cores."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle as O
-    threads = host_threads()
+    threads = threads or host_threads()
     rng = O.seed_tree(0, "bench-gemv")
     W, S, B = rng.synthetic_affine(G_M, G_N, 4, 1)
     x = rng.normal_f16(G_N)
@@ -426,7 +461,20 @@ def gemv_cpu_sample(seconds: float):
     return n / el, threads, f"{n} config-0 GEMVs (1408x2816 int4 g64, fp16 scales) in {el:.1f} s"
 
 
-def run_gemv(a, rank, world, local_rank):
+def cpu_baseline_record(sampler, unit_bytes: float, seconds: float, unit: str = "GB/s") -> dict:
+    """The oracle port timed twice on the host: one thread, then every host
+    thread; `value` is the all-thread figure.  sampler(seconds, threads)
+    returns (units/s, threads, sample text); unit_bytes scales units to bytes."""
+    half = max(2.0, seconds / 2)
+    u1, _, s1 = sampler(half, 1)
+    un, thr, sn = sampler(half, host_threads())
+    return {"value": un * unit_bytes / 1e9, "unit": unit, "cores": thr, "kind": "port",
+            "sample": f"all threads: {sn}; 1 thread: {s1}",
+            "single_thread": {"value": u1 * unit_bytes / 1e9, "unit": unit, "cores": 1},
+            "cpu_model": cpu_model()}
+
+
+def run_gemv(a, rank, world, local_rank, emit: bool = True):
     """Config 0: the int4 g64 GEMV 1408x2816 over `--matrices` distinct,
     HBM-resident weight matrices (> L2 in total), one batched launch per step."""
     import torch
@@ -545,8 +593,7 @@ def run_gemv(a, rank, world, local_rank):
     achieved = per_step / (ms * 1e-3) / 1e9
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        gps, threads, sample = gemv_cpu_sample(a.cpu_seconds)
-        cpu = {"value": gps * G_BYTES / 1e9, "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample}
+        cpu = cpu_baseline_record(gemv_cpu_sample, G_BYTES, a.cpu_seconds if emit else min(a.cpu_seconds, 6.0))
     traffic = None
     tr = ROOT / "profiles" / "gemv_traffic.json"
     if tr.exists():
@@ -569,7 +616,9 @@ def run_gemv(a, rank, world, local_rank):
                          "traffic": traffic, "bytes_per_launch": per_step, "us_per_launch": ms * 1e3},
             "cpu_baseline": cpu, "clocks": clk, "gpu_launches": a.steps,
         }
-        print(json.dumps(line), flush=True)
+        if emit:
+            print(json.dumps(line), flush=True)
+        return line
 
 
 # ------------------------------------------------- expert parallel (EP) ----
@@ -673,6 +722,307 @@ def run_ep(a, rank, world, local_rank):
             "e2e": None, "roofline": None, "cpu_baseline": None, "clocks": clk,
             "gpu_launches": None,
         }), flush=True)
+
+
+# ------------------------------------------- MoE decode stack (default) ----
+MOE_BATCHES = (256, 32, 1)
+
+
+def tokens_of(B: int, world: int, rank: int) -> int:
+    """Tokens rank `rank` owns of a global decode batch B (DP split)."""
+    return B // world + (1 if rank < B % world else 0)
+
+
+def moe_step_bytes(B: int, world: int, distinct_local: float, L: int) -> float:
+    """Algorithmic HBM bytes one GPU reads in one step of a batch-B decode
+    through L MoE layers: router + shared expert (replicated) + every local
+    routed expert the batch hits, once."""
+    from edgeexpert_b200.format import affine_bytes
+    expert = 2 * affine_bytes(F, D) + affine_bytes(D, F)
+    shared = 2 * affine_bytes(FS, D) + affine_bytes(D, FS)
+    router = affine_bytes(E, D, 8)
+    return L * (router + shared + distinct_local * expert)
+
+
+def run_moe(a, rank, world, local_rank):
+    """Config-4-shaped decode through `--layers` (30) config-1 MoE layers at
+    global batches 256, 32 and 1, experts sharded E/N per GPU and tokens split
+    B/N per GPU (strong scaling: the batch is fixed as N grows).  Per layer and
+    rank: batched router over its tokens, the routed experts (N=1: device sort
+    + grouped int4 GEMMs + token-major reduce; N>1: fixed-capacity NCCL
+    all-to-all dispatch / combine), the shared expert over its tokens.  Batch
+    1 on one GPU runs the fused decode layer (tf_moe_decode_layer).  Each
+    batch's L-layer step is one CUDA graph; layer inputs come from a ring of 4
+    sets.  value = whole-job tok/s at batch 256."""
+    import copy
+
+    import torch
+    import torch.distributed as dist
+
+    from edgeexpert_b200._lib import Context
+    from edgeexpert_b200.ep import ExpertParallelMoE
+    from edgeexpert_b200.format import synthetic_moe_layer
+    from edgeexpert_b200.moe import ExpertPool, moe_decode_layer
+    from edgeexpert_b200.prefill import (PrefillGroupedRoutedMoE, PrefillMoE, PrefillRouter, PrefillSharedExpert,
+                                         route_sort)
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    ctx = Context.get(local_rank)
+    sdt = torch.bfloat16 if a.scale_dtype == "bf16" else torch.float16
+    L, per = a.layers, E // world
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(2024)  # the same model on every rank; each keeps its experts
+    layers = []
+    for _ in range(L):
+        Lw = synthetic_moe_layer(D, F, FS, E, TOPK, 4, sdt, dev, gen)
+        if world > 1:
+            full = Lw.experts
+            blob = full.blob.view(E, -1)[rank * per:(rank + 1) * per].reshape(-1).clone()
+            Lw.experts = ExpertPool(blob, full.stride, per, full.offsets, D, F, full.scale_dtype)
+            del full, blob
+        layers.append(Lw)
+    torch.cuda.empty_cache()
+    c_layers = [Lw.as_c() for Lw in layers]
+    router, shared = PrefillRouter(ctx), PrefillSharedExpert(ctx)
+    grouped = PrefillGroupedRoutedMoE(ctx)
+    stream = torch.cuda.Stream(device=dev)
+    R = 4
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    batches = [a.tokens] if a.tokens else list(MOE_BATCHES)
+    results = {}
+    clk_all = None
+    for B in batches:
+        T = tokens_of(B, world, rank)
+        cap = -(-B // world)
+        Tm = max(T, 1)
+        g2 = torch.Generator(device=dev)
+        g2.manual_seed(99 + 7 * rank + B)
+        xs = torch.randn(R, L, Tm, D, device=dev, generator=g2).to(torch.float16)
+        x_in = torch.empty(L, Tm, D, dtype=torch.float16, device=dev)
+        idx = torch.empty(L, Tm, TOPK, dtype=torch.int32, device=dev)
+        wts = torch.empty(L, Tm, TOPK, dtype=torch.float16, device=dev)
+        h2 = torch.empty(L, Tm, D, dtype=torch.float16, device=dev)
+        ys = torch.empty(L, Tm, D, dtype=torch.float16, device=dev)
+        sact = torch.empty(Tm, FS, dtype=torch.float16, device=dev)
+        fused_b1 = world == 1 and B == 1
+        if world > 1:
+            eps = [ExpertParallelMoE(layers[l].experts, E, TOPK, cap, D, F, context=ctx, device=dev) for l in range(L)]
+        elif not fused_b1:
+            act = torch.empty(T * TOPK, F, dtype=torch.float16, device=dev)
+            part = torch.empty(T * TOPK, D, dtype=torch.float16, device=dev)
+            routes = route_sort(idx[0].view(-1)[:1], wts[0].view(-1)[:1], 1, 1, E, 16, context=ctx)  # buffers only
+            from edgeexpert_b200.prefill import DeviceRoutes
+            routes = DeviceRoutes(torch.empty(T * TOPK, 4, dtype=torch.int32, device=dev), *[
+                torch.empty_like(t) for t in (routes.offsets, routes.counts, routes.groups, routes.n_groups,
+                                              routes.tiles, routes.n_tiles)])
+        launches = 0
+
+        def step(xx):
+            nonlocal launches
+            launches = 0
+            for l in range(L):
+                Lw, x = layers[l], xx[l]
+                if fused_b1:
+                    moe_decode_layer(Lw, x[0], x[0], h2[l][0], out_indices=idx[l][0], out_weights=wts[l][0],
+                                     stream=stream, context=ctx, c_layer=c_layers[l])
+                    launches += 3
+                    continue
+                if T:
+                    router.encode_gemma4_block(Lw.router_w, Lw.router_s, Lw.router_b, x, Lw.eff_scale,
+                                               Lw.per_expert_scale, idx[l], wts[l], T, E, D, TOPK, stream=stream)
+                    launches += 1
+                if world > 1:
+                    eps[l].forward(x[:T], idx[l][:T], wts[l][:T], h2[l][:T], stream=stream)
+                    launches += 9
+                else:
+                    route_sort(idx[l], wts[l], T, TOPK, E, 16, stream=stream, context=ctx, out=routes)
+                    grouped.encode(Lw.experts, routes, x, act, part, T, TOPK, stream=stream)
+                    PrefillMoE.encode_reduce_token_major(part, wts[l], h2[l], T, TOPK, D, stream=stream, context=ctx)
+                    launches += 7
+                if T:
+                    shared.encode(x, Lw.shared_gate, Lw.shared_up, Lw.shared_down, sact, ys[l], T, stream=stream)
+                    launches += 3
+
+        # eager warm-up (kernel attributes, NCCL communicators), then one graph per ring slot + x_in
+        with torch.cuda.stream(stream):
+            step(xs[0])
+        torch.cuda.synchronize()
+        barrier()
+        graphs = []
+        use_graph = True
+        try:
+            for r in range(R + 1):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    step(xs[r] if r < R else x_in)
+                graphs.append(g)
+        except Exception as exc:  # noqa: BLE001 -- fall back to eager launches, reported in the line
+            use_graph = False
+            graphs = []
+            torch.cuda.synchronize()
+            print(f"[bench] CUDA graph capture failed ({exc}); timing eager launches", file=sys.stderr)
+        torch.cuda.synchronize()
+        barrier()
+
+        def run(r):
+            if use_graph:
+                graphs[r].replay()
+            else:
+                step(xs[r] if r < R else x_in)
+
+        with torch.cuda.stream(stream):
+            for i in range(a.warmup):
+                run(i % R)
+        torch.cuda.synchronize()
+        clocks = ClockSampler(local_rank)
+        clocks.start()
+        barrier()
+        torch.cuda.synchronize()
+        steps = max(3, a.steps if B > 1 else a.steps)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for i in range(steps):
+                run(i % R)
+            e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+        clk = clocks.stop()
+        if clk_all is None:
+            clk_all = clk
+
+        # end to end: each step's inputs H2D from pinned memory, outputs (h2, ys, routing) D2H
+        h_in = torch.empty(L, Tm, D, dtype=torch.float16, pin_memory=True)
+        h_in.copy_(xs[0].cpu())
+        h_h2 = torch.empty(L, Tm, D, dtype=torch.float16, pin_memory=True)
+        h_ys = torch.empty(L, Tm, D, dtype=torch.float16, pin_memory=True)
+        h_idx = torch.empty(L, Tm, TOPK, dtype=torch.int32, pin_memory=True)
+        with torch.cuda.stream(stream):
+            for _ in range(a.warmup):
+                x_in.copy_(h_in, non_blocking=True)
+                run(R)
+                h_h2.copy_(h2, non_blocking=True)
+        torch.cuda.synchronize()
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            f0.record(stream)
+            for _ in range(steps):
+                x_in.copy_(h_in, non_blocking=True)
+                run(R)
+                h_h2.copy_(h2, non_blocking=True)
+                h_ys.copy_(ys, non_blocking=True)
+                h_idx.copy_(idx, non_blocking=True)
+            f1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms_e2e = max_over_ranks(f0.elapsed_time(f1) / steps)
+        ctx.check_device(stream)
+
+        # distinct local experts the step hit (routing of ring slot 0), for the HBM roofline
+        with torch.cuda.stream(stream):
+            run(0)
+        torch.cuda.synchronize()
+        ids_all = idx[:, :T].reshape(L, -1).cpu() if T else torch.empty(L, 0, dtype=torch.int32)
+        if world > 1:  # what this rank's experts saw: every rank's routing
+            ids_g = [torch.empty(L, cap * TOPK, dtype=torch.int32, device=dev) for _ in range(world)]
+            mine = torch.full((L, cap * TOPK), -1, dtype=torch.int32, device=dev)
+            if T:
+                mine[:, :T * TOPK] = idx[:, :T].reshape(L, -1)
+            dist.all_gather(ids_g, mine)
+            ids_all = torch.cat([t.cpu() for t in ids_g], dim=1)
+        distinct = 0.0
+        for l in range(L):
+            v = ids_all[l]
+            v = v[(v >= rank * per) & (v < (rank + 1) * per)]
+            distinct += float(torch.unique(v).numel())
+        distinct /= L
+        bytes_gpu = moe_step_bytes(B, world, distinct, L)
+        results[B] = {
+            "tokens": B, "tokens_per_gpu": cap, "ms_per_step": ms, "tok_s": B * 1e3 / ms,
+            "tok_s_e2e": B * 1e3 / ms_e2e, "ms_e2e": ms_e2e, "graph": use_graph,
+            "distinct_local_experts_per_layer": distinct,
+            "hbm_bytes_per_gpu": bytes_gpu, "hbm_gbs_per_gpu": bytes_gpu / (ms * 1e-3) / 1e9,
+            "gpu_launches_per_step": launches,
+            "h2d_bytes_per_step": L * T * D * 2, "d2h_bytes_per_step": L * T * (2 * D * 2 + TOPK * 4),
+            "nvlink_bytes_per_gpu_per_step": (2 * L * (world - 1) * cap * (2 * D + 64 + 4 * D)) if world > 1 else 0,
+            "clocks": clk,
+        }
+        del graphs
+        if world > 1:
+            del eps
+        torch.cuda.empty_cache()
+
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak, peak_src = (peaks["hbm_gbs"], "measured hbm_gbs") if "hbm_gbs" in peaks else (6650.0, "fallback")
+    Bh = batches[0]
+    head = results[Bh]
+
+    # single-GPU extras: the batch-1 decode roofline and the config-0 GEMV, in the same run
+    dec = None
+    gemv = None
+    cpu = None
+    if world == 1 and rank == 0:
+        if not a.no_gemv:
+            da = copy.copy(a)
+            da.steps = max(20, a.steps)
+            dec = run_ours(da, rank, world, local_rank, emit=False, layers=layers)
+            ga = copy.copy(a)
+            ga.steps, ga.scale_dtype = max(10 * a.steps, DEFAULT_STEPS["gemv"] // 3), "f16"
+            gemv = run_gemv(ga, rank, world, local_rank, emit=False)
+        if not a.no_cpu_baseline:
+            # the oracle's per-token layer math, scaled to tokens through L layers
+            cpu = cpu_baseline_record(lambda sec, th: cpu_sample(sec, "cpu", th), 1.0 / L * 1e9, a.cpu_seconds,
+                                      unit="tok/s")
+            cpu["sample"] += f"; tok/s = layer-tokens/s / {L} layers"
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": head["tok_s"], "unit": "tok/s", "n_gpus": world, "steps": a.steps,
+        "warmup": a.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f16-act/int4-w/fp32-acc",
+        "data": "synthetic (BASELINE config-1 layer distributions, random-init weights, device RNG)",
+        "config": {"workload": f"config-4 MoE decode step: batch {Bh} through {L} config-1 MoE layers "
+                               f"(router + {TOPK} routed of {E} + shared), experts sharded {per} per GPU",
+                   "d": D, "f": F, "fs": FS, "experts": E, "top_k": TOPK, "layers": L, "global_batch": Bh,
+                   "parallelism": f"ep{world}" if world > 1 else "1gpu", "scale_dtype": a.scale_dtype,
+                   "l2": "weights per step (%.1f GB per GPU) exceed L2 (126 MB); no flush needed" %
+                         (head["hbm_bytes_per_gpu"] / 1e9),
+                   "outputs": "routed h2 and shared y per layer, kept separate"},
+        "batches": {str(b): results[b] for b in batches},
+        "tok_s": head["tok_s"],
+        "e2e": {"value": head["tok_s_e2e"], "unit": "tok/s", "h2d_bytes_per_step": head["h2d_bytes_per_step"],
+                "d2h_bytes_per_step": head["d2h_bytes_per_step"]},
+        "roofline": {"bound": "hbm", "kernel": "whole step per GPU (all kernels)",
+                     "achieved": head["hbm_gbs_per_gpu"], "peak": peak,
+                     "peak_source": peak_src, "unit": "GB/s", "frac": head["hbm_gbs_per_gpu"] / peak,
+                     "traffic": None, "bytes_per_step_per_gpu": head["hbm_bytes_per_gpu"]},
+        "cpu_baseline": cpu,
+        "clocks": head["clocks"],
+        "gpu_launches": head["gpu_launches_per_step"] * a.steps,
+    }
+    if dec is not None:
+        line["decode_b1"] = {k: dec[k] for k in ("metric", "value", "unit", "ms_per_step", "tok_s", "config", "e2e",
+                                                 "roofline", "cpu_baseline", "clocks", "gpu_launches")}
+        line["roofline_dominant_kernel"] = dec["roofline"]
+    if gemv is not None:
+        line["gemv"] = {k: gemv[k] for k in ("metric", "value", "unit", "steps", "ms_per_step", "config",
+                                             "single_gemv_us", "single_gemv_gbs", "e2e", "roofline", "cpu_baseline",
+                                             "clocks", "gpu_launches")}
+    print(json.dumps(line), flush=True)
 
 
 # ------------------------------------------------------ chunk workloads ----
@@ -903,7 +1253,7 @@ def run_chunk(a, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
-DEFAULT_STEPS = {"decode": 400, "gemv": 3000, "batched": 1000, "prefill": 300, "ep": 200}
+DEFAULT_STEPS = {"moe": 50, "decode": 400, "gemv": 3000, "batched": 1000, "prefill": 300, "ep": 200}
 
 
 def main():
@@ -923,7 +1273,9 @@ def main():
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
-    if a.workload == "decode":
+    if a.workload == "moe":
+        run_moe(a, rank, world, local_rank)
+    elif a.workload == "decode":
         run_ours(a, rank, world, local_rank)
     elif a.workload == "gemv":
         run_gemv(a, rank, world, local_rank)

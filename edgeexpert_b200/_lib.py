@@ -111,6 +111,10 @@ _PROTOS = {
                           _P, _P, _I, _P], _I),
     "tf_moe_decode_layer": ([_P, C.POINTER(MoELayer), _P, _P, _P, _P, _P, _P, _P], _I),
     "tf_router_topk_noalloc": ([_P, _P, _P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _I, _P], _I),
+    "tf_router_topk_noalloc_check": ([_P, C.POINTER(_U32)], _I),
+    "tf_router_topk_with_logits": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _I, _P], _I),
+    "tf_router_topk_batched_with_logits": ([_P, _P, _P, _P, _P, _U32, _P, _P, _P, _P, _P, _U32, _U32, _U32, _U32,
+                                            _I, _P], _I),
     "tf_group_token_expert_pairs": ([_P, _U32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, _P, _U32, _P, _P, _P,
                                      _P, _P, _P, _P, C.POINTER(GroupingError)], _I),
     "tf_router_topk_batched": ([_P, _P, _P, _P, _P, _U32, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _I, _P], _I),
@@ -121,9 +125,10 @@ _PROTOS = {
     "tf_moe_grouped_routed": ([_P, _P, _U64, _U32, C.POINTER(ExpertOffsets), _P, _P, _P, _P, _U32, _P, _P, _U32,
                                _U32, _U32, _U32, _I, _P], _I),
     "tf_moe_reduce_token_major": ([_P, _P, _P, _P, _U32, _U32, _U32, _P], _I),
-    "tf_ep_send_counts": ([_P, _P, _U32, _U32, _U32, _P, _P], _I),
-    "tf_ep_pack": ([_P, _P, _U32, _P, _U32, _U32, _U32, _U32, _P, _P, _P], _I),
-    "tf_moe_combine_sorted": ([_P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _P], _I),
+    "tf_ep_dispatch_pack": ([_P, _P, _U32, _P, _P, _U32, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P], _I),
+    "tf_ep_dispatch_unpack": ([_P, _P, _U32, _U32, _U32, _P, _P, _P], _I),
+    "tf_ep_expert_combine": ([_P, _P, _P, _P, _U32, _U32, _U32, _P, _P], _I),
+    "tf_ep_return_reduce": ([_P, _P, _U32, _U32, _U32, _U32, _P, _U32, _P], _I),
 }
 
 # Symbols of include/tfcuda.h added by later milestones register here too.

@@ -14,7 +14,8 @@ namespace {
 template <class Fn>
 tf_status dispatch_scale(tf_scale_type st, Fn&& fn) {
     if (st == TF_SCALE_F16) return fn(__half{});
-    return fn(__nv_bfloat16{});
+    if (st == TF_SCALE_BF16) return fn(__nv_bfloat16{});
+    return TF_ERR_INVALID_ARG;  // not a tf_scale_type value
 }
 
 tf_status check_ctx(tf_context* ctx) {
@@ -89,6 +90,7 @@ tf_status gemv_common(tf_context* ctx, uint32_t bits, const void* W, const void*
     if (s) return s;
     if (!W || !S || !B || !x || !y) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
     if (bits != 4 && bits != 8) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: bits must be 4 or 8", name);
+    if (st != TF_SCALE_BF16 && st != TF_SCALE_F16) return fail(ctx, TF_ERR_INVALID_ARG, "%s: unknown scale type", name);
     if (m == 0 || n == 0 || batch == 0 || ntok == 0) return fail(ctx, TF_ERR_INVALID_ARG, "%s: zero dimension", name);
     if (n % 64) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: N must be a multiple of 64, got %u", name, n);
     if (ntok > 8) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: at most 8 tokens per call, got %u", name, ntok);
@@ -283,9 +285,10 @@ tf_status tf_affine_gemv_batched(tf_context* ctx, uint32_t bits, const void* W, 
 static tf_status router_launch(tf_context* ctx, const void* W, const void* S, const void* B, const void* hidden,
                                const void* es, const void* pes, void* out_idx, void* out_w, uint32_t E, uint32_t d,
                                uint32_t top_k, tf_scale_type st, cudaStream_t cs,
-                               RouterParams* build_only = nullptr) {
+                               RouterParams* build_only = nullptr, float* out_logits = nullptr) {
     const char* name = "tf_router_topk";
     if (!W || !S || !B || !hidden || !es || !pes || !out_idx || !out_w) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
+    if (st != TF_SCALE_BF16 && st != TF_SCALE_F16) return fail(ctx, TF_ERR_INVALID_ARG, "%s: unknown scale type", name);
     if (d == 0 || d % 64) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: d must be a positive multiple of 64", name);
     if (E == 0 || E > (uint32_t)kMaxRouterExperts) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: num_experts must be in 1..256", name);
     if (top_k == 0 || top_k > 32 || top_k > E) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: top_k must be in 1..min(32, num_experts)", name);
@@ -304,6 +307,7 @@ static tf_status router_launch(tf_context* ctx, const void* W, const void* S, co
     p.D = (int)d;
     p.top_k = (int)top_k;
     p.logits = ctx->d_logits;
+    p.out_logits = out_logits;
     p.ticket = ctx->d_ticket;
     p.out_idx = static_cast<uint32_t*>(out_idx);
     p.out_w = static_cast<__half*>(out_w);
@@ -328,6 +332,19 @@ tf_status tf_router_topk(tf_context* ctx, const void* W, const void* S, const vo
     if (s) return s;
     return router_launch(ctx, W, S, B, hidden, es, pes, out_idx, out_w, E, d, top_k, st,
                          static_cast<cudaStream_t>(stream));
+}
+
+tf_status tf_router_topk_with_logits(tf_context* ctx, const void* W, const void* S, const void* B,
+                                     const void* hidden, const void* es, const void* pes, void* out_idx, void* out_w,
+                                     void* out_logits, uint32_t E, uint32_t d, uint32_t top_k, tf_scale_type st,
+                                     void* stream) {
+    tf_status s = check_ctx(ctx);
+    if (s) return s;
+    if (!out_logits) return fail(ctx, TF_ERR_INVALID_ARG, "tf_router_topk_with_logits: null out_logits");
+    if (reinterpret_cast<uintptr_t>(out_logits) & 3u)
+        return fail(ctx, TF_ERR_MISALIGNED, "tf_router_topk_with_logits: out_logits must be 4-byte aligned");
+    return router_launch(ctx, W, S, B, hidden, es, pes, out_idx, out_w, E, d, top_k, st,
+                         static_cast<cudaStream_t>(stream), nullptr, static_cast<float*>(out_logits));
 }
 
 static tf_status phase1_launch(tf_context* ctx, const ExpertSource& src, const void* x, void* acts, uint32_t d,

@@ -34,8 +34,11 @@ std::mutex g_setup_mutex;
 DeviceSetup g_setup[64];
 
 // Once per device, with that device current: resolve the array's device
-// address (its host-side name is not a device pointer), read the launch
-// limits, and zero the ticket and error words.
+// address (its host-side name is a stand-in, not a device pointer) and read
+// the launch limits.  Nothing is written: a __device__ array without an
+// initialiser is zero when the module loads, and every launch leaves the
+// ticket at 0 again.  The cached address assumes the module stays loaded, so
+// cudaDeviceReset between calls is not supported.
 tf_status setup_device(int dev, DeviceSetup** out) {
     if (dev < 0 || dev >= 64) return TF_ERR_NO_DEVICE;
     std::lock_guard<std::mutex> lk(g_setup_mutex);
@@ -49,8 +52,6 @@ tf_status setup_device(int dev, DeviceSetup** out) {
             return TF_ERR_CUDA;
         void* ptr = nullptr;
         if (cudaGetSymbolAddress(&ptr, g_router_scratch) != cudaSuccess || ptr == nullptr) return TF_ERR_CUDA;
-        if (cudaMemset(ptr, 0, kNoAllocBytes) != cudaSuccess) return TF_ERR_CUDA;
-        if (cudaDeviceSynchronize() != cudaSuccess) return TF_ERR_CUDA;
         s.scratch = static_cast<uint8_t*>(ptr);
         s.num_sms = sms;
         s.max_smem_optin = (size_t)optin;
@@ -68,6 +69,7 @@ tf_status tf_router_topk_noalloc(const void* W, const void* S, const void* B, co
                                  const void* pes, void* out_idx, void* out_w, uint32_t E, uint32_t d,
                                  uint32_t top_k, tf_scale_type st, void* stream) {
     if (!W || !S || !B || !hidden || !es || !pes || !out_idx || !out_w) return TF_ERR_INVALID_ARG;
+    if (st != TF_SCALE_BF16 && st != TF_SCALE_F16) return TF_ERR_INVALID_ARG;
     if (E == 0 || E > (uint32_t)kNoAllocMaxExperts) return TF_ERR_UNSUPPORTED_SHAPE;  // beyond the fixed scratch
     if (d == 0 || d % 64) return TF_ERR_UNSUPPORTED_SHAPE;
     if (top_k == 0 || top_k > 32 || top_k > E) return TF_ERR_UNSUPPORTED_SHAPE;
@@ -111,6 +113,26 @@ tf_status tf_router_topk_noalloc(const void* W, const void* S, const void* B, co
                                                            "tf_router_topk_noalloc");
     return launch_engine<RouterPolicy<__nv_bfloat16>, __nv_bfloat16>(
         &ctx, p, RouterPolicy<__nv_bfloat16>::x_bytes((int)d), sj, cs, "tf_router_topk_noalloc");
+}
+
+tf_status tf_router_topk_noalloc_check(void* stream, uint32_t* flags_out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return TF_ERR_NO_DEVICE;
+    DeviceSetup* s = nullptr;
+    tf_status rc = setup_device(dev, &s);
+    if (rc) return rc;
+    cudaStream_t cs = static_cast<cudaStream_t>(stream);
+    uint32_t* err = reinterpret_cast<uint32_t*>(s->scratch + kNoAllocErrOff);
+    uint32_t words[4] = {0, 0, 0, 0};
+    cudaError_t e = cudaMemcpyAsync(words, err, sizeof(words), cudaMemcpyDeviceToHost, cs);
+    if (e == cudaSuccess) e = cudaMemsetAsync(err, 0, sizeof(words), cs);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(cs);
+    if (e != cudaSuccess) return TF_ERR_CUDA;
+    if (flags_out) *flags_out = words[0];
+    if (words[0] & kErrMbarTimeout) return TF_ERR_TIMEOUT;
+    if (words[0] & kErrAlign) return TF_ERR_MISALIGNED;
+    if (words[0] & kErrBadExpert) return TF_ERR_INVALID_ARG;
+    return TF_OK;
 }
 
 }  // extern "C"

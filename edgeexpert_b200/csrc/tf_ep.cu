@@ -2,82 +2,103 @@
 // sharded across GPUs in contiguous id ranges, experts_per_rank each).
 //
 // The reference has no multi-GPU path; this is the B200 replacement for its
-// SSD expert streaming when experts are spread over several GPUs.  A step on
-// each rank is:
-//   route + tf_moe_route_sort over its own tokens  (pairs sorted by expert,
-//       hence by destination rank)
-//   tf_ep_send_counts     pairs per destination rank
-//   tf_ep_pack            the pairs' token rows in sorted order + the local
-//                         expert id at the destination (the send buffer)
-//   all-to-all (NCCL)     rows and ids to the expert owners
-//   tf_moe_route_sort (K = 1) + tf_moe_grouped_routed (top_k = 1) on the
-//                         received rows: one output row per received row
-//   all-to-all (NCCL)     output rows back, in the sender's sorted order
-//   tf_moe_combine_sorted h2[t] = half(sum_r fma(w[t][r], part[pair(t, r)])),
-//                         the token-major reduce of prefill.metal:575-596 in
-//                         the same rank order, reading the partials through
-//                         the sorted-pair permutation
+// SSD expert streaming when experts are spread over several GPUs.  A layer on
+// each rank, with a fixed capacity of rows per (sender, owner) pair so the
+// exchange sizes never leave the device:
+//   tf_ep_dispatch_pack    token t -> slot (owner r, t) when one of its experts
+//                          lives on r: fp16 row + header (local ids, weights)
+//   all-to-all (NCCL)      equal splits: capacity rows to every rank
+//   tf_ep_dispatch_unpack  received headers -> [rows][top_k] routing
+//   tf_moe_route_sort + tf_moe_grouped_routed on the received rows (the
+//                          grouped gate/up/GELU and down of the reference's
+//                          prefill.metal:336-440,598-670)
+//   tf_ep_expert_combine   per received row: fp32 sum over its slots here, in
+//                          slot order, of fma(w, half partial)
+//   all-to-all (NCCL)      the fp32 rows back to their senders
+//   tf_ep_return_reduce    h2[t] = half(sum over owner ranks, in rank order)
 #include "tf_context.cuh"
 
 using namespace tf;
 
 namespace {
 
-__global__ void send_counts_kernel(const uint32_t* __restrict__ counts, int E, int per_rank, int P,
-                                   uint32_t* out) {
-    const int r = threadIdx.x;
-    if (r >= P) return;
-    uint32_t s = 0;
-    for (int e = r * per_rank; e < min(E, (r + 1) * per_rank); ++e) s += counts[e];
-    out[r] = s;
+// ---- fixed-capacity dispatch (device-resident counts, graph-capturable) ----
+// A dispatch row is the token's fp16 hidden row (d halves) followed by a
+// tf_ep_row_header.  Slot (r, t) of the send buffer carries token t to rank r
+// when at least one of its top-k experts lives there; otherwise only the
+// header is written (n_valid = 0) and the payload is left as it was.
+__global__ void ep_dispatch_pack_kernel(const __half* __restrict__ x, long long ldx,
+                                        const uint32_t* __restrict__ ids, const __half* __restrict__ w, int T, int K,
+                                        int E, int per_rank, int cap, int d, uint8_t* __restrict__ send,
+                                        uint32_t* err) {
+    const int slot = blockIdx.x;  // r * cap + t
+    const int r = slot / cap, t = slot - r * cap;
+    const size_t row_bytes = (size_t)d * 2 + sizeof(tf_ep_row_header);
+    uint8_t* row = send + (size_t)slot * row_bytes;
+    __shared__ int s_n;
+    if (threadIdx.x == 0) {
+        tf_ep_row_header h;
+        uint32_t n = 0;
+        for (int k = 0; k < 8; ++k) {
+            h.local_expert[k] = 0xFFFFFFFFu;
+            h.weight_bits[k] = 0;
+        }
+        if (t < T) {
+            for (int k = 0; k < K; ++k) {
+                const uint32_t e = ids[(size_t)t * K + k];
+                if (e >= (uint32_t)E) {
+                    if (err) atomicOr(err, kErrBadExpert);
+                    continue;
+                }
+                if ((int)(e / (uint32_t)per_rank) == r) {
+                    h.local_expert[k] = e - (uint32_t)(r * per_rank);
+                    h.weight_bits[k] = __half_as_ushort(w[(size_t)t * K + k]);
+                    ++n;
+                }
+            }
+        }
+        h.n_valid = n;
+        h.src_token = (uint32_t)t;
+        h.reserved[0] = h.reserved[1] = 0;
+        *reinterpret_cast<tf_ep_row_header*>(row + (size_t)d * 2) = h;
+        s_n = (int)n;
+    }
+    __syncthreads();
+    if (s_n == 0) return;
+    const uint4* src = reinterpret_cast<const uint4*>(x + (long long)t * ldx);
+    uint4* dst = reinterpret_cast<uint4*>(row);
+    for (int c = threadIdx.x; c < d / 8; c += blockDim.x) dst[c] = __ldg(src + c);
 }
 
-// rows[p][:] = hidden[pairs[p].token][:], local[p] = pairs[p].expert % per_rank
-__global__ void ep_pack_kernel(const __half* __restrict__ x, long long ldx,
-                               const tf_token_expert_pair* __restrict__ pairs, int n, int d, int T, int per_rank,
-                               __half* __restrict__ rows, uint32_t* __restrict__ local, uint32_t* err) {
+// ids_out[i][k] / w_out[i][k] from the received headers (UINT32_MAX = empty slot)
+__global__ void ep_dispatch_unpack_kernel(const uint8_t* __restrict__ recv, int rows, int d, int K,
+                                          uint32_t* __restrict__ ids_out, __half* __restrict__ w_out) {
+    const size_t row_bytes = (size_t)d * 2 + sizeof(tf_ep_row_header);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < rows * K; i += gridDim.x * blockDim.x) {
+        const int row = i / K, k = i - row * K;
+        const tf_ep_row_header* h = reinterpret_cast<const tf_ep_row_header*>(recv + (size_t)row * row_bytes + (size_t)d * 2);
+        ids_out[i] = h->local_expert[k];
+        w_out[i] = __ushort_as_half(h->weight_bits[k]);
+    }
+}
+
+// out[row][:] = sum over the row's valid slots, in slot (rank) order, of
+// fma(w, partial[row*K + slot]) in fp32; 0 for a row with none.
+__global__ void ep_expert_combine_kernel(const __half* __restrict__ part, const uint32_t* __restrict__ ids,
+                                         const __half* __restrict__ w, int rows, int K, int d,
+                                         float* __restrict__ out) {
     const int d8 = d >> 3;
-    const long long total = (long long)n * d8;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-         i += (long long)gridDim.x * blockDim.x) {
-        const int p = (int)(i / d8), c = (int)(i - (long long)p * d8);
-        const tf_token_expert_pair pr = pairs[p];
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (pr.token < (uint32_t)T)
-            v = __ldg(reinterpret_cast<const uint4*>(x + (long long)pr.token * ldx) + c);
-        else if (c == 0 && err)
-            atomicOr(err, kErrBadExpert);
-        reinterpret_cast<uint4*>(rows + (long long)p * d)[c] = v;
-        if (c == 0) local[p] = pr.expert % (uint32_t)per_rank;
-    }
-}
-
-// inv[token * K + rank] = sorted position of that pair
-__global__ void invert_pairs_kernel(const tf_token_expert_pair* __restrict__ pairs, int n, int K, int T,
-                                    uint32_t* inv, uint32_t* err) {
-    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < n; p += gridDim.x * blockDim.x) {
-        const tf_token_expert_pair pr = pairs[p];
-        if (pr.token < (uint32_t)T && pr.rank < (uint32_t)K)
-            inv[pr.token * K + pr.rank] = (uint32_t)p;
-        else if (err)
-            atomicOr(err, kErrBadExpert);
-    }
-}
-
-__global__ void combine_sorted_kernel(const __half* __restrict__ part, const uint32_t* __restrict__ inv,
-                                      const __half* __restrict__ w, __half* __restrict__ h2, int T, int K, int D) {
-    const int d8 = D >> 3;
-    const long long n = (long long)T * d8;
+    const long long n = (long long)rows * d8;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x) {
-        const int t = (int)(i / d8), dv = (int)(i - (long long)t * d8);
+        const int row = (int)(i / d8), dv = (int)(i - (long long)row * d8);
         float acc[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-        for (int r = 0; r < K; ++r) {
-            const float wr = __half2float(w[(long long)t * K + r]);
-            const uint32_t p = __ldg(&inv[(long long)t * K + r]);
-            const uint4 q = __ldcs(reinterpret_cast<const uint4*>(part + (long long)p * D) + dv);
+        for (int k = 0; k < K; ++k) {
+            if (__ldg(&ids[(size_t)row * K + k]) == 0xFFFFFFFFu) continue;
+            const float wr = __half2float(w[(size_t)row * K + k]);
+            const uint4 q = __ldcs(reinterpret_cast<const uint4*>(part + ((long long)row * K + k) * d) + dv);
             const __half2* hp = reinterpret_cast<const __half2*>(&q);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -86,11 +107,31 @@ __global__ void combine_sorted_kernel(const __half* __restrict__ part, const uin
                 acc[2 * j + 1] = fmaf(wr, f2.y, acc[2 * j + 1]);
             }
         }
-        uint4 o;
-        __half2* op = reinterpret_cast<__half2*>(&o);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) op[j] = __floats2half2_rn(acc[2 * j], acc[2 * j + 1]);
-        reinterpret_cast<uint4*>(h2 + (long long)t * D)[dv] = o;
+        float4* o = reinterpret_cast<float4*>(out + (long long)row * d) + dv * 2;
+        o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+}
+
+// h2[t][:] = half(sum_r back[r][t][:]) in rank order (+ nothing else)
+__global__ void ep_return_reduce_kernel(const float* __restrict__ back, int world, int cap, int T, int d,
+                                        __half* __restrict__ h2, long long ldh) {
+    const int d4 = d >> 2;
+    const long long n = (long long)T * d4;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int t = (int)(i / d4), dv = (int)(i - (long long)t * d4);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < world; ++r) {
+            const float4 v = __ldcs(reinterpret_cast<const float4*>(back + ((long long)r * cap + t) * d) + dv);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        __half2* o = reinterpret_cast<__half2*>(h2 + (long long)t * ldh) + dv * 2;
+        o[0] = __floats2half2_rn(acc.x, acc.y);
+        o[1] = __floats2half2_rn(acc.z, acc.w);
     }
 }
 
@@ -102,65 +143,80 @@ int grid_for(const tf_context* ctx, long long n) {
 
 extern "C" {
 
-tf_status tf_ep_send_counts(tf_context* ctx, const void* counts, uint32_t num_experts, uint32_t experts_per_rank,
-                            uint32_t world, void* send_counts, void* stream) {
+tf_status tf_ep_dispatch_pack(tf_context* ctx, const void* hidden, uint32_t hidden_stride, const void* expert_ids,
+                              const void* weights, uint32_t T, uint32_t top_k, uint32_t num_experts,
+                              uint32_t experts_per_rank, uint32_t world, uint32_t capacity, uint32_t d, void* send,
+                              void* stream) {
     if (!ctx) return TF_ERR_INVALID_ARG;
-    const char* name = "tf_ep_send_counts";
+    const char* name = "tf_ep_dispatch_pack";
     if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, TF_ERR_CUDA, "cudaSetDevice failed");
-    if (!counts || !send_counts) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
-    if (world == 0 || world > 1024 || experts_per_rank == 0 || experts_per_rank * world != num_experts)
+    if (d == 0 || d % 8 || top_k == 0 || top_k > 8) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: d %% 8 == 0, 1 <= top_k <= 8", name);
+    if (world == 0 || experts_per_rank == 0 || (uint64_t)experts_per_rank * world != num_experts)
         return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: num_experts must equal experts_per_rank * world", name);
-    send_counts_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const uint32_t*>(counts), (int)num_experts, (int)experts_per_rank, (int)world,
-        static_cast<uint32_t*>(send_counts));
-    return cuda_check(ctx, cudaGetLastError(), name);
-}
-
-tf_status tf_ep_pack(tf_context* ctx, const void* hidden, uint32_t hidden_stride, const void* sorted_pairs,
-                     uint32_t n_pairs, uint32_t d, uint32_t T, uint32_t experts_per_rank, void* rows,
-                     void* local_expert, void* stream) {
-    if (!ctx) return TF_ERR_INVALID_ARG;
-    const char* name = "tf_ep_pack";
-    if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, TF_ERR_CUDA, "cudaSetDevice failed");
-    if (d == 0 || d % 8 || experts_per_rank == 0) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: d %% 8 == 0", name);
+    if (T > capacity) return fail(ctx, TF_ERR_INVALID_ARG, "%s: T (%u) exceeds the capacity (%u)", name, T, capacity);
     if (hidden_stride == 0) hidden_stride = d;
     if (hidden_stride < d || hidden_stride % 8) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: hidden stride", name);
-    if (n_pairs == 0) return TF_OK;
-    if (!hidden || !sorted_pairs || !rows || !local_expert) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
-    if (!aligned16(hidden) || !aligned16(rows) || !aligned4(sorted_pairs) || !aligned4(local_expert))
-        return fail(ctx, TF_ERR_MISALIGNED, "%s: hidden/rows 16-byte aligned", name);
-    const long long n = (long long)n_pairs * (d / 8);
-    ep_pack_kernel<<<grid_for(ctx, n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const __half*>(hidden), hidden_stride, static_cast<const tf_token_expert_pair*>(sorted_pairs),
-        (int)n_pairs, (int)d, (int)T, (int)experts_per_rank, static_cast<__half*>(rows),
-        static_cast<uint32_t*>(local_expert), ctx->d_err);
+    if (capacity == 0) return TF_OK;
+    if (!send || (T && (!hidden || !expert_ids || !weights))) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
+    if (!aligned16(send) || (T && (!aligned16(hidden) || !aligned4(expert_ids) || !aligned2(weights))))
+        return fail(ctx, TF_ERR_MISALIGNED, "%s: hidden/send 16-byte aligned", name);
+    ep_dispatch_pack_kernel<<<world * capacity, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __half*>(hidden), hidden_stride, static_cast<const uint32_t*>(expert_ids),
+        static_cast<const __half*>(weights), (int)T, (int)top_k, (int)num_experts, (int)experts_per_rank,
+        (int)capacity, (int)d, static_cast<uint8_t*>(send), ctx->d_err);
     return cuda_check(ctx, cudaGetLastError(), name);
 }
 
-tf_status tf_moe_combine_sorted(tf_context* ctx, const void* sorted_pairs, const void* partials_sorted,
-                                const void* routing_weights, void* inv_scratch, void* h2, uint32_t T,
-                                uint32_t top_k, uint32_t d, void* stream) {
+tf_status tf_ep_dispatch_unpack(tf_context* ctx, const void* recv, uint32_t rows, uint32_t d, uint32_t top_k,
+                                void* expert_ids_out, void* weights_out, void* stream) {
     if (!ctx) return TF_ERR_INVALID_ARG;
-    const char* name = "tf_moe_combine_sorted";
+    const char* name = "tf_ep_dispatch_unpack";
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, TF_ERR_CUDA, "cudaSetDevice failed");
+    if (d == 0 || d % 8 || top_k == 0 || top_k > 8) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: d %% 8 == 0, 1 <= top_k <= 8", name);
+    if (rows == 0) return TF_OK;
+    if (!recv || !expert_ids_out || !weights_out) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
+    if (!aligned16(recv) || !aligned4(expert_ids_out) || !aligned2(weights_out))
+        return fail(ctx, TF_ERR_MISALIGNED, "%s: misaligned buffer", name);
+    ep_dispatch_unpack_kernel<<<grid_for(ctx, (long long)rows * top_k), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint8_t*>(recv), (int)rows, (int)d, (int)top_k, static_cast<uint32_t*>(expert_ids_out),
+        static_cast<__half*>(weights_out));
+    return cuda_check(ctx, cudaGetLastError(), name);
+}
+
+tf_status tf_ep_expert_combine(tf_context* ctx, const void* route_partials, const void* expert_ids,
+                               const void* weights, uint32_t rows, uint32_t top_k, uint32_t d, void* out,
+                               void* stream) {
+    if (!ctx) return TF_ERR_INVALID_ARG;
+    const char* name = "tf_ep_expert_combine";
     if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, TF_ERR_CUDA, "cudaSetDevice failed");
     if (d == 0 || d % 8 || top_k == 0) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: d %% 8 == 0, top_k > 0", name);
+    if (rows == 0) return TF_OK;
+    if (!route_partials || !expert_ids || !weights || !out) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
+    if (!aligned16(route_partials) || !aligned16(out) || !aligned4(expert_ids) || !aligned2(weights))
+        return fail(ctx, TF_ERR_MISALIGNED, "%s: partials/out 16-byte aligned", name);
+    const long long n = (long long)rows * (d / 8);
+    ep_expert_combine_kernel<<<grid_for(ctx, n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __half*>(route_partials), static_cast<const uint32_t*>(expert_ids),
+        static_cast<const __half*>(weights), (int)rows, (int)top_k, (int)d, static_cast<float*>(out));
+    return cuda_check(ctx, cudaGetLastError(), name);
+}
+
+tf_status tf_ep_return_reduce(tf_context* ctx, const void* back, uint32_t world, uint32_t capacity, uint32_t T,
+                              uint32_t d, void* h2, uint32_t h2_stride, void* stream) {
+    if (!ctx) return TF_ERR_INVALID_ARG;
+    const char* name = "tf_ep_return_reduce";
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, TF_ERR_CUDA, "cudaSetDevice failed");
+    if (d == 0 || d % 8 || world == 0) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: d %% 8 == 0", name);
+    if (T > capacity) return fail(ctx, TF_ERR_INVALID_ARG, "%s: T exceeds the capacity", name);
+    if (h2_stride == 0) h2_stride = d;
+    if (h2_stride < d || h2_stride % 8) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: h2 stride", name);
     if (T == 0) return TF_OK;
-    if (!sorted_pairs || !partials_sorted || !routing_weights || !inv_scratch || !h2)
-        return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
-    if (!aligned16(partials_sorted) || !aligned16(h2) || !aligned2(routing_weights) || !aligned4(inv_scratch) ||
-        !aligned4(sorted_pairs))
-        return fail(ctx, TF_ERR_MISALIGNED, "%s: partials/h2 16-byte aligned", name);
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const int n = (int)(T * top_k);
-    invert_pairs_kernel<<<grid_for(ctx, n), 256, 0, s>>>(static_cast<const tf_token_expert_pair*>(sorted_pairs), n,
-                                                         (int)top_k, (int)T, static_cast<uint32_t*>(inv_scratch),
-                                                         ctx->d_err);
-    tf_status rc = cuda_check(ctx, cudaGetLastError(), name);
-    if (rc != TF_OK) return rc;
-    const long long m = (long long)T * (d / 8);
-    combine_sorted_kernel<<<grid_for(ctx, m), 256, 0, s>>>(
-        static_cast<const __half*>(partials_sorted), static_cast<const uint32_t*>(inv_scratch),
-        static_cast<const __half*>(routing_weights), static_cast<__half*>(h2), (int)T, (int)top_k, (int)d);
+    if (!back || !h2) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
+    if (!aligned16(back) || !aligned16(h2)) return fail(ctx, TF_ERR_MISALIGNED, "%s: back/h2 16-byte aligned", name);
+    const long long n = (long long)T * (d / 4);
+    ep_return_reduce_kernel<<<grid_for(ctx, n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const float*>(back), (int)world, (int)capacity, (int)T, (int)d, static_cast<__half*>(h2),
+        (long long)h2_stride);
     return cuda_check(ctx, cudaGetLastError(), name);
 }
 

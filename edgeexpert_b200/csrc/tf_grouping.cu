@@ -35,7 +35,7 @@ __global__ void __launch_bounds__(kSortThreads) route_count_kernel(const uint32_
         const uint32_t e = ids[p];
         if (e < (uint32_t)E)
             atomicAdd(&c[e], 1u);
-        else
+        else if (e != 0xFFFFFFFFu)  // UINT32_MAX marks an empty slot: skipped silently
             atomicOr(err, kErrBadExpert);
     }
     __syncthreads();

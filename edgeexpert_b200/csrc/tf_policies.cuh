@@ -476,6 +476,7 @@ struct RouterParams {
     const __nv_bfloat16* per_expert_scale;
     int E, D, top_k;
     float* logits;        // [E] workspace
+    float* out_logits;    // optional caller copy of the fp32 logits [E] (NULL = none)
     unsigned int* ticket; // workspace counter, left at 0
     uint32_t* out_idx;
     __half* out_w;
@@ -660,6 +661,10 @@ struct RouterPolicy {
             for (int r = 0; r < max(1, p.replicas); ++r) {
                 if (e0 < p.E) p.logits[r * 256 + e0] = f[0] + f[1];
                 if (e1 < p.E) p.logits[r * 256 + e1] = f[2] + f[3];
+            }
+            if (p.out_logits) {
+                if (e0 < p.E) p.out_logits[e0] = f[0] + f[1];
+                if (e1 < p.E) p.out_logits[e1] = f[2] + f[3];
             }
         }
         if (p.fused) return;

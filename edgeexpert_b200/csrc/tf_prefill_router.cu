@@ -27,7 +27,7 @@ template <typename ST>
 __global__ void __launch_bounds__(kRtThreads) prefill_router_kernel(
     const uint8_t* __restrict__ W, const ST* __restrict__ S, const ST* __restrict__ B, const __half* __restrict__ H,
     int hstride, const __nv_bfloat16* __restrict__ es, const __nv_bfloat16* __restrict__ pes, uint32_t* out_idx,
-    __half* out_w, int T, int E, int D, int K) {
+    __half* out_w, float* out_logits, int T, int E, int D, int K) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int ws = x_words_stride(D);
     const int ng = D / kGroup;
@@ -144,6 +144,10 @@ __global__ void __launch_bounds__(kRtThreads) prefill_router_kernel(
         for (int cg = 0; cg < kRtCG; ++cg) {
             if (va) logits[(4 * cg + t) * kRtMaxE + rA] = accA[cg];
             if (vb) logits[(4 * cg + t) * kRtMaxE + rB] = accB[cg];
+            if (out_logits && 4 * cg + t < ntok) {  // optional caller copy, [T][E]
+                if (va) out_logits[(size_t)(t0 + 4 * cg + t) * E + rA] = accA[cg];
+                if (vb) out_logits[(size_t)(t0 + 4 * cg + t) * E + rB] = accB[cg];
+            }
         }
     }
     __syncthreads();
@@ -181,13 +185,14 @@ __global__ void __launch_bounds__(kRtThreads) prefill_router_kernel(
 
 extern "C" {
 
-tf_status tf_router_topk_batched(tf_context* ctx, const void* W, const void* S, const void* B, const void* hidden,
-                                 uint32_t hidden_stride, const void* es, const void* pes, void* out_indices,
-                                 void* out_weights, uint32_t T, uint32_t E, uint32_t d, uint32_t top_k,
-                                 tf_scale_type st, void* stream) {
+static tf_status router_batched(tf_context* ctx, const void* W, const void* S, const void* B, const void* hidden,
+                                uint32_t hidden_stride, const void* es, const void* pes, void* out_indices,
+                                void* out_weights, float* out_logits, uint32_t T, uint32_t E, uint32_t d,
+                                uint32_t top_k, tf_scale_type st, void* stream) {
     if (!ctx) return TF_ERR_INVALID_ARG;
     if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, TF_ERR_CUDA, "cudaSetDevice failed");
     const char* name = "tf_router_topk_batched";
+    if (st != TF_SCALE_BF16 && st != TF_SCALE_F16) return fail(ctx, TF_ERR_INVALID_ARG, "%s: unknown scale type", name);
     if (T == 0) return TF_OK;
     if (!W || !S || !B || !hidden || !es || !pes || !out_indices || !out_weights)
         return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
@@ -220,7 +225,7 @@ tf_status tf_router_topk_batched(tf_context* ctx, const void* W, const void* S, 
             static_cast<const uint8_t*>(W), static_cast<const __half*>(S), static_cast<const __half*>(B),
             static_cast<const __half*>(hidden), (int)hidden_stride, static_cast<const __nv_bfloat16*>(es),
             static_cast<const __nv_bfloat16*>(pes), static_cast<uint32_t*>(out_indices), static_cast<__half*>(out_weights),
-            (int)T, (int)E, (int)d, (int)top_k);
+            out_logits, (int)T, (int)E, (int)d, (int)top_k);
     } else {
         s = run(prefill_router_kernel<__nv_bfloat16>);
         if (s) return s;
@@ -228,9 +233,30 @@ tf_status tf_router_topk_batched(tf_context* ctx, const void* W, const void* S, 
             static_cast<const uint8_t*>(W), static_cast<const __nv_bfloat16*>(S), static_cast<const __nv_bfloat16*>(B),
             static_cast<const __half*>(hidden), (int)hidden_stride, static_cast<const __nv_bfloat16*>(es),
             static_cast<const __nv_bfloat16*>(pes), static_cast<uint32_t*>(out_indices), static_cast<__half*>(out_weights),
-            (int)T, (int)E, (int)d, (int)top_k);
+            out_logits, (int)T, (int)E, (int)d, (int)top_k);
     }
     return cuda_check(ctx, cudaGetLastError(), name);
+}
+
+tf_status tf_router_topk_batched(tf_context* ctx, const void* W, const void* S, const void* B, const void* hidden,
+                                 uint32_t hidden_stride, const void* es, const void* pes, void* out_indices,
+                                 void* out_weights, uint32_t T, uint32_t E, uint32_t d, uint32_t top_k,
+                                 tf_scale_type st, void* stream) {
+    return router_batched(ctx, W, S, B, hidden, hidden_stride, es, pes, out_indices, out_weights, nullptr, T, E, d,
+                          top_k, st, stream);
+}
+
+tf_status tf_router_topk_batched_with_logits(tf_context* ctx, const void* W, const void* S, const void* B,
+                                             const void* hidden, uint32_t hidden_stride, const void* es,
+                                             const void* pes, void* out_indices, void* out_weights,
+                                             void* out_logits, uint32_t T, uint32_t E, uint32_t d, uint32_t top_k,
+                                             tf_scale_type st, void* stream) {
+    if (!ctx) return TF_ERR_INVALID_ARG;
+    if (!out_logits) return fail(ctx, TF_ERR_INVALID_ARG, "tf_router_topk_batched_with_logits: null out_logits");
+    if (reinterpret_cast<uintptr_t>(out_logits) & 3u)
+        return fail(ctx, TF_ERR_MISALIGNED, "tf_router_topk_batched_with_logits: out_logits must be 4-byte aligned");
+    return router_batched(ctx, W, S, B, hidden, hidden_stride, es, pes, out_indices, out_weights,
+                          static_cast<float*>(out_logits), T, E, d, top_k, st, stream);
 }
 
 }  // extern "C"

@@ -3,24 +3,35 @@ process group in contiguous id ranges (rank r owns experts
 [r*E/P, (r+1)*E/P)), tokens owned by the rank that routed them.
 
 The reference has no multi-GPU path (one Apple GPU, experts streamed from
-SSD); this is the B200 layout for 2/4/8 GPUs.  One step on every rank:
+SSD); this is the B200 layout for 2/4/8 GPUs.  The exchange has a fixed
+capacity: every rank sends every rank exactly `capacity` rows per layer, one
+slot per (owner, token), so the all-to-all splits are equal and known on the
+host.  Nothing is read back to the host and every buffer is allocated once,
+so a whole layer (or a stack of them) can be captured in one CUDA graph.
 
-1. sort its token->expert pairs by expert on the device (tf_moe_route_sort):
-   the pairs for each destination rank are then one contiguous range;
-2. exchange the per-destination pair counts (all-to-all of P integers);
-3. pack the pairs' token rows and local expert ids (tf_ep_pack) and send them
-   to the owners (all-to-all-v);
-4. on the owner: group the received rows by local expert (tf_moe_route_sort
-   with K = 1) and run the grouped gate/up/GELU and down GEMMs on them
-   (tf_moe_grouped_routed with top_k = 1: one output row per received row);
-5. send the output rows back (all-to-all-v with the splits swapped): they
-   arrive in the sender's sorted-pair order;
-6. h2[t] = half(sum_r w[t][r] * out[pair(t, r)]) in rank order
-   (tf_moe_combine_sorted), the reference's token-major reduce.
+One layer on every rank:
+
+1. tf_ep_dispatch_pack: slot (r, t) carries token t's fp16 row and a header
+   with its routing slots that live on rank r (local expert id, weight);
+   a token reaches an owner once, however many of its experts live there;
+2. all-to-all (equal splits) to the owners;
+3. tf_ep_dispatch_unpack: received headers -> [rows][top_k] routing, with
+   UINT32_MAX for slots of other ranks;
+4. tf_moe_route_sort + tf_moe_grouped_routed over the received rows: the
+   reference's grouped gate/up/GELU and down (prefill.metal:336-440,598-670),
+   one fp16 partial per (row, slot);
+5. tf_ep_expert_combine: per received row, fp32 sum in slot order of
+   fma(w, partial) over its slots on this rank;
+6. all-to-all of the fp32 rows back to their senders;
+7. tf_ep_return_reduce: h2[t] = half(sum over owner ranks in rank order).
+
+Compared with the single-GPU token-major reduce (prefill.metal:575-596, one
+fp32 fma chain over the k slots in rank order) the fp32 sum is regrouped by
+owner rank, so results agree to fp32 rounding, not bit for bit.
 
 The collectives go through torch.distributed (NCCL between GPUs, gloo in the
-CPU tests); the device work goes through `ops`, by default the CUDA kernels of
-libtfcuda.so.
+CPU tests); the device work goes through `ops`, by default the CUDA kernels
+of libtfcuda.so.
 """
 from __future__ import annotations
 
@@ -32,121 +43,143 @@ import torch.distributed as dist
 
 from ._lib import Context, lib, ptr, stream_ptr
 
-
-def exchange_counts(send_counts, group=None, device=None) -> list[int]:
-    """recv[r] = what rank r sends here, given send[r] = what this rank sends to r."""
-    if not dist.is_initialized():  # one rank: everything stays here
-        return [int(v) for v in send_counts]
-    p = dist.get_world_size(group)
-    dev = device if device is not None else torch.device("cpu")
-    s = torch.as_tensor(list(send_counts), dtype=torch.int64, device=dev)
-    if s.numel() != p:
-        raise ValueError(f"send_counts has {s.numel()} entries for {p} ranks")
-    r = torch.empty_like(s)
-    dist.all_to_all_single(r, s, group=group)
-    return [int(v) for v in r.cpu().tolist()]
+ROW_HEADER_BYTES = 64  # sizeof(tf_ep_row_header)
+EMPTY_SLOT = 0xFFFFFFFF
 
 
-def exchange_rows(send: torch.Tensor, send_counts, recv_counts, group=None) -> torch.Tensor:
-    """All-to-all-v of the leading dimension: send[sum(send_counts[:r]) : ...] goes to rank r."""
-    if not dist.is_initialized():
+def row_bytes(d: int) -> int:
+    """Bytes of one dispatch row: d fp16 values + tf_ep_row_header."""
+    return 2 * d + ROW_HEADER_BYTES
+
+
+def exchange_equal(send: torch.Tensor, recv: torch.Tensor, group=None) -> torch.Tensor:
+    """All-to-all with equal splits along dim 0 (world blocks of the same size).
+    With one rank (or no process group) the send buffer is returned as is."""
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
         return send
-    out = torch.empty((int(sum(recv_counts)),) + tuple(send.shape[1:]), dtype=send.dtype, device=send.device)
-    dist.all_to_all_single(out, send.contiguous(), [int(c) for c in recv_counts], [int(c) for c in send_counts],
-                           group=group)
-    return out
+    dist.all_to_all_single(recv, send, group=group)
+    return recv
 
 
 @dataclass
-class EPStats:
-    sent: list
-    received: list
+class EPBuffers:
+    """Every device buffer of one expert-parallel layer, allocated once."""
+
+    send: torch.Tensor      # uint8 [world*capacity, row_bytes]
+    recv: torch.Tensor      # uint8 [world*capacity, row_bytes]
+    ids: torch.Tensor       # int32 [world*capacity, K]
+    w: torch.Tensor         # fp16  [world*capacity, K]
+    act: torch.Tensor       # fp16  [world*capacity*K, f]
+    part: torch.Tensor      # fp16  [world*capacity*K, d]
+    ret: torch.Tensor       # fp32  [world*capacity, d]
+    back: torch.Tensor      # fp32  [world*capacity, d]
+    routes: object          # DeviceRoutes of the received rows
 
 
 class CudaOps:
-    """The device work of an expert-parallel step on one GPU (libtfcuda.so)."""
+    """The device work of an expert-parallel layer on one GPU (libtfcuda.so)."""
 
     def __init__(self, context: Context):
         self.ctx = context
 
-    def route(self, expert_ids, weights, T, K, E):
-        from .prefill import route_sort
-        return route_sort(expert_ids, weights, T, K, E, 16, context=self.ctx)
+    def alloc(self, world, capacity, K, d, f, num_local, device) -> EPBuffers:
+        from .prefill import DeviceRoutes
+        rows = world * capacity
+        rb = row_bytes(d)
+        n = max(rows * K, 1)
+        routes = DeviceRoutes(torch.empty(n, 4, dtype=torch.int32, device=device),
+                              torch.empty(num_local, dtype=torch.int32, device=device),
+                              torch.empty(num_local, dtype=torch.int32, device=device),
+                              torch.empty(num_local, 3, dtype=torch.int32, device=device),
+                              torch.empty(1, dtype=torch.int32, device=device),
+                              torch.empty(num_local, 4, dtype=torch.int32, device=device),
+                              torch.empty(1, dtype=torch.int32, device=device))
+        return EPBuffers(torch.zeros(rows, rb, dtype=torch.uint8, device=device),
+                         torch.zeros(rows, rb, dtype=torch.uint8, device=device),
+                         torch.empty(rows, K, dtype=torch.int32, device=device),
+                         torch.empty(rows, K, dtype=torch.float16, device=device),
+                         torch.empty(n, f, dtype=torch.float16, device=device),
+                         torch.empty(n, d, dtype=torch.float16, device=device),
+                         torch.empty(rows, d, dtype=torch.float32, device=device),
+                         torch.empty(rows, d, dtype=torch.float32, device=device),
+                         routes)
 
-    def send_counts(self, routes, E, per_rank, world):
-        out = torch.empty(world, dtype=torch.int32, device=routes.counts.device)
-        st = lib().tf_ep_send_counts(self.ctx.handle, ptr(routes.counts), E, per_rank, world, ptr(out),
-                                     stream_ptr(None))
-        self.ctx.check(st, "tf_ep_send_counts")
-        return [int(v) for v in out.cpu().tolist()]
-
-    def pack(self, hidden, routes, n, T, per_rank):
+    def dispatch_pack(self, hidden, expert_ids, weights, T, K, E, per_rank, world, capacity, send, stream=None):
         d = hidden.shape[1]
-        rows = torch.empty(n, d, dtype=torch.float16, device=hidden.device)
-        local = torch.empty(n, dtype=torch.int32, device=hidden.device)
-        st = lib().tf_ep_pack(self.ctx.handle, ptr(hidden), hidden.stride(0), ptr(routes.sorted_pairs), n, d, T,
-                              per_rank, ptr(rows), ptr(local), stream_ptr(None))
-        self.ctx.check(st, "tf_ep_pack")
-        return rows, local
+        st = lib().tf_ep_dispatch_pack(self.ctx.handle, ptr(hidden), hidden.stride(0), ptr(expert_ids), ptr(weights),
+                                       T, K, E, per_rank, world, capacity, d, ptr(send), stream_ptr(stream))
+        self.ctx.check(st, "tf_ep_dispatch_pack")
 
-    def experts(self, pool, rows, local):
-        """out[i] = down_e(gelu(gate_e . rows[i]) * up_e . rows[i]), e = local[i]."""
-        from .prefill import PrefillGroupedRoutedMoE
-        n = rows.shape[0]
-        d = rows.shape[1]
-        out = torch.empty(n, d, dtype=torch.float16, device=rows.device)
-        if n == 0:
-            return out
-        ones = torch.ones(n, dtype=torch.float16, device=rows.device)
-        routes = self.route(local, ones, n, 1, pool.num_experts)
-        act = torch.empty(n, pool.f, dtype=torch.float16, device=rows.device)
-        PrefillGroupedRoutedMoE(self.ctx).encode(pool, routes, rows, act, out, n, 1)
-        return out
+    def unpack(self, recv, rows, d, K, ids, w, stream=None):
+        st = lib().tf_ep_dispatch_unpack(self.ctx.handle, ptr(recv), rows, d, K, ptr(ids), ptr(w), stream_ptr(stream))
+        self.ctx.check(st, "tf_ep_dispatch_unpack")
 
-    def combine(self, routes, back, weights, h2, T, K):
+    def experts(self, pool, buf: EPBuffers, recv, rows, K, stream=None):
+        """buf.ret[i] = sum over row i's slots here of w * down(gelu(gate.x)*up.x)."""
+        from .prefill import PrefillGroupedRoutedMoE, route_sort
+        d = pool.d
+        route_sort(buf.ids, buf.w, rows, K, pool.num_experts, 16, stream=stream, context=self.ctx, out=buf.routes)
+        PrefillGroupedRoutedMoE(self.ctx).encode(pool, buf.routes, recv, buf.act, buf.part, rows, K,
+                                                 hidden_stride=row_bytes(d) // 2, stream=stream)
+        st = lib().tf_ep_expert_combine(self.ctx.handle, ptr(buf.part), ptr(buf.ids), ptr(buf.w), rows, K, d,
+                                        ptr(buf.ret), stream_ptr(stream))
+        self.ctx.check(st, "tf_ep_expert_combine")
+
+    def reduce(self, back, world, capacity, T, h2, stream=None):
         d = h2.shape[1]
-        inv = torch.empty(max(T * K, 1), dtype=torch.int32, device=h2.device)
-        src = back if back.numel() else torch.empty(1, d, dtype=torch.float16, device=h2.device)
-        st = lib().tf_moe_combine_sorted(self.ctx.handle, ptr(routes.sorted_pairs), ptr(src), ptr(weights),
-                                         ptr(inv), ptr(h2), T, K, d, stream_ptr(None))
-        self.ctx.check(st, "tf_moe_combine_sorted")
+        st = lib().tf_ep_return_reduce(self.ctx.handle, ptr(back), world, capacity, T, d, ptr(h2), h2.stride(0),
+                                       stream_ptr(stream))
+        self.ctx.check(st, "tf_ep_return_reduce")
+
+
+@dataclass
+class EPStats:
+    rows_per_rank: int  # slots sent to (and received from) every rank
 
 
 class ExpertParallelMoE:
     """Routed experts of one MoE layer sharded over `group`.
 
     `experts_local` holds this rank's E/P experts (local ids 0..E/P-1 are
-    global ids rank*E/P ...).  `forward` takes this rank's tokens with their
-    routing (device [T][K] ids and fp16 weights, as tf_router_topk_batched
-    writes them) and returns the routed output h2 [T][d] for those tokens.
+    global ids rank*E/P ...).  `forward` takes this rank's T <= capacity
+    tokens with their routing (device [T][K] ids and fp16 weights, as
+    tf_router_topk_batched writes them) and writes the routed output h2 [T][d]
+    for those tokens.  Every rank must use the same capacity.
     """
 
-    def __init__(self, experts_local, num_experts: int, top_k: int, group=None, ops=None,
-                 context: Context | None = None):
+    def __init__(self, experts_local, num_experts: int, top_k: int, capacity: int, d: int, f: int, group=None,
+                 ops=None, context: Context | None = None, device=None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         if num_experts % self.world:
             raise ValueError(f"{num_experts} experts do not split over {self.world} ranks")
+        if top_k > 8:
+            raise ValueError("the dispatch header holds at most 8 routing slots")
         self.E = num_experts
         self.per_rank = num_experts // self.world
         self.K = top_k
+        self.capacity = capacity
+        self.d, self.f = d, f
         self.pool = experts_local
         if ops is None:
             ops = CudaOps(context or Context.get(torch.cuda.current_device()))
         self.ops = ops
-        self.last = None
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else "cpu"
+        self.buf = ops.alloc(self.world, capacity, top_k, d, f, self.per_rank, device)
+        self.last = EPStats(capacity)
 
-    def forward(self, hidden, expert_ids, weights, h2):
+    def forward(self, hidden, expert_ids, weights, h2, stream=None):
         T = hidden.shape[0]
-        routes = self.ops.route(expert_ids, weights, T, self.K, self.E)
-        send = self.ops.send_counts(routes, self.E, self.per_rank, self.world)
-        recv = exchange_counts(send, self.group, device=hidden.device)
-        rows, local = self.ops.pack(hidden, routes, T * self.K, T, self.per_rank)
-        r_rows = exchange_rows(rows, send, recv, self.group)
-        r_local = exchange_rows(local, send, recv, self.group)
-        out = self.ops.experts(self.pool, r_rows, r_local)
-        back = exchange_rows(out, recv, send, self.group)
-        self.ops.combine(routes, back, weights, h2, T, self.K)
-        self.last = EPStats(send, recv)
+        if T > self.capacity:
+            raise ValueError(f"{T} tokens exceed the dispatch capacity {self.capacity}")
+        b, rows = self.buf, self.world * self.capacity
+        self.ops.dispatch_pack(hidden, expert_ids, weights, T, self.K, self.E, self.per_rank, self.world,
+                               self.capacity, b.send, stream)
+        recv = exchange_equal(b.send, b.recv, self.group)
+        self.ops.unpack(recv, rows, self.d, self.K, b.ids, b.w, stream)
+        self.ops.experts(self.pool, b, recv, rows, self.K, stream)
+        back = exchange_equal(b.ret, b.back, self.group)
+        self.ops.reduce(back, self.world, self.capacity, T, h2, stream)
         return h2

@@ -59,10 +59,20 @@ class MoE:
         self.ctx = context or Context.get(torch.cuda.current_device())
 
     def encode_router_gemma4(self, weights, scales, biases, hidden, effective_scale, per_expert_scale,
-                             out_indices, out_weights, num_experts: int, d: int, top_k: int, stream=None):
-        st = lib().tf_router_topk(self.ctx.handle, ptr(weights), ptr(scales), ptr(biases), ptr(hidden),
-                                  ptr(effective_scale), ptr(per_expert_scale), ptr(out_indices), ptr(out_weights),
-                                  num_experts, d, top_k, scale_type_of(scales), stream_ptr(stream))
+                             out_indices, out_weights, num_experts: int, d: int, top_k: int, stream=None,
+                             out_logits=None):
+        """Router + top-k (MoE.encodeRouterGemma4).  `out_logits` (optional,
+        float32[num_experts] on the device) receives the fp32 router logits."""
+        if out_logits is not None:
+            st = lib().tf_router_topk_with_logits(
+                self.ctx.handle, ptr(weights), ptr(scales), ptr(biases), ptr(hidden), ptr(effective_scale),
+                ptr(per_expert_scale), ptr(out_indices), ptr(out_weights), ptr(out_logits), num_experts, d, top_k,
+                scale_type_of(scales), stream_ptr(stream))
+        else:
+            st = lib().tf_router_topk(self.ctx.handle, ptr(weights), ptr(scales), ptr(biases), ptr(hidden),
+                                      ptr(effective_scale), ptr(per_expert_scale), ptr(out_indices),
+                                      ptr(out_weights), num_experts, d, top_k, scale_type_of(scales),
+                                      stream_ptr(stream))
         self.ctx.check(st, "MoE.encodeRouterGemma4")
 
     encodeRouterGemma4 = encode_router_gemma4

@@ -111,14 +111,19 @@ class PrefillRouter:
 
     def encode_gemma4_block(self, weights, scales, biases, hidden, effective_scale, per_expert_scale, out_indices,
                             out_weights, query_count: int, num_experts: int, d: int, top_k: int,
-                            hidden_stride_elements: int | None = None, stream=None):
-        """Router + top-k for `query_count` tokens (PrefillRouter.encodeGemma4Block)."""
+                            hidden_stride_elements: int | None = None, stream=None, out_logits=None):
+        """Router + top-k for `query_count` tokens (PrefillRouter.encodeGemma4Block).
+        `out_logits` (optional, float32[query_count][num_experts] on the device)
+        receives every token's fp32 logits."""
         from .quant import scale_type_of
-        st = lib().tf_router_topk_batched(
-            self.ctx.handle, ptr(weights), ptr(scales), ptr(biases), ptr(hidden),
-            hidden_stride_elements if hidden_stride_elements is not None else d, ptr(effective_scale),
-            ptr(per_expert_scale), ptr(out_indices), ptr(out_weights), query_count, num_experts, d, top_k,
-            scale_type_of(scales), stream_ptr(stream))
+        hs = hidden_stride_elements if hidden_stride_elements is not None else d
+        head = (self.ctx.handle, ptr(weights), ptr(scales), ptr(biases), ptr(hidden), hs, ptr(effective_scale),
+                ptr(per_expert_scale), ptr(out_indices), ptr(out_weights))
+        tail = (query_count, num_experts, d, top_k, scale_type_of(scales), stream_ptr(stream))
+        if out_logits is not None:
+            st = lib().tf_router_topk_batched_with_logits(*head, ptr(out_logits), *tail)
+        else:
+            st = lib().tf_router_topk_batched(*head, *tail)
         self.ctx.check(st, "PrefillRouter.encodeGemma4Block")
 
     encodeGemma4Block = encode_gemma4_block

@@ -112,6 +112,17 @@ TF_API tf_status tf_router_topk(tf_context* ctx, const void* W, const void* scal
                          void* out_indices, void* out_weights, uint32_t num_experts, uint32_t d,
                          uint32_t top_k, tf_scale_type st, void* stream);
 
+/* tf_router_topk plus a copy of the fp32 router logits, out_logits float[num_experts]
+ * (device, 4-byte aligned), for parity checks of the accumulator and for
+ * callers that log or post-process the logits.  The reference keeps them in
+ * its internal 256-float buffer (Sources/TurboFieldfare/Kernels/MoE/MoE.swift:130-137,
+ * written by router_gemv_gemma4_r4, Metal/MoE/moe.metal:78-133). */
+TF_API tf_status tf_router_topk_with_logits(tf_context* ctx, const void* W, const void* scales, const void* biases,
+                                            const void* hidden, const void* eff_scale, const void* per_expert_scale,
+                                            void* out_indices, void* out_weights, void* out_logits,
+                                            uint32_t num_experts, uint32_t d, uint32_t top_k, tf_scale_type st,
+                                            void* stream);
+
 /* Same computation as tf_router_topk, for callers that cannot allocate
  * device memory (a host application whose allocator owns every device byte,
  * or code that must not allocate after start-up).  No counterpart in the
@@ -120,13 +131,23 @@ TF_API tf_status tf_router_topk(tf_context* ctx, const void* W, const void* scal
  * library that every GPU loading the library keeps until process exit.
  * Limit: num_experts <= 256 (TF_ERR_UNSUPPORTED_SHAPE beyond), other limits
  * as tf_router_topk.  The first call on a device, with that device current,
- * looks up the array's device address and zeroes it (synchronously); make
- * that first call before any stream capture.  All calls on a device share the
- * array, so calls that overlap on the GPU race: serialise them on one stream. */
+ * looks up the array's device address (it writes nothing); make that first
+ * call before any stream capture, and do not call cudaDeviceReset between
+ * calls.  All calls on a device share the array, so calls that overlap on the
+ * GPU race: serialise them on one stream.  Device-side errors (a bounded wait
+ * that gave up, a skipped misaligned access) are not visible in the return
+ * code of the launch; read them with tf_router_topk_noalloc_check. */
 TF_API tf_status tf_router_topk_noalloc(const void* W, const void* scales, const void* biases,
                                         const void* hidden, const void* eff_scale, const void* per_expert_scale,
                                         void* out_indices, void* out_weights, uint32_t num_experts, uint32_t d,
                                         uint32_t top_k, tf_scale_type st, void* stream);
+
+/* Companion of tf_router_topk_noalloc (no counterpart in the reference): on
+ * the current device, copies the fixed array's device error flags to the host
+ * and clears them, ordered on `stream`, then synchronises `stream`.  Returns
+ * TF_ERR_TIMEOUT (a bounded wait gave up), TF_ERR_MISALIGNED (an access was
+ * skipped) or TF_OK; *flags_out (optional) receives the raw flag bits. */
+TF_API tf_status tf_router_topk_noalloc_check(void* stream, uint32_t* flags_out);
 
 /* ---- decode MoE ---------------------------------------------------------- */
 /* MoEExpertOffsets (Sources/TurboFieldfare/Kernels/MoE/MoE.swift:4-29): byte offsets of
@@ -210,6 +231,16 @@ TF_API tf_status tf_router_topk_batched(tf_context* ctx, const void* W, const vo
                                         uint32_t T, uint32_t num_experts, uint32_t d, uint32_t top_k,
                                         tf_scale_type st, void* stream);
 
+/* tf_router_topk_batched plus a copy of every token's fp32 logits,
+ * out_logits float[T][num_experts] (device, 4-byte aligned).  The reference
+ * keeps them in the kernel's threadgroup memory (prefill.metal:478-573). */
+TF_API tf_status tf_router_topk_batched_with_logits(tf_context* ctx, const void* W, const void* scales,
+                                                    const void* biases, const void* hidden, uint32_t hidden_stride,
+                                                    const void* eff_scale, const void* per_expert_scale,
+                                                    void* out_indices, void* out_weights, void* out_logits, uint32_t T,
+                                                    uint32_t num_experts, uint32_t d, uint32_t top_k,
+                                                    tf_scale_type st, void* stream);
+
 /* ---- token -> expert grouping ------------------------------------------------ */
 /* PrefillTokenExpertPair (Sources/TurboFieldfare/Kernels/Prefill/MoE/PrefillRouter.swift:4-28):
  * weight_bits holds the fp16 routing weight in its low 16 bits. */
@@ -254,7 +285,8 @@ TF_API tf_status tf_group_token_expert_pairs(const tf_token_expert_pair* pairs, 
  * without the host round trip (RealForwardRunner.swift:1750-1822).  All
  * arrays are device memory; n_groups / n_tiles are device uint32 scalars.
  * sort_keys: device uint64[num_experts] or NULL.  num_experts <= 256.
- * Out-of-range expert ids are skipped and raise the context's device error bit. */
+ * Out-of-range expert ids are skipped and raise the context's device error bit,
+ * except UINT32_MAX, which marks an empty slot and is skipped silently. */
 TF_API tf_status tf_moe_route_sort(tf_context* ctx, const void* expert_ids, const void* weights, uint32_t T,
                                    uint32_t top_k, uint32_t num_experts, uint32_t tile_expert_count,
                                    const void* sort_keys, void* sorted_pairs, void* offsets, void* counts,
@@ -304,30 +336,54 @@ TF_API tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64
 TF_API tf_status tf_moe_reduce_token_major(tf_context* ctx, const void* route_partials, const void* routing_weights,
                                            void* h2, uint32_t T, uint32_t top_k, uint32_t d, void* stream);
 
-/* ---- expert parallelism (routed experts sharded over GPUs) ------------------------------ */
-/* No reference counterpart: the reference runs on one Apple GPU and streams
- * experts from SSD.  Experts are sharded in contiguous id ranges of
- * experts_per_rank; the exchange itself is the caller's all-to-all (NCCL). */
+/* ---- expert parallelism (routed experts sharded over GPUs) ------------------------------
+ * No reference counterpart (the reference streams experts from SSD on one GPU).
+ * Experts are sharded in contiguous id ranges of experts_per_rank; the
+ * exchange itself is the caller's all-to-all (NCCL).
+ * Every rank sends every other rank exactly `capacity` rows per layer, so the
+ * all-to-all has equal splits known on the host in advance: no count readback,
+ * no host synchronisation, and the whole step can be captured in a CUDA graph.
+ * A row carries a token to an owner rank at most once, whatever the number of
+ * its experts there.  Row layout: the token's d fp16 values, then this header
+ * (row bytes = 2*d + 64): */
+typedef struct {
+    uint32_t local_expert[8]; /* per top-k slot: expert id on the owner, UINT32_MAX = not there */
+    uint16_t weight_bits[8];  /* per slot: fp16 routing weight */
+    uint32_t n_valid;         /* slots that live on the owner (0: payload not written) */
+    uint32_t src_token;       /* token index on the sender */
+    uint32_t reserved[2];
+} tf_ep_row_header;
 
-/* send_counts[r] = sum of counts[e] over the experts rank r owns
- * (counts: the per-expert output of tf_moe_route_sort).  Device uint32 arrays. */
-TF_API tf_status tf_ep_send_counts(tf_context* ctx, const void* counts, uint32_t num_experts,
-                                   uint32_t experts_per_rank, uint32_t world, void* send_counts, void* stream);
+/* send[(r*capacity + t)] = token t of this rank for owner rank r (r < world,
+ * t < capacity; t >= T gives an empty header).  expert_ids uint32[T][top_k]
+ * and weights fp16[T][top_k] as tf_router_topk_batched writes them.
+ * top_k <= 8, T <= capacity, send 16-byte aligned. */
+TF_API tf_status tf_ep_dispatch_pack(tf_context* ctx, const void* hidden, uint32_t hidden_stride,
+                                     const void* expert_ids, const void* weights, uint32_t T, uint32_t top_k,
+                                     uint32_t num_experts, uint32_t experts_per_rank, uint32_t world,
+                                     uint32_t capacity, uint32_t d, void* send, void* stream);
 
-/* The all-to-all send buffer: rows[p] = hidden[pairs[p].token] (fp16 [n][d]) and
- * local_expert[p] = pairs[p].expert % experts_per_rank, in sorted-pair order,
- * so each destination's rows are one contiguous range. */
-TF_API tf_status tf_ep_pack(tf_context* ctx, const void* hidden, uint32_t hidden_stride, const void* sorted_pairs,
-                            uint32_t n_pairs, uint32_t d, uint32_t T, uint32_t experts_per_rank, void* rows,
-                            void* local_expert, void* stream);
+/* Owner side: the received rows' headers as token-major routing for
+ * tf_moe_route_sort (which skips UINT32_MAX silently): expert_ids_out
+ * uint32[rows][top_k], weights_out fp16[rows][top_k].  The received rows
+ * themselves are the grouped GEMM's hidden input, stride (2*d + 64)/2 elements. */
+TF_API tf_status tf_ep_dispatch_unpack(tf_context* ctx, const void* recv, uint32_t rows, uint32_t d, uint32_t top_k,
+                                       void* expert_ids_out, void* weights_out, void* stream);
 
-/* PrefillMoE.encodeReduceTokenMajor (PrefillMoE.swift:11-40; prefill.metal:575-596) over
- * partials held in sorted-pair order (what the combine all-to-all returns):
- * h2[t][i] = half(sum_r fma(w[t][r], partials_sorted[pos(t, r)][i])), rank order, where
- * pos(t, r) is the pair's index in sorted_pairs.  inv_scratch: uint32[T*top_k]. */
-TF_API tf_status tf_moe_combine_sorted(tf_context* ctx, const void* sorted_pairs, const void* partials_sorted,
-                                       const void* routing_weights, void* inv_scratch, void* h2, uint32_t T,
-                                       uint32_t top_k, uint32_t d, void* stream);
+/* Owner side, after tf_moe_grouped_routed over the received rows:
+ * out[i][:] (fp32) = sum over row i's slots on this rank, in slot order, of
+ * fma(w, route_partials[i*top_k + slot][:]) -- the reference's token-major
+ * reduce (prefill.metal:575-596) restricted to this rank's experts; 0 when the
+ * row has none.  out 16-byte aligned. */
+TF_API tf_status tf_ep_expert_combine(tf_context* ctx, const void* route_partials, const void* expert_ids,
+                                      const void* weights, uint32_t rows, uint32_t top_k, uint32_t d, void* out,
+                                      void* stream);
+
+/* Sender side, after the return all-to-all (back fp32 [world][capacity][d]):
+ * h2[t][:] = half(sum_r back[r][t][:]) in rank order, t < T.
+ * h2_stride in elements (0 = d). */
+TF_API tf_status tf_ep_return_reduce(tf_context* ctx, const void* back, uint32_t world, uint32_t capacity,
+                                     uint32_t T, uint32_t d, void* h2, uint32_t h2_stride, void* stream);
 
 #ifdef __cplusplus
 }

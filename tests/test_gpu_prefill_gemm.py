@@ -237,3 +237,68 @@ def test_prefill_argument_validation(cuda):
     with pytest.raises(TFError) as ei:
         PrefillMoE.encode_reduce_token_major(Y, Y, Y, 4, 8, 100)  # d % 8 != 0
     assert ei.value.status == 3
+
+
+def test_prefill_config3_t4096_values(cuda):
+    """BASELINE config 3 at full size: 4096 tokens, 128 experts (D=2816, F=704),
+    top-8, through the tcgen05 grouped GEMMs and the token-major reduce, plus
+    the shared expert (Fs=2112) on the tcgen05 dense GEMMs.  Values are checked
+    against the oracle (fp32 fma(fma(q,s,b),x,acc) per element, the reference's
+    prefill.metal:336-440,598-709 arithmetic) on 256 token rows spread over the
+    batch, and every expert is hit.  This settles the one rounding difference
+    (w rounded to fp16 once before the tensor-core product) at the
+    configuration BASELINE names."""
+    from edgeexpert_b200.moe import SharedExpertProjection
+    T, K, E, D, F, Fs = 4096, 8, 128, 2816, 704, 2112
+    ex = Experts(E, D, F, 0, "cfg3-4096")
+    rng = np.random.default_rng(4096)
+    p = rng.random(E) ** 2 + 0.05
+    p /= p.sum()
+    idx = np.stack([rng.choice(E, K, replace=False, p=p) for _ in range(T)]).astype(np.uint32)
+    w = (rng.random((T, K)) * 0.3 + 0.05).astype(np.float16)
+    X = rng.standard_normal((T, D)).astype(np.float16).view(np.uint16)
+    routes = route_sort(dev(idx.view(np.int32)), dev(w), T, K, E, 16)
+    act = torch.empty(T * K, F, dtype=torch.float16, device="cuda")
+    part = torch.empty(T * K, D, dtype=torch.float16, device="cuda")
+    PrefillGroupedRoutedMoE().encode(ex.pool(), routes, dev(X, torch.float16), act, part, T, K)
+    h2 = torch.empty(T, D, dtype=torch.float16, device="cuda")
+    PrefillMoE.encode_reduce_token_major(part, dev(w), h2, T, K, D)
+
+    srng = O.seed_tree(5, "cfg3-shared")
+    g = srng.synthetic_affine(Fs, D, 4, 0)
+    u = srng.synthetic_affine(Fs, D, 4, 0)
+    dn = srng.synthetic_affine(D, Fs, 4, 0)
+
+    def proj(m, rows, cols):
+        return SharedExpertProjection(dev(m[0]), dev(m[1], torch.bfloat16), dev(m[2], torch.bfloat16), rows, cols, 4)
+    sact = torch.empty(T, Fs, dtype=torch.float16, device="cuda")
+    sy = torch.empty(T, D, dtype=torch.float16, device="cuda")
+    PrefillSharedExpert().encode(dev(X, torch.float16), proj(g, Fs, D), proj(u, Fs, D), proj(dn, D, Fs), sact, sy, T)
+    torch.cuda.synchronize()
+    assert int(np.count_nonzero(np.bincount(idx.reshape(-1), minlength=E))) == E
+
+    sample = np.unique(np.linspace(0, T - 1, 256).astype(np.int64))
+    pairs = PrefillRouter.make_token_expert_pairs(idx, w, T, K)
+    ref = O.group_pairs(pairs, T, K, E, 16)
+    srt = ref["sorted"]
+    sub = srt[np.isin(srt["token"], sample)]
+    part_ref = O.grouped_routed(ex.host.reshape(-1), ex.lay.stride, ex.off, sub, X, D, D, F, K, T, 0)
+    part_ref = part_ref.reshape(T, K, D)[sample]
+    got_part = f16(part).reshape(T, K, D)[sample]
+    assert O.rel_error(O.f16_to_f32(got_part), O.f16_to_f32(part_ref)) < FP16_TOL
+    h2_ref = O.reduce_token_major(part_ref.reshape(-1), w[sample].view(np.uint16), len(sample), K, D)
+    got_h2 = f16(h2).reshape(T, D)[sample]
+    assert O.rel_error(O.f16_to_f32(got_h2), O.f16_to_f32(h2_ref)) < FP16_TOL
+
+    y_ref = np.empty((len(sample), D), np.float32)
+    for i, t in enumerate(sample):
+        _, _, y_ref[i] = O.shared_expert(g, u, dn, X[t], D, Fs, 4)
+    assert O.rel_error(O.f16_to_f32(f16(sy).reshape(T, D)[sample]), y_ref) < FP16_TOL
+
+    # the dense QMM alone (gate projection) on the same rows
+    _, q32 = O.int4_qmm(g[0], g[1], g[2], X[sample], len(sample), Fs, D, 0)
+    yq = torch.empty(T, Fs, dtype=torch.float16, device="cuda")
+    PrefillInt4QMM().encode(dev(g[0]), dev(g[1], torch.bfloat16), dev(g[2], torch.bfloat16), dev(X, torch.float16), yq,
+                            T, Fs, D)
+    torch.cuda.synchronize()
+    assert O.rel_error(O.f16_to_f32(f16(yq).reshape(T, Fs)[sample]), q32.reshape(len(sample), Fs)) < FP16_TOL
