@@ -822,11 +822,11 @@ def run_moe(a, rank, world, local_rank):
         elif not fused_b1:
             act = torch.empty(T * TOPK, F, dtype=torch.float16, device=dev)
             part = torch.empty(T * TOPK, D, dtype=torch.float16, device=dev)
-            routes = route_sort(idx[0].view(-1)[:1], wts[0].view(-1)[:1], 1, 1, E, 16, context=ctx)  # buffers only
             from edgeexpert_b200.prefill import DeviceRoutes
-            routes = DeviceRoutes(torch.empty(T * TOPK, 4, dtype=torch.int32, device=dev), *[
-                torch.empty_like(t) for t in (routes.offsets, routes.counts, routes.groups, routes.n_groups,
-                                              routes.tiles, routes.n_tiles)])
+            i32 = dict(dtype=torch.int32, device=dev)
+            routes = DeviceRoutes(torch.empty(T * TOPK, 4, **i32), torch.empty(E, **i32), torch.empty(E, **i32),
+                                  torch.empty(E, 3, **i32), torch.empty(1, **i32), torch.empty(E, 4, **i32),
+                                  torch.empty(1, **i32))
         launches = 0
 
         def step(xx):

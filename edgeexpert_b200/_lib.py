@@ -125,6 +125,16 @@ _PROTOS = {
     "tf_moe_grouped_routed": ([_P, _P, _U64, _U32, C.POINTER(ExpertOffsets), _P, _P, _P, _P, _U32, _P, _P, _U32,
                                _U32, _U32, _U32, _I, _P], _I),
     "tf_moe_reduce_token_major": ([_P, _P, _P, _P, _U32, _U32, _U32, _P], _I),
+    "tf_rmsnorm": ([_P, _P, _U32, _P, _P, _U32, _U32, _U32, C.c_float, _P], _I),
+    "tf_qkv_epilogue": ([_P, _P, _U32, _P, _P, _U64, _P, _P, _U32, _U32, _U32, _U32, _U32, C.c_float, _U32,
+                         C.c_float, _P], _I),
+    "tf_attention_workspace_bytes": ([_P, _U32, _U32, _U32, _U32, _U32], C.c_size_t),
+    "tf_attention_decode": ([_P, _P, _U32, _P, _P, _U64, _P, _U32, _U32, _U32, _U32, _U32, _U32, _U32,
+                             C.c_float, _P, C.c_size_t, _P], _I),
+    "tf_post_attn_setup": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _U32, _U32, C.c_float, _P], _I),
+    "tf_layer_tail": ([_P, _P, _P, _P, _P, _P, _P, C.c_float, _U32, _U32, C.c_float, _P], _I),
+    "tf_embed_int4": ([_P, _P, _P, _P, _P, _U32, _U32, _U32, C.c_float, _P, _U32, _I, _P], _I),
+    "tf_lm_head_greedy": ([_P, _P, _U32, _P, C.c_float, _P, _P, _P, _U32, _U32, _U32, _P, _P, _P, _I, _P], _I),
     "tf_ep_dispatch_pack": ([_P, _P, _U32, _P, _P, _U32, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P], _I),
     "tf_ep_dispatch_unpack": ([_P, _P, _U32, _U32, _U32, _P, _P, _P], _I),
     "tf_ep_expert_combine": ([_P, _P, _P, _P, _U32, _U32, _U32, _P, _P], _I),

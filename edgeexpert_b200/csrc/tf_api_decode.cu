@@ -212,6 +212,10 @@ tf_status tf_context_create(int device, tf_context** out) {
     e = e ? e : cudaMalloc(&ctx->d_acts, sizeof(__half) * kMaxTopKDecode * kMaxF);
     e = e ? e : cudaMalloc(&ctx->d_shared_act, sizeof(__half) * kMaxFs);
     e = e ? e : cudaMalloc(&ctx->d_sort_cnt, sizeof(uint32_t) * kRouteSortChunks * 256);
+    e = e ? e : cudaMalloc(&ctx->d_lm_keys, sizeof(unsigned long long) * kMaxLmTokens);
+    e = e ? e : cudaMalloc(&ctx->d_lm_tickets, sizeof(unsigned int) * kMaxLmTokens);
+    e = e ? e : cudaMemset(ctx->d_lm_keys, 0, sizeof(unsigned long long) * kMaxLmTokens);
+    e = e ? e : cudaMemset(ctx->d_lm_tickets, 0, sizeof(unsigned int) * kMaxLmTokens);
     e = e ? e : cudaMemset(ctx->d_err, 0, 4 * sizeof(uint32_t));
     e = e ? e : cudaMemset(ctx->d_ticket, 0, sizeof(unsigned int) * 64);
     e = e ? e : cudaMemset(ctx->d_flags, 0, sizeof(unsigned int) * 32 * 1024);
@@ -236,6 +240,8 @@ void tf_context_destroy(tf_context* ctx) {
     cudaFree(ctx->d_acts);
     cudaFree(ctx->d_shared_act);
     cudaFree(ctx->d_sort_cnt);
+    cudaFree(ctx->d_lm_keys);
+    cudaFree(ctx->d_lm_tickets);
     delete ctx;
 }
 

@@ -26,6 +26,8 @@ struct tf_context {
     __half* d_acts = nullptr;          // [8][kMaxF] routed activations
     __half* d_shared_act = nullptr;    // [kMaxFs] shared-expert activation
     uint32_t* d_sort_cnt = nullptr;    // [kRouteSortChunks][256] per-chunk expert counts / bases
+    unsigned long long* d_lm_keys = nullptr;  // [kMaxLmTokens] LM-head argmax keys (left 0)
+    unsigned int* d_lm_tickets = nullptr;     // [kMaxLmTokens] LM-head argmax block tickets (left 0)
 };
 
 // Device grouping: pairs are split into at most this many chunks (one CTA each).
@@ -37,6 +39,7 @@ constexpr int kMaxRouterExperts = 256;
 constexpr int kMaxF = 4096;
 constexpr int kMaxFs = 16384;
 constexpr int kMaxTopKDecode = 8;
+constexpr int kMaxLmTokens = 256;
 
 inline tf_status fail(tf_context* ctx, tf_status s, const char* fmt, ...) {
     if (ctx) {

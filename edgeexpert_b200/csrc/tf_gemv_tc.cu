@@ -68,6 +68,7 @@ struct GtParams {
     long long sb_bstride;  // bytes between matrices' scale (and bias) arrays
     const __half* x;
     __half* y;
+    float* y32;           // fp32 output instead of y (NULL = fp16 y)
     long long y_bstride;  // elements between matrices' outputs
     int M, K, batch, tiles, jobs, R;
     uint32_t* err;
@@ -369,7 +370,12 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemv_tc_kernel(const __grid_con
                 }
             }
             if (!ok) break;
-            if (row0 + rr < p.M) p.y[(long long)b * p.y_bstride + row0 + rr] = __float2half_rn(acc);
+            if (row0 + rr < p.M) {
+                if (p.y32)
+                    p.y32[(long long)b * p.y_bstride + row0 + rr] = acc;
+                else
+                    p.y[(long long)b * p.y_bstride + row0 + rr] = __float2half_rn(acc);
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh.sempty[js]);
         }
@@ -577,9 +583,15 @@ __global__ void __launch_bounds__(GsCfg<SPLIT>::kThreads, 1) gemv_stream_kernel(
                 if (lane == 0) mbar_arrive(&sh.pfree[w]);
             }
             const int rA = row0 + 16 * w + g;
-            __half* yb = p.y + (long long)b * p.y_bstride;
-            if (t == 0 && rA < p.M) yb[rA] = __float2half_rn(accA);
-            if (t == 1 && rA + 8 < p.M) yb[rA + 8] = __float2half_rn(accB);
+            if (p.y32) {
+                float* yb = p.y32 + (long long)b * p.y_bstride;
+                if (t == 0 && rA < p.M) yb[rA] = accA;
+                if (t == 1 && rA + 8 < p.M) yb[rA + 8] = accB;
+            } else {
+                __half* yb = p.y + (long long)b * p.y_bstride;
+                if (t == 0 && rA < p.M) yb[rA] = __float2half_rn(accA);
+                if (t == 1 && rA + 8 < p.M) yb[rA + 8] = __float2half_rn(accB);
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh.sempty[js]);
         }
@@ -683,6 +695,39 @@ tf_status gemv_tc_try(tf_context* ctx, const void* W, const void* S, const void*
     if (kind == kGemvTensorCore)
         return st == TF_SCALE_BF16 ? launch_gemv_tc<__nv_bfloat16>(ctx, p, stream, name)
                                    : launch_gemv_tc<__half>(ctx, p, stream, name);
+    return st == TF_SCALE_BF16 ? launch_gemv_stream<__nv_bfloat16>(ctx, p, stream, name)
+                               : launch_gemv_stream<__half>(ctx, p, stream, name);
+}
+
+}  // namespace tf
+
+namespace tf {
+
+// One-token int4 GEMV on the ring-streamed kernel with fp32 output (the LM
+// head's logits).  Returns TF_ERR_UNSUPPORTED_SHAPE when the shape does not
+// suit the kernel (n % 64, fewer row tiles than SMs, misaligned scales).
+tf_status gemv_stream_f32(tf_context* ctx, const void* W, const void* S, const void* B, const void* x, float* y32,
+                          uint32_t m, uint32_t n, tf_scale_type st, cudaStream_t stream, const char* name) {
+    if (n % 64 || n / 2 % 16 || !aligned16(S) || !aligned16(B) || (st != TF_SCALE_BF16 && st != TF_SCALE_F16))
+        return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: shape or alignment unsupported by the streaming GEMV", name);
+    const int tiles = (int)((m + kGtRows - 1) / kGtRows);
+    const int R = gs_ring_stages((int)n);
+    if (R < 2) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: K too large for the streaming GEMV", name);
+    GtParams p;
+    memset(&p, 0, sizeof(p));
+    if (!make_gt_map(&p.wmap, W, n / 2, m, 1, 0))
+        return fail(ctx, TF_ERR_MISALIGNED, "%s: weights must be 16-byte aligned", name);
+    p.S = static_cast<const uint8_t*>(S);
+    p.B = static_cast<const uint8_t*>(B);
+    p.x = static_cast<const __half*>(x);
+    p.y32 = y32;
+    p.M = (int)m;
+    p.K = (int)n;
+    p.batch = 1;
+    p.tiles = tiles;
+    p.jobs = tiles;
+    p.R = R;
+    p.err = ctx->d_err;
     return st == TF_SCALE_BF16 ? launch_gemv_stream<__nv_bfloat16>(ctx, p, stream, name)
                                : launch_gemv_stream<__half>(ctx, p, stream, name);
 }

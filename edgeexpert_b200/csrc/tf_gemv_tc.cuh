@@ -20,4 +20,15 @@ tf_status gemv_tc_try(tf_context* ctx, const void* W, const void* S, const void*
                       uint32_t batch, const void* x, void* y, uint64_t ybs, uint32_t m, uint32_t n,
                       tf_scale_type st, cudaStream_t stream, int kind, int force, bool* used, const char* name);
 
+// One-token int4 GEMV [m][n] with fp32 output on the ring-streamed kernel
+// (the LM head's logits); TF_ERR_UNSUPPORTED_SHAPE when the kernel cannot
+// take the shape.
+tf_status gemv_stream_f32(tf_context* ctx, const void* W, const void* S, const void* B, const void* x, float* y32,
+                          uint32_t m, uint32_t n, tf_scale_type st, cudaStream_t stream, const char* name);
+
+// Dense int4 GEMM [t][k] x [n][k]^T with fp32 output (tf_qmm.cu).
+tf_status int4_qmm_f32(tf_context* ctx, const void* weights, const void* scales, const void* biases, const void* x,
+                       float* y32, uint32_t t, uint32_t n, uint32_t k, uint32_t x_stride, uint32_t y_stride,
+                       tf_scale_type st, cudaStream_t stream, const char* name);
+
 }  // namespace tf

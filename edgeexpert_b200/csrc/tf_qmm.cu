@@ -90,6 +90,7 @@ struct QmmParams {
     const tf_token_expert_pair* pairs;
     int top_k;
     __half* y;
+    float* y32;  // dense plain mode: fp32 output instead of y (NULL = fp16 y)
     long long ldy;
     int round_gu;  // gate/up rounded to fp16 before GELU (shared expert)
     uint32_t* err;
@@ -624,10 +625,16 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
                         if (fok && colbase + j < t.cnt) p.y[o * p.ldy + f] = __float2half_rn(v[j]);
                     }
                 } else {
+                    if (p.y32) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (fok && colbase + j < t.cnt)
-                            p.y[(long long)(t.row0 + colbase + j) * p.ldy + f] = __float2half_rn(v[j]);
+                        for (int j = 0; j < 32; ++j)
+                            if (fok && colbase + j < t.cnt) p.y32[(long long)(t.row0 + colbase + j) * p.ldy + f] = v[j];
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (fok && colbase + j < t.cnt)
+                                p.y[(long long)(t.row0 + colbase + j) * p.ldy + f] = __float2half_rn(v[j]);
+                    }
                 }
             }
             tc_fence_before();
@@ -651,10 +658,20 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
 
 // Xg[p][:] = X[pairs[p].token][:] (16-byte units): the routed rows in
 // sorted-pair order, so each expert's tokens are one contiguous TMA range.
+// Only the pairs the group table covers are gathered: with empty routing
+// slots (UINT32_MAX ids, skipped by the sort) fewer than P entries are valid.
 __global__ void gather_rows_kernel(const __half* __restrict__ x, long long ldx,
                                    const tf_token_expert_pair* __restrict__ pairs, __half* __restrict__ xg, int P,
-                                   int D, int T, uint32_t* err) {
+                                   int D, int T, const tf_moe_group* __restrict__ groups,
+                                   const uint32_t* __restrict__ n_groups, uint32_t* err) {
     const int d8 = D >> 3;
+    const uint32_t ng = __ldg(n_groups);
+    if (ng) {
+        const tf_moe_group last = groups[ng - 1];
+        P = min(P, (int)(last.pair_start + last.pair_count));
+    } else {
+        P = 0;
+    }
     const long long n = (long long)P * d8;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x) {
@@ -787,11 +804,10 @@ tf_status grouped_gemv(tf_context* ctx, GroupedParams p, cudaStream_t s, const c
 
 extern "C" {
 
-tf_status tf_int4_qmm(tf_context* ctx, const void* weights, const void* scales, const void* biases, const void* x,
-                      void* y, uint32_t t, uint32_t n, uint32_t k, uint32_t x_stride, uint32_t y_stride,
-                      tf_scale_type st, void* stream) {
+static tf_status qmm_dense(tf_context* ctx, const void* weights, const void* scales, const void* biases,
+                           const void* x, void* y, float* y32, uint32_t t, uint32_t n, uint32_t k, uint32_t x_stride,
+                           uint32_t y_stride, tf_scale_type st, void* stream, const char* name) {
     if (!ctx) return TF_ERR_INVALID_ARG;
-    const char* name = "tf_int4_qmm";
     if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, TF_ERR_CUDA, "cudaSetDevice failed");
     if (!scale_type_ok(st)) return fail(ctx, TF_ERR_INVALID_ARG, "%s: bad scale type", name);
     if (k == 0 || k % 64 || n == 0) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: k %% 64 == 0, n > 0", name);
@@ -800,8 +816,10 @@ tf_status tf_int4_qmm(tf_context* ctx, const void* weights, const void* scales, 
     if (x_stride < k || y_stride < n || x_stride % 8)
         return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: x_stride >= k (multiple of 8), y_stride >= n", name);
     if (t == 0) return TF_OK;
-    if (!weights || !scales || !biases || !x || !y) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
-    if (!aligned16(weights) || !aligned16(x) || !aligned2(y) || !aligned2(scales) || !aligned2(biases))
+    void* out = y32 ? static_cast<void*>(y32) : y;
+    if (!weights || !scales || !biases || !x || !out) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
+    if (!aligned16(weights) || !aligned16(x) || !(y32 ? aligned4(out) : aligned2(out)) || !aligned2(scales) ||
+        !aligned2(biases))
         return fail(ctx, TF_ERR_MISALIGNED, "%s: weights/x 16-byte, y/scales/biases 2-byte aligned", name);
     QmmParams p{};
     p.mode = kDensePlain;
@@ -811,9 +829,17 @@ tf_status tf_int4_qmm(tf_context* ctx, const void* weights, const void* scales, 
     if (!dense_weights(p, &p.wmap0, weights, n, k, scales, biases, 0) || !make_act_map(&p.xmap, x, k, t, x_stride))
         return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: tensor map rejected", name);
     p.y = static_cast<__half*>(y);
+    p.y32 = y32;
     p.ldy = y_stride;
     p.err = ctx->d_err;
     return launch_qmm(ctx, p, st, static_cast<cudaStream_t>(stream), name);
+}
+
+tf_status tf_int4_qmm(tf_context* ctx, const void* weights, const void* scales, const void* biases, const void* x,
+                      void* y, uint32_t t, uint32_t n, uint32_t k, uint32_t x_stride, uint32_t y_stride,
+                      tf_scale_type st, void* stream) {
+    return qmm_dense(ctx, weights, scales, biases, x, y, nullptr, t, n, k, x_stride, y_stride, st, stream,
+                     "tf_int4_qmm");
 }
 
 tf_status tf_prefill_shared_expert(tf_context* ctx, const void* x, uint32_t x_stride, const tf_affine_matrix* gate,
@@ -969,7 +995,8 @@ tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64_t expe
         gather_rows_kernel<<<grid, 256, 0, s>>>(static_cast<const __half*>(hidden), hidden_stride,
                                                 static_cast<const tf_token_expert_pair*>(sorted_pairs),
                                                 static_cast<__half*>(route_partials), (int)P, (int)d, (int)t,
-                                                ctx->d_err);
+                                                static_cast<const tf_moe_group*>(groups),
+                                                static_cast<const uint32_t*>(n_groups), ctx->d_err);
         tf_status rc0 = cuda_check(ctx, cudaGetLastError(), name);
         if (rc0 != TF_OK) return rc0;
     }
@@ -998,3 +1025,15 @@ tf_status tf_moe_reduce_token_major(tf_context* ctx, const void* route_partials,
 }
 
 }  // extern "C"
+
+namespace tf {
+
+// Dense int4 GEMM with fp32 output Y32[t][j] (row stride y_stride floats):
+// the LM head's logits for several tokens at once.
+tf_status int4_qmm_f32(tf_context* ctx, const void* weights, const void* scales, const void* biases, const void* x,
+                       float* y32, uint32_t t, uint32_t n, uint32_t k, uint32_t x_stride, uint32_t y_stride,
+                       tf_scale_type st, cudaStream_t stream, const char* name) {
+    return qmm_dense(ctx, weights, scales, biases, x, nullptr, y32, t, n, k, x_stride, y_stride, st, stream, name);
+}
+
+}  // namespace tf

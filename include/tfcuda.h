@@ -336,6 +336,79 @@ TF_API tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64
 TF_API tf_status tf_moe_reduce_token_major(tf_context* ctx, const void* route_partials, const void* routing_weights,
                                            void* h2, uint32_t T, uint32_t top_k, uint32_t d, void* stream);
 
+/* ---- dense decode stack (the Gemma 4 decoder layer around the MoE FFN) ----------------------
+ * RealForwardRunner.produceToken (Sources/TurboFieldfare/Runtime/Inference/RealForwardRunner.swift:2240-2480).
+ * Norm weights are BF16 [d] (or [head_dim]); activations fp16; rows are tokens. */
+
+/* rmsnorm_bf16w / rmsnorm_no_scale (Sources/TurboFieldfare/Metal/Primitives/rmsnorm.metal:32-150):
+ * out[r][i] = half(x[r][i] * rsqrt(mean_i(x^2) + eps) * w[i]); weight NULL = no scale.
+ * Strides in elements (0 = d). */
+TF_API tf_status tf_rmsnorm(tf_context* ctx, const void* x, uint32_t x_stride, const void* weight, void* out,
+                            uint32_t out_stride, uint32_t rows, uint32_t d, float eps, void* stream);
+
+/* fused_qkv_epilogue (Sources/TurboFieldfare/Metal/Fusions/fused.metal:84-170), in place, for T
+ * tokens: per head RMSNorm over head_dim (Q and K times the shared BF16 q/k
+ * weight, V without scale), rounded to fp16, then NeoX RoPE at `position`
+ * (freq = theta^(-2i/head_dim)) on the first rotated_pairs pairs of Q and K.
+ * q[t*q_stride + h*head_dim + i]; k/v: the cache slots of this position,
+ * token t at k + t*kv_stride elements.  head_dim even, <= 512. */
+TF_API tf_status tf_qkv_epilogue(tf_context* ctx, void* q, uint32_t q_stride, void* k, void* v, uint64_t kv_stride,
+                                 const void* q_weight, const void* k_weight, uint32_t head_dim, uint32_t num_q_heads,
+                                 uint32_t num_kv_heads, uint32_t T, uint32_t position, float theta,
+                                 uint32_t rotated_pairs, float eps, void* stream);
+
+/* Split-KV GQA decode attention over an fp16 cache
+ * (attention_decode_partial / _combine, Sources/TurboFieldfare/Metal/Attention/attention.metal:135-240;
+ * the same online-softmax result as attention_decode_single :241-312):
+ * out[t][h] = half(sum_p softmax_p(scale * q[t][h].k_p) v_p), p in [kv_start, seq_len),
+ * kv head = h / (num_q_heads / num_kv_heads).  Caches are [seq][num_kv_heads][head_dim]
+ * per token, token t at + t*seq_stride elements.  head_dim a multiple of 8 up to 256 (or 512);
+ * at most 8 query heads per KV head.  workspace: caller-owned device scratch of
+ * tf_attention_workspace_bytes (the reference's m/d/o partial buffers). */
+TF_API size_t tf_attention_workspace_bytes(const tf_context* ctx, uint32_t T, uint32_t head_dim, uint32_t num_q_heads,
+                                           uint32_t num_kv_heads, uint32_t seq_len);
+TF_API tf_status tf_attention_decode(tf_context* ctx, const void* q, uint32_t q_stride, const void* k_cache,
+                                     const void* v_cache, uint64_t seq_stride, void* out, uint32_t out_stride,
+                                     uint32_t head_dim, uint32_t num_q_heads, uint32_t num_kv_heads, uint32_t T,
+                                     uint32_t seq_len, uint32_t kv_start, float scale, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+
+/* fused_post_attn_setup (Sources/TurboFieldfare/Metal/Fusions/fused.metal:190-269), per row:
+ *   hidden = half(hidden + half(attn * inv(attn) * w_post_attn));
+ *   dense_x = half(hidden * inv(hidden) * w_pre_ffn), routed_x = ... * w_pre_ffn2,
+ *   router_x = half(hidden * inv(hidden)).  dense_x / routed_x / router_x may be NULL. */
+TF_API tf_status tf_post_attn_setup(tf_context* ctx, void* hidden, const void* attn, void* dense_x, void* routed_x,
+                                    void* router_x, const void* w_post_attn, const void* w_pre_ffn,
+                                    const void* w_pre_ffn2, uint32_t rows, uint32_t d, float eps, void* stream);
+
+/* The decoder-layer tail, the layer combine of the MoE FFN (fused_layer_tail,
+ * Sources/TurboFieldfare/Metal/Fusions/fused.metal:271-375), per row, after the shared
+ * expert's own post-FFN norm when w_post_ffn1 != NULL (RealForwardRunner.swift:191):
+ *   h1n = half(h1 * inv(h1) * w_post_ffn1)          (h1n = h1 when w_post_ffn1 is NULL)
+ *   h12 = half(h1n + half(h2 * inv(h2) * w_post_ffn2))
+ *   hidden = half(half(hidden + half(h12 * inv(h12) * w_post_ffn)) * half(layer_scalar)). */
+TF_API tf_status tf_layer_tail(tf_context* ctx, const void* h2, const void* h1, void* hidden, const void* w_post_ffn1,
+                               const void* w_post_ffn2, const void* w_post_ffn, float layer_scalar, uint32_t rows,
+                               uint32_t d, float eps, void* stream);
+
+/* embed_lookup_int4 (Sources/TurboFieldfare/Metal/Quant/dequant_int4.metal:65-84) for T tokens:
+ * out[t][i] = half((q * s + b) * out_scale) of row token_ids[t] (device uint32) of the int4
+ * table [vocab][d].  An id >= vocab gives a zero row and the device error bit. */
+TF_API tf_status tf_embed_int4(tf_context* ctx, const void* table, const void* scales, const void* biases,
+                               const void* token_ids, uint32_t T, uint32_t vocab, uint32_t d, float out_scale,
+                               void* out, uint32_t out_stride, tf_scale_type st, void* stream);
+
+/* LMHeadChainInt4 (Sources/TurboFieldfare/Kernels/Fusions/LMHeadChainInt4.swift:1-135;
+ * lm_head_greedy_int4_rows_chunk_raw / _reduce, Metal/Sampling/logit.metal:687-787):
+ * x = rmsnorm_bf16w(hidden, norm_weight) -> fp32 logits = W x (int4 [vocab][d]) ->
+ * out_tokens[t] = the row with the largest finite logit, ties to the lower row (0 when none).
+ * Scratch (caller-owned): x_normed fp16 [T][d], logits float [T][vocab], 16-byte aligned.
+ * T <= 256; one token streams the weights on the ring GEMV, more use the tcgen05 GEMM. */
+TF_API tf_status tf_lm_head_greedy(tf_context* ctx, const void* hidden, uint32_t hidden_stride, const void* norm_weight,
+                                   float eps, const void* W, const void* scales, const void* biases, uint32_t vocab,
+                                   uint32_t d, uint32_t T, void* x_normed, void* logits, void* out_tokens,
+                                   tf_scale_type st, void* stream);
+
 /* ---- expert parallelism (routed experts sharded over GPUs) ------------------------------
  * No reference counterpart (the reference streams experts from SSD on one GPU).
  * Experts are sharded in contiguous id ranges of experts_per_rank; the

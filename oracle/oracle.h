@@ -190,6 +190,30 @@ float orc_rel_error(const float *actual, const float *ref, size_t n);
 /* Number of OpenMP threads available (1 when built without OpenMP). */
 int orc_max_threads(void);
 
+/* ---- dense decode stack (oracle_decoder.c) -------------------------------- */
+/* rmsnorm_bf16w / rmsnorm_no_scale (Metal/Primitives/rmsnorm.metal:32-150); w NULL = no scale. */
+void orc_rmsnorm(const uint16_t *x, const uint16_t *w_bf16, uint16_t *out, int rows, int d, float eps);
+/* fused_qkv_epilogue (Metal/Fusions/fused.metal:84-170), in place. */
+void orc_qkv_epilogue(uint16_t *q, uint16_t *k, uint16_t *v, const uint16_t *qw, const uint16_t *kw, int hd,
+                      int nq, int nkv, int position, float theta, int rotated_pairs, float eps);
+/* attention_decode_single (Metal/Attention/attention.metal:241-312), K/V [seq][nkv][hd]. */
+void orc_attention_decode(const uint16_t *q, const uint16_t *K, const uint16_t *V, uint16_t *out, float *out32,
+                          int hd, int nq, int nkv, int seq_len, int kv_start, float scale);
+/* fused_post_attn_setup (Metal/Fusions/fused.metal:190-269). */
+void orc_post_attn_setup(uint16_t *hidden, const uint16_t *attn, uint16_t *dense_x, uint16_t *routed_x,
+                         uint16_t *router_x, const uint16_t *w_post_attn, const uint16_t *w_pre_ffn,
+                         const uint16_t *w_pre_ffn2, int rows, int d, float eps);
+/* fused_layer_tail (Metal/Fusions/fused.metal:271-375) after the optional post-FFN-1 norm. */
+void orc_layer_tail(const uint16_t *h2, const uint16_t *h1, uint16_t *hidden, const uint16_t *w_postffn1,
+                    const uint16_t *w_postffn2, const uint16_t *w_postffn, float layer_scalar, int rows, int d,
+                    float eps);
+/* embed_lookup_int4 (Metal/Quant/dequant_int4.metal:65-84). */
+void orc_embed_int4(const uint8_t *table, const uint16_t *S, const uint16_t *B, int st, const uint32_t *tokens,
+                    int T, int d, float out_scale, uint16_t *out);
+/* lm_head_greedy_int4_rows_chunk_raw + _reduce (Metal/Sampling/logit.metal:687-787). */
+uint32_t orc_lm_head_greedy(const uint8_t *W, const uint16_t *S, const uint16_t *B, int st, const uint16_t *x_f16,
+                            int vocab, int d, float *logits, int nthreads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -104,6 +104,13 @@ def lib():
                 "orc_int4_qmm": ([u8p, u16p, u16p, I, u16p, u16p, f32p, I, I, I, I], None),
                 "orc_rel_error": ([f32p, f32p, C.c_size_t], C.c_float),
                 "orc_max_threads": ([], I),
+                "orc_rmsnorm": ([u16p, VP, u16p, I, I, C.c_float], None),
+                "orc_qkv_epilogue": ([u16p, u16p, u16p, u16p, u16p, I, I, I, I, C.c_float, I, C.c_float], None),
+                "orc_attention_decode": ([u16p, u16p, u16p, VP, VP, I, I, I, I, I, C.c_float], None),
+                "orc_post_attn_setup": ([u16p, u16p, u16p, u16p, u16p, u16p, u16p, u16p, I, I, C.c_float], None),
+                "orc_layer_tail": ([u16p, u16p, u16p, VP, u16p, u16p, C.c_float, I, I, C.c_float], None),
+                "orc_embed_int4": ([u8p, u16p, u16p, I, u32p, I, I, C.c_float, u16p], None),
+                "orc_lm_head_greedy": ([u8p, u16p, u16p, I, u16p, I, I, VP, I], C.c_uint32),
             }
             for name, (args, res) in sig.items():
                 fn = getattr(L, name)
@@ -367,3 +374,66 @@ def rel_error(actual, ref) -> float:
     a = np.ascontiguousarray(actual, np.float32).reshape(-1)
     r = np.ascontiguousarray(ref, np.float32).reshape(-1)
     return float(lib().orc_rel_error(a, r, a.size))
+
+
+# ------------------------------------------------------- decode stack ------
+def _vp(a):
+    return None if a is None else np.ascontiguousarray(a).ctypes.data_as(C.c_void_p)
+
+
+def rmsnorm(x_f16, w_bf16, rows: int, d: int, eps: float = 1e-6) -> np.ndarray:
+    """rmsnorm_bf16w (w given) / rmsnorm_no_scale (w None), fp16 bits out."""
+    out = np.empty(rows * d, np.uint16)
+    w = None if w_bf16 is None else np.ascontiguousarray(w_bf16, np.uint16)
+    lib().orc_rmsnorm(np.ascontiguousarray(x_f16, np.uint16).reshape(-1), _vp(w), out, rows, d, eps)
+    return out
+
+
+def qkv_epilogue(q, k, v, qw, kw, hd, nq, nkv, position, theta, rotated_pairs, eps=1e-6):
+    q, k, v = (np.ascontiguousarray(a, np.uint16).reshape(-1).copy() for a in (q, k, v))
+    lib().orc_qkv_epilogue(q, k, v, np.ascontiguousarray(qw, np.uint16), np.ascontiguousarray(kw, np.uint16), hd,
+                           nq, nkv, position, theta, rotated_pairs, eps)
+    return q, k, v
+
+
+def attention_decode(q, K, V, hd, nq, nkv, seq_len, kv_start=0, scale=1.0):
+    """Returns (fp16 bits, fp32) [nq*hd]."""
+    o16 = np.empty(nq * hd, np.uint16)
+    o32 = np.empty(nq * hd, np.float32)
+    keep = [np.ascontiguousarray(a, np.uint16).reshape(-1) for a in (q, K, V)]
+    lib().orc_attention_decode(*keep, _vp(o16), _vp(o32), hd, nq, nkv, seq_len, kv_start, scale)
+    return o16, o32
+
+
+def post_attn_setup(hidden, attn, w_post_attn, w_pre_ffn, w_pre_ffn2, rows, d, eps=1e-6):
+    h = np.ascontiguousarray(hidden, np.uint16).reshape(-1).copy()
+    dx, rx, rt = (np.empty(rows * d, np.uint16) for _ in range(3))
+    lib().orc_post_attn_setup(h, np.ascontiguousarray(attn, np.uint16).reshape(-1), dx, rx, rt,
+                              *[np.ascontiguousarray(w, np.uint16) for w in (w_post_attn, w_pre_ffn, w_pre_ffn2)],
+                              rows, d, eps)
+    return h, dx, rx, rt
+
+
+def layer_tail(h2, h1, hidden, w_postffn1, w_postffn2, w_postffn, layer_scalar, rows, d, eps=1e-6):
+    h = np.ascontiguousarray(hidden, np.uint16).reshape(-1).copy()
+    w1 = None if w_postffn1 is None else np.ascontiguousarray(w_postffn1, np.uint16)
+    lib().orc_layer_tail(np.ascontiguousarray(h2, np.uint16).reshape(-1), np.ascontiguousarray(h1, np.uint16).reshape(-1),
+                         h, _vp(w1), np.ascontiguousarray(w_postffn2, np.uint16),
+                         np.ascontiguousarray(w_postffn, np.uint16), layer_scalar, rows, d, eps)
+    return h
+
+
+def embed_int4(table, S, B, tokens, d, out_scale=1.0, scale_type=0):
+    t = np.ascontiguousarray(tokens, np.uint32)
+    out = np.empty(t.size * d, np.uint16)
+    lib().orc_embed_int4(np.ascontiguousarray(table), np.ascontiguousarray(S), np.ascontiguousarray(B), scale_type, t,
+                         t.size, d, out_scale, out)
+    return out
+
+
+def lm_head_greedy(W, S, B, x_f16, vocab, d, scale_type=0, nthreads=0, want_logits=False):
+    logits = np.empty(vocab, np.float32) if want_logits else None
+    tok = lib().orc_lm_head_greedy(np.ascontiguousarray(W), np.ascontiguousarray(S), np.ascontiguousarray(B),
+                                   scale_type, np.ascontiguousarray(x_f16, np.uint16), vocab, d, _vp(logits),
+                                   _nt(nthreads))
+    return (int(tok), logits) if want_logits else int(tok)
