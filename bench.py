@@ -51,6 +51,9 @@ def parse():
                     help="scale/bias storage; default fp16 for config 0 (as BASELINE states it), else bf16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemv", action="store_true", help="decode: skip the config-0 GEMV sub-record")
+    ap.add_argument("--no-stack", action="store_true", help="moe: skip the full decoder-stack sub-record")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="expert-parallel exchange at N > 1: peer-memory stores (default) or NCCL all-to-alls")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--workload", choices=["moe", "decode", "gemv", "batched", "prefill", "ep"], default="moe",
                     help="moe (default) = config-4 MoE decode step at batch 256/32/1 through 30 layers, experts "
@@ -817,8 +820,12 @@ def run_moe(a, rank, world, local_rank):
         ys = torch.empty(L, Tm, D, dtype=torch.float16, device=dev)
         sact = torch.empty(Tm, FS, dtype=torch.float16, device=dev)
         fused_b1 = world == 1 and B == 1
+        xch = None
         if world > 1:
-            eps = [ExpertParallelMoE(layers[l].experts, E, TOPK, cap, D, F, context=ctx, device=dev) for l in range(L)]
+            from edgeexpert_b200.ep import P2PExchange
+            xch = P2PExchange(world, rank, cap, D, context=ctx, device=dev) if a.exchange == "p2p" else None
+            eps = [ExpertParallelMoE(layers[l].experts, E, TOPK, cap, D, F, context=ctx, device=dev, p2p=xch)
+                   for l in range(L)]
         elif not fused_b1:
             act = torch.empty(T * TOPK, F, dtype=torch.float16, device=dev)
             part = torch.empty(T * TOPK, D, dtype=torch.float16, device=dev)
@@ -856,6 +863,8 @@ def run_moe(a, rank, world, local_rank):
                     launches += 3
 
         # eager warm-up (kernel attributes, NCCL communicators), then one graph per ring slot + x_in
+        torch.cuda.synchronize()
+        barrier()
         with torch.cuda.stream(stream):
             step(xs[0])
         torch.cuda.synchronize()
@@ -958,13 +967,23 @@ def run_moe(a, rank, world, local_rank):
             "hbm_bytes_per_gpu": bytes_gpu, "hbm_gbs_per_gpu": bytes_gpu / (ms * 1e-3) / 1e9,
             "gpu_launches_per_step": launches,
             "h2d_bytes_per_step": L * T * D * 2, "d2h_bytes_per_step": L * T * (2 * D * 2 + TOPK * 4),
-            "nvlink_bytes_per_gpu_per_step": (2 * L * (world - 1) * cap * (2 * D + 64 + 4 * D)) if world > 1 else 0,
+            "nvlink_bytes_per_gpu_per_step": (L * (world - 1) * cap * (2 * D + 64 + 4 * D)) if world > 1 else 0,
+            "exchange": (a.exchange if world > 1 else "none"),
             "clocks": clk,
         }
         del graphs
         if world > 1:
             del eps
+            if xch is not None:
+                barrier()
+                xch.close()
         torch.cuda.empty_cache()
+
+    # the full config-4 decode step (attention over a 4096-token fp16 KV cache,
+    # norms, the MoE layers above, the int4 LM head and greedy selection)
+    stack = None
+    if not a.no_stack:
+        stack = run_decoder_stack(a, rank, world, local_rank, layers, dev, ctx, stream, max_over_ranks, barrier)
 
     peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
     peak, peak_src = (peaks["hbm_gbs"], "measured hbm_gbs") if "hbm_gbs" in peaks else (6650.0, "fallback")
@@ -999,6 +1018,7 @@ def run_moe(a, rank, world, local_rank):
                                f"(router + {TOPK} routed of {E} + shared), experts sharded {per} per GPU",
                    "d": D, "f": F, "fs": FS, "experts": E, "top_k": TOPK, "layers": L, "global_batch": Bh,
                    "parallelism": f"ep{world}" if world > 1 else "1gpu", "scale_dtype": a.scale_dtype,
+                   "exchange": (f"{a.exchange} (fixed capacity, no host readback)" if world > 1 else "none"),
                    "l2": "weights per step (%.1f GB per GPU) exceed L2 (126 MB); no flush needed" %
                          (head["hbm_bytes_per_gpu"] / 1e9),
                    "outputs": "routed h2 and shared y per layer, kept separate"},
@@ -1022,7 +1042,143 @@ def run_moe(a, rank, world, local_rank):
         line["gemv"] = {k: gemv[k] for k in ("metric", "value", "unit", "steps", "ms_per_step", "config",
                                              "single_gemv_us", "single_gemv_gbs", "e2e", "roofline", "cpu_baseline",
                                              "clocks", "gpu_launches")}
+    if stack is not None:
+        line["decoder_stack"] = stack
     print(json.dumps(line), flush=True)
+
+
+CONTEXT = 4096
+
+
+def run_decoder_stack(a, rank, world, local_rank, moe_layers, dev, ctx, stream, max_over_ranks, barrier):
+    """Config 4: one decode step of B sequences at position 4095 (attention over
+    4096 cached tokens) through every layer (input norm, q/k/v int4 GEMVs, q/k/v
+    norms + RoPE, split-KV attention, o_proj, post-attention norms, router,
+    routed experts -- expert-parallel over the GPUs --, shared expert, layer
+    tail) and the int4 LM head with greedy selection.  Tokens are split B/N
+    per GPU with their KV caches.  A batch whose caches do not fit (1 GB per
+    sequence) on every rank is reported as skipped."""
+    import torch
+    import torch.distributed as dist
+
+    from edgeexpert_b200.decoder import Decoder, DecoderConfig, KVCache, synthetic_decoder
+    from edgeexpert_b200.ep import ExpertParallelMoE
+    cfg = DecoderConfig(layers=len(moe_layers), max_context=CONTEXT)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4040)
+    w = synthetic_decoder(cfg, dev, gen, moe_layers=moe_layers)
+    per = E // world
+    out = {"context": CONTEXT, "layers": cfg.layers, "heads": f"{cfg.num_q_heads}q/{cfg.num_kv_heads}kv x {cfg.head_dim}",
+           "vocab": cfg.vocab, "batches": {}}
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs", 6650.0)
+    for B in (1, 32, 256):
+        T = tokens_of(B, world, rank)
+        cap = -(-B // world)
+        kv_bytes = 2 * cfg.layers * max(T, 1) * CONTEXT * cfg.num_kv_heads * cfg.head_dim * 2
+        free, _ = torch.cuda.mem_get_info(dev)
+        fits = kv_bytes + (6 << 30) < free
+        if world > 1:
+            f = torch.tensor([1 if fits else 0], device=dev)
+            dist.all_reduce(f, op=dist.ReduceOp.MIN)
+            fits = bool(f.item())
+        if not fits:
+            out["batches"][str(B)] = {"skipped": f"KV cache of {max(T, 1)} sequences x {CONTEXT} tokens "
+                                                 f"({kv_bytes / 1e9:.0f} GB per GPU) does not fit"}
+            continue
+        cache = KVCache(cfg, max(T, 1), dev)
+        cache.fill_random(gen, CONTEXT)
+        eps, xch = None, None
+        if world > 1:
+            from edgeexpert_b200.ep import P2PExchange
+            xch = P2PExchange(world, rank, cap, D, context=ctx, device=dev) if a.exchange == "p2p" else None
+            eps = [ExpertParallelMoE(L.experts, E, TOPK, cap, D, F, context=ctx, device=dev, p2p=xch)
+                   for L in moe_layers]
+        dec = Decoder(w, T, cache, context=ctx, device=dev, ep_layers=eps)
+        toks = torch.randint(0, cfg.vocab, (max(T, 1),), device=dev, dtype=torch.int32, generator=gen)
+        torch.cuda.synchronize()
+        barrier()
+        with torch.cuda.stream(stream):
+            dec.step(toks, CONTEXT - 1, stream=stream)
+        torch.cuda.synchronize()
+        barrier()
+        g = torch.cuda.CUDAGraph()
+        use_graph = True
+        try:
+            with torch.cuda.graph(g, stream=stream):
+                dec.step(toks, CONTEXT - 1, stream=stream)
+        except Exception as exc:  # noqa: BLE001 -- eager launches, reported
+            use_graph = False
+            torch.cuda.synchronize()
+            print(f"[bench] decoder graph capture failed ({exc}); timing eager launches", file=sys.stderr)
+        torch.cuda.synchronize()
+        barrier()
+
+        def run():
+            if use_graph:
+                g.replay()
+            else:
+                dec.step(toks, CONTEXT - 1, stream=stream)
+
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, a.warmup)):
+                run()
+        torch.cuda.synchronize()
+        barrier()
+        steps = max(5, a.steps // 2)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(steps):
+                run()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+        # end to end: the step's token ids from pinned host memory, the next tokens back
+        h_tok = torch.empty(max(T, 1), dtype=torch.int32, pin_memory=True)
+        h_tok.copy_(toks.cpu())
+        h_next = torch.empty(max(T, 1), dtype=torch.int32, pin_memory=True)
+        barrier()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            f0.record(stream)
+            for _ in range(steps):
+                toks.copy_(h_tok, non_blocking=True)
+                run()
+                h_next.copy_(dec.tokens, non_blocking=True)
+            f1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms_e2e = max_over_ranks(f0.elapsed_time(f1) / steps)
+        ctx.check_device(stream)
+        # distinct local experts of the last layer's routing (every rank's tokens reach these experts)
+        mine = torch.full((cap * TOPK,), -1, dtype=torch.int32, device=dev)
+        if T:
+            mine[:T * TOPK] = dec.idx[:T].reshape(-1)
+        if world > 1:
+            allr = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(allr, mine)
+            idx_all = torch.cat(allr).cpu()
+        else:
+            idx_all = mine.cpu()
+        distinct = float(torch.unique(idx_all[(idx_all >= rank * per) & (idx_all < (rank + 1) * per)]).numel())
+        wbytes = dec.weight_bytes_per_step(distinct)
+        kv_read = cache.nbytes_per_token(CONTEXT) * T
+        out["batches"][str(B)] = {
+            "tokens": B, "tokens_per_gpu": T, "ms_per_step": ms, "tok_s": B * 1e3 / ms, "tok_s_e2e": B * 1e3 / ms_e2e,
+            "graph": use_graph, "gpu_launches_per_step": dec.launches,
+            "hbm_bytes_per_gpu": wbytes + kv_read, "kv_bytes_per_gpu": kv_read,
+            "hbm_gbs_per_gpu": (wbytes + kv_read) / (ms * 1e-3) / 1e9,
+            "roofline_frac": (wbytes + kv_read) / (ms * 1e-3) / 1e9 / peak,
+            "h2d_bytes_per_step": 4 * T, "d2h_bytes_per_step": 4 * T,
+        }
+        del g, dec, cache, eps
+        if xch is not None:
+            barrier()
+            xch.close()
+        torch.cuda.empty_cache()
+    return out
 
 
 # ------------------------------------------------------ chunk workloads ----

@@ -135,6 +135,19 @@ _PROTOS = {
     "tf_layer_tail": ([_P, _P, _P, _P, _P, _P, _P, C.c_float, _U32, _U32, C.c_float, _P], _I),
     "tf_embed_int4": ([_P, _P, _P, _P, _P, _U32, _U32, _U32, C.c_float, _P, _U32, _I, _P], _I),
     "tf_lm_head_greedy": ([_P, _P, _U32, _P, C.c_float, _P, _P, _P, _U32, _U32, _U32, _P, _P, _P, _I, _P], _I),
+    "tf_softcap_softmax": ([_P, _P, _I, _P, _U32, _U32, C.c_float, _P], _I),
+    "tf_sample": ([_P, _P, _U32, C.c_float, _U32, C.c_float, _U64, _U32, _P, _P], _I),
+    "tf_sample_topk64": ([_P, _P, _U32, C.c_float, C.c_float, _U64, _P, _P], _I),
+    "tf_ep_flag_bytes": ([_U32], C.c_size_t),
+    "tf_ep_ipc_alloc": ([_P, C.c_size_t, C.POINTER(_P), _P], _I),
+    "tf_ep_ipc_open": ([_P, _P, C.POINTER(_P)], _I),
+    "tf_ep_ipc_close": ([_P, _P], _I),
+    "tf_ep_ipc_free": ([_P, _P], _I),
+    "tf_ep_dispatch_p2p": ([_P, _P, _U32, _P, _P, _U32, _U32, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P, _P, _P],
+                           _I),
+    "tf_ep_dispatch_unpack_p2p": ([_P, _P, _P, _U32, _U32, _U32, _U32, _P, _P, _P], _I),
+    "tf_ep_combine_p2p": ([_P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _P, _P, _P, _P], _I),
+    "tf_ep_return_reduce_p2p": ([_P, _P, _P, _U32, _U32, _U32, _U32, _P, _U32, _P], _I),
     "tf_ep_dispatch_pack": ([_P, _P, _U32, _P, _P, _U32, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P], _I),
     "tf_ep_dispatch_unpack": ([_P, _P, _U32, _U32, _U32, _P, _P, _P], _I),
     "tf_ep_expert_combine": ([_P, _P, _P, _P, _U32, _U32, _U32, _P, _P], _I),

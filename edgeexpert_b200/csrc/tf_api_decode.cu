@@ -215,6 +215,9 @@ tf_status tf_context_create(int device, tf_context** out) {
     e = e ? e : cudaMalloc(&ctx->d_lm_keys, sizeof(unsigned long long) * kMaxLmTokens);
     e = e ? e : cudaMalloc(&ctx->d_lm_tickets, sizeof(unsigned int) * kMaxLmTokens);
     e = e ? e : cudaMemset(ctx->d_lm_keys, 0, sizeof(unsigned long long) * kMaxLmTokens);
+    e = e ? e : cudaMalloc(&ctx->d_smx, sizeof(float) * kMaxLmTokens * 128 * 2);
+    e = e ? e : cudaMalloc(&ctx->d_cand_v, sizeof(float) * 2 * kCandCap);
+    e = e ? e : cudaMalloc(&ctx->d_cand_i, sizeof(uint32_t) * 2 * kCandCap);
     e = e ? e : cudaMemset(ctx->d_lm_tickets, 0, sizeof(unsigned int) * kMaxLmTokens);
     e = e ? e : cudaMemset(ctx->d_err, 0, 4 * sizeof(uint32_t));
     e = e ? e : cudaMemset(ctx->d_ticket, 0, sizeof(unsigned int) * 64);
@@ -242,6 +245,9 @@ void tf_context_destroy(tf_context* ctx) {
     cudaFree(ctx->d_sort_cnt);
     cudaFree(ctx->d_lm_keys);
     cudaFree(ctx->d_lm_tickets);
+    cudaFree(ctx->d_smx);
+    cudaFree(ctx->d_cand_v);
+    cudaFree(ctx->d_cand_i);
     delete ctx;
 }
 

@@ -28,6 +28,9 @@ struct tf_context {
     uint32_t* d_sort_cnt = nullptr;    // [kRouteSortChunks][256] per-chunk expert counts / bases
     unsigned long long* d_lm_keys = nullptr;  // [kMaxLmTokens] LM-head argmax keys (left 0)
     unsigned int* d_lm_tickets = nullptr;     // [kMaxLmTokens] LM-head argmax block tickets (left 0)
+    float* d_smx = nullptr;                   // [kMaxLmTokens][128][2] softmax partials (m, d)
+    float* d_cand_v = nullptr;                // [2][kCandCap] top-K candidate values (sampling)
+    uint32_t* d_cand_i = nullptr;             // [2][kCandCap] top-K candidate indices
 };
 
 // Device grouping: pairs are split into at most this many chunks (one CTA each).
@@ -40,6 +43,7 @@ constexpr int kMaxF = 4096;
 constexpr int kMaxFs = 16384;
 constexpr int kMaxTopKDecode = 8;
 constexpr int kMaxLmTokens = 256;
+constexpr int kCandCap = 65536;  // 256 tiles x 256 candidates: a 262144-entry vocabulary
 
 inline tf_status fail(tf_context* ctx, tf_status s, const char* fmt, ...) {
     if (ctx) {

@@ -1,5 +1,6 @@
 // tf_gemv_tc.cuh -- entry of the tensor-core one-token int4 GEMV (tf_gemv_tc.cu).
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "../../include/tfcuda.h"
@@ -30,5 +31,14 @@ tf_status gemv_stream_f32(tf_context* ctx, const void* W, const void* S, const v
 tf_status int4_qmm_f32(tf_context* ctx, const void* weights, const void* scales, const void* biases, const void* x,
                        float* y32, uint32_t t, uint32_t n, uint32_t k, uint32_t x_stride, uint32_t y_stride,
                        tf_scale_type st, cudaStream_t stream, const char* name);
+
+// Grouped routed experts (gate/up + GELU, then down) on the ring-streamed
+// grouped kernel (tf_grouped_stream.cu); TF_ERR_UNSUPPORTED_SHAPE when the
+// shapes do not suit it.
+tf_status grouped_stream(tf_context* ctx, const uint8_t* pool, uint64_t stride, uint32_t num_experts,
+                         const tf_expert_offsets* off, const tf_token_expert_pair* pairs, const tf_moe_group* groups,
+                         const uint32_t* n_groups, const __half* hidden, uint32_t hidden_stride, __half* acts,
+                         __half* partials, uint32_t T, uint32_t d, uint32_t f, uint32_t top_k, tf_scale_type st,
+                         cudaStream_t s, const char* name);
 
 }  // namespace tf

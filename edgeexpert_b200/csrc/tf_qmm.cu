@@ -32,6 +32,7 @@
 // rows are first gathered into sorted-pair order (gather_rows_kernel) so that
 // every expert's tokens are one contiguous TMA range.
 #include "tf_context.cuh"
+#include "tf_gemv_tc.cuh"
 #include "tf_umma.cuh"
 
 using namespace tf;
@@ -928,7 +929,18 @@ tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64_t expe
     // (prefill): the tcgen05 GEMMs.  TFCUDA_GROUPED=gemv|gemm forces one.
     const char* env = getenv("TFCUDA_GROUPED");
     bool gemv = (uint64_t)P <= 12ull * num_experts;
+    bool engine = false;
     if (env && env[0] == 'g' && env[1] == 'e' && env[2] == 'm') gemv = env[3] == 'v';
+    if (env && env[0] == 'e' && env[1] == 'n') gemv = engine = true;
+    if (gemv && !engine) {
+        // default for few tokens per expert: the grouped ring-streamed kernel
+        const tf_status rc = grouped_stream(
+            ctx, pb, expert_stride, num_experts, off, static_cast<const tf_token_expert_pair*>(sorted_pairs),
+            static_cast<const tf_moe_group*>(groups), static_cast<const uint32_t*>(n_groups),
+            static_cast<const __half*>(hidden), hidden_stride, static_cast<__half*>(act_scratch),
+            static_cast<__half*>(route_partials), t, d, f, top_k, st, s, name);
+        if (rc != TF_ERR_UNSUPPORTED_SHAPE) return rc;
+    }
     if (gemv) {
         GroupedParams g{};
         bool ok = make_weight_map(&g.map[0], pb + off->gate_w, d / 2, f, num_experts, expert_stride) &&

@@ -248,41 +248,45 @@ class Decoder:
     is allocated here once; `step` only enqueues work."""
 
     def __init__(self, weights: DecoderWeights, T: int, cache: KVCache, context: Context | None = None,
-                 device=None):
-        from .moe import MoE  # noqa: F401  (the MoE ops share the context)
+                 device=None, ep_layers: list | None = None):
+        """`ep_layers` (one ExpertParallelMoE per layer) routes the experts over
+        the process group; the router, shared expert and attention stay local.
+        T may be 0 on a rank that only serves experts."""
         cfg = weights.cfg
         self.w, self.cfg, self.T, self.cache = weights, cfg, T, cache
+        self.ep = ep_layers
+        Ta = max(T, 1)  # buffers of a rank without tokens (it still serves experts)
         self.ctx = context or Context.get(torch.cuda.current_device())
         dev = device or torch.device("cuda", torch.cuda.current_device())
         d, hd, nq, nkv = cfg.d, cfg.head_dim, cfg.num_q_heads, cfg.num_kv_heads
         f16 = dict(dtype=torch.float16, device=dev)
-        self.h = torch.zeros(T, d, **f16)
-        self.normed = torch.empty(T, d, **f16)
-        self.q = torch.empty(T, nq * hd, **f16)
-        self.attn = torch.empty(T, nq * hd, **f16)
-        self.o = torch.empty(T, d, **f16)
-        self.dense_x = torch.empty(T, d, **f16)
-        self.routed_x = torch.empty(T, d, **f16)
-        self.router_x = torch.empty(T, d, **f16)
-        self.h1 = torch.empty(T, d, **f16)
-        self.h2 = torch.empty(T, d, **f16)
-        self.idx = torch.empty(T, cfg.top_k, dtype=torch.int32, device=dev)
-        self.wts = torch.empty(T, cfg.top_k, dtype=torch.float16, device=dev)
-        self.sact = torch.empty(T, cfg.fs, **f16)
-        self.x_normed = torch.empty(T, d, **f16)
-        self.logits = torch.empty(T, cfg.vocab, dtype=torch.float32, device=dev)
-        self.tokens = torch.zeros(T, dtype=torch.int32, device=dev)
-        self.ws_bytes = int(lib().tf_attention_workspace_bytes(self.ctx.handle, T, hd, nq, nkv, cache.ctx_len))
+        self.h = torch.zeros(Ta, d, **f16)
+        self.normed = torch.empty(Ta, d, **f16)
+        self.q = torch.empty(Ta, nq * hd, **f16)
+        self.attn = torch.empty(Ta, nq * hd, **f16)
+        self.o = torch.empty(Ta, d, **f16)
+        self.dense_x = torch.empty(Ta, d, **f16)
+        self.routed_x = torch.empty(Ta, d, **f16)
+        self.router_x = torch.empty(Ta, d, **f16)
+        self.h1 = torch.empty(Ta, d, **f16)
+        self.h2 = torch.empty(Ta, d, **f16)
+        self.idx = torch.empty(Ta, cfg.top_k, dtype=torch.int32, device=dev)
+        self.wts = torch.empty(Ta, cfg.top_k, dtype=torch.float16, device=dev)
+        self.sact = torch.empty(Ta, cfg.fs, **f16)
+        self.x_normed = torch.empty(Ta, d, **f16)
+        self.logits = torch.empty(Ta, cfg.vocab, dtype=torch.float32, device=dev)
+        self.tokens = torch.zeros(Ta, dtype=torch.int32, device=dev)
+        self.ws_bytes = int(lib().tf_attention_workspace_bytes(self.ctx.handle, Ta, hd, nq, nkv, cache.ctx_len))
         self.attn_ws = torch.empty(max(self.ws_bytes, 16) // 4 + 4, dtype=torch.float32, device=dev)
-        if T > 1:
+        if T > 1 and ep_layers is None:
             from .prefill import DeviceRoutes
             E = cfg.num_experts
             i32 = dict(dtype=torch.int32, device=dev)
-            self.routes = DeviceRoutes(torch.empty(T * cfg.top_k, 4, **i32), torch.empty(E, **i32),
+            self.routes = DeviceRoutes(torch.empty(Ta * cfg.top_k, 4, **i32), torch.empty(E, **i32),
                                        torch.empty(E, **i32), torch.empty(E, 3, **i32), torch.empty(1, **i32),
                                        torch.empty(E, 4, **i32), torch.empty(1, **i32))
-            self.ract = torch.empty(T * cfg.top_k, cfg.f, **f16)
-            self.rpart = torch.empty(T * cfg.top_k, d, **f16)
+            self.ract = torch.empty(Ta * cfg.top_k, cfg.f, **f16)
+            self.rpart = torch.empty(Ta * cfg.top_k, d, **f16)
         self.c_moe = [L.moe.as_c() for L in weights.layers]
         self.launches = 0
 
@@ -302,8 +306,10 @@ class Decoder:
 
     def layer(self, i: int, position: int, stream=None):
         """One decoder layer for the T tokens at `position` (cache slot)."""
-        from .moe import SharedExpertRuntime, moe_decode_layer  # noqa: F401
         cfg, L, T = self.cfg, self.w.layers[i], self.T
+        if T == 0:  # no tokens here: only serve this rank's experts
+            self._moe(i, stream)
+            return
         d, hd, nq, nkv = cfg.d, cfg.head_dim, cfg.num_q_heads, cfg.num_kv_heads
         ctx = self.ctx
         seq_stride = self.cache.ctx_len * nkv * hd
@@ -332,6 +338,20 @@ class Decoder:
         from .moe import SharedExpertRuntime, moe_decode_layer
         from .prefill import PrefillGroupedRoutedMoE, PrefillMoE, PrefillRouter, PrefillSharedExpert, route_sort
         cfg, M, T, ctx = self.cfg, self.w.layers[i].moe, self.T, self.ctx
+        if self.ep is not None:
+            if T:
+                PrefillRouter(ctx).encode_gemma4_block(M.router_w, M.router_s, M.router_b, self.router_x, M.eff_scale,
+                                                       M.per_expert_scale, self.idx, self.wts, T, cfg.num_experts,
+                                                       cfg.d, cfg.top_k, stream=stream)
+            self.ep[i].forward(self.routed_x[:T], self.idx[:T], self.wts[:T], self.h2[:T], stream=stream)
+            if T == 1:
+                SharedExpertRuntime(4, ctx).encode(self.dense_x[0], M.shared_gate, M.shared_up, M.shared_down,
+                                                   self.h1[0], self.sact[0], stream=stream)
+            elif T:
+                PrefillSharedExpert(ctx).encode(self.dense_x, M.shared_gate, M.shared_up, M.shared_down, self.sact,
+                                                self.h1, T, stream=stream)
+            self.launches += 13
+            return
         if T == 1:
             # the reference's shared expert runs on dense_x and the routed
             # experts on routed_x: shared separately, then the fused routed layer
@@ -367,6 +387,8 @@ class Decoder:
         return self._c_routed[i]
 
     def embed(self, token_ids, stream=None):
+        if self.T == 0:
+            return
         cfg = self.cfg
         e = self.w.embed
         EmbedLookupInt4(self.ctx).encode(e.W, e.S, e.B, token_ids, self.h, self.T, cfg.vocab, cfg.d,
@@ -374,6 +396,8 @@ class Decoder:
         self.launches += 1
 
     def lm_head(self, stream=None):
+        if self.T == 0:
+            return
         cfg, e = self.cfg, self.w.embed
         LMHeadChainInt4(self.ctx).encode(self.h, self.w.final_norm, e.W, e.S, e.B, cfg.vocab, cfg.d, self.T,
                                          self.x_normed, self.logits, self.tokens, cfg.eps, stream=stream)

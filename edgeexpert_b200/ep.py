@@ -132,6 +132,56 @@ class CudaOps:
         self.ctx.check(st, "tf_ep_return_reduce")
 
 
+class P2PExchange:
+    """Peer-memory buffers of the fixed-capacity exchange (one set, shared by
+    every layer): this rank's receive rows, return rows and arrival counters,
+    allocated once with tf_ep_ipc_alloc, and device arrays of every rank's
+    buffer pointers (the peers' opened through CUDA IPC).  The data path then
+    needs no collective: the dispatch and combine kernels store into the
+    peers' buffers and signal their counters (tf_ep_*_p2p)."""
+
+    def __init__(self, world: int, rank: int, capacity: int, d: int, group=None, context: Context | None = None,
+                 device=None):
+        self.ctx = context or Context.get(torch.cuda.current_device())
+        self.world, self.rank, self.capacity, self.d = world, rank, capacity, d
+        rows = world * capacity
+        sizes = (rows * row_bytes(d), rows * d * 4, int(lib().tf_ep_flag_bytes(world)))
+        self.own, handles = [], []
+        for nbytes in sizes:
+            ptr_out, h = C.c_void_p(), (C.c_uint8 * 64)()
+            self.ctx.check(lib().tf_ep_ipc_alloc(self.ctx.handle, nbytes, C.byref(ptr_out), h), "tf_ep_ipc_alloc")
+            self.own.append(ptr_out.value)
+            handles.append(bytes(h))
+        self.recv, self.back, self.flags = self.own
+        allh = [None] * world
+        if world > 1:
+            dist.all_gather_object(allh, handles, group=group)
+        else:
+            allh = [handles]
+        self.opened = []
+        tables = []
+        for i in range(3):
+            ptrs = []
+            for r in range(world):
+                if r == rank:
+                    ptrs.append(self.own[i])
+                    continue
+                pp = C.c_void_p()
+                hb = (C.c_uint8 * 64).from_buffer_copy(allh[r][i])
+                self.ctx.check(lib().tf_ep_ipc_open(self.ctx.handle, hb, C.byref(pp)), "tf_ep_ipc_open")
+                self.opened.append(pp.value)
+                ptrs.append(pp.value)
+            tables.append(torch.tensor(ptrs, dtype=torch.int64, device=device))
+        self.peer_recv, self.peer_back, self.peer_flags = tables
+
+    def close(self):
+        for pp in self.opened:
+            lib().tf_ep_ipc_close(self.ctx.handle, C.c_void_p(pp))
+        for pp in self.own:
+            lib().tf_ep_ipc_free(self.ctx.handle, C.c_void_p(pp))
+        self.opened, self.own = [], []
+
+
 @dataclass
 class EPStats:
     rows_per_rank: int  # slots sent to (and received from) every rank
@@ -148,7 +198,9 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, experts_local, num_experts: int, top_k: int, capacity: int, d: int, f: int, group=None,
-                 ops=None, context: Context | None = None, device=None):
+                 ops=None, context: Context | None = None, device=None, p2p: P2PExchange | None = None):
+        """`p2p` (a P2PExchange of the same capacity and d) replaces the two
+        NCCL all-to-alls with peer-memory stores; it may be shared by layers."""
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -168,6 +220,7 @@ class ExpertParallelMoE:
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else "cpu"
         self.buf = ops.alloc(self.world, capacity, top_k, d, f, self.per_rank, device)
+        self.p2p = p2p if self.world > 1 else None
         self.last = EPStats(capacity)
 
     def forward(self, hidden, expert_ids, weights, h2, stream=None):
@@ -175,6 +228,8 @@ class ExpertParallelMoE:
         if T > self.capacity:
             raise ValueError(f"{T} tokens exceed the dispatch capacity {self.capacity}")
         b, rows = self.buf, self.world * self.capacity
+        if self.p2p is not None:
+            return self._forward_p2p(hidden, expert_ids, weights, h2, T, rows, stream)
         self.ops.dispatch_pack(hidden, expert_ids, weights, T, self.K, self.E, self.per_rank, self.world,
                                self.capacity, b.send, stream)
         recv = exchange_equal(b.send, b.recv, self.group)
@@ -182,4 +237,27 @@ class ExpertParallelMoE:
         self.ops.experts(self.pool, b, recv, rows, self.K, stream)
         back = exchange_equal(b.ret, b.back, self.group)
         self.ops.reduce(back, self.world, self.capacity, T, h2, stream)
+        return h2
+
+    def _forward_p2p(self, hidden, expert_ids, weights, h2, T, rows, stream):
+        x, b, ctx = self.p2p, self.buf, self.ops.ctx
+        sp = stream_ptr(stream)
+        d, K = self.d, self.K
+        ctx.check(lib().tf_ep_dispatch_p2p(ctx.handle, ptr(hidden), hidden.stride(0) if T else d, ptr(expert_ids),
+                                           ptr(weights), T, K, self.E, self.per_rank, self.world, self.rank,
+                                           self.capacity, d, ptr(x.peer_recv), ptr(x.peer_flags), C.c_void_p(x.flags),
+                                           sp), "tf_ep_dispatch_p2p")
+        ctx.check(lib().tf_ep_dispatch_unpack_p2p(ctx.handle, C.c_void_p(x.recv), C.c_void_p(x.flags), self.world,
+                                                  self.capacity, d, K, ptr(b.ids), ptr(b.w), sp),
+                  "tf_ep_dispatch_unpack_p2p")
+        from .prefill import PrefillGroupedRoutedMoE, route_sort
+        route_sort(b.ids, b.w, rows, K, self.pool.num_experts, 16, stream=stream, context=ctx, out=b.routes)
+        PrefillGroupedRoutedMoE(ctx).encode(self.pool, b.routes, x.recv, b.act, b.part, rows, K,
+                                            hidden_stride=row_bytes(d) // 2, stream=stream)
+        ctx.check(lib().tf_ep_combine_p2p(ctx.handle, ptr(b.part), ptr(b.ids), ptr(b.w), self.world, self.rank,
+                                          self.capacity, K, d, ptr(x.peer_back), ptr(x.peer_flags),
+                                          C.c_void_p(x.flags), sp), "tf_ep_combine_p2p")
+        ctx.check(lib().tf_ep_return_reduce_p2p(ctx.handle, C.c_void_p(x.back), C.c_void_p(x.flags), self.world,
+                                                self.capacity, T, d, ptr(h2) if T else C.c_void_p(0),
+                                                h2.stride(0) if T else d, sp), "tf_ep_return_reduce_p2p")
         return h2

@@ -409,6 +409,29 @@ TF_API tf_status tf_lm_head_greedy(tf_context* ctx, const void* hidden, uint32_t
                                    uint32_t d, uint32_t T, void* x_normed, void* logits, void* out_tokens,
                                    tf_scale_type st, void* stream);
 
+/* ---- sampling (Sources/TurboFieldfare/Metal/Sampling/logit.metal:42-617;
+ *      LogitSoftcapSoftmax / Sample / SampleTopK64, Kernels/Sampling/LogitOutput.swift) ---- */
+
+/* logit_softcap_softmax: probs[r][i] = half(exp(z' - max z') / sum exp(z' - max z')),
+ * z' = softcap * tanh(z / softcap), for `rows` (<= 256) rows of V logits
+ * (fp32 when logits_fp32, else fp16). */
+TF_API tf_status tf_softcap_softmax(tf_context* ctx, const void* logits, int logits_fp32, void* probs, uint32_t V,
+                                    uint32_t rows, float softcap, void* stream);
+
+/* Sample.encode (logit.metal:183-446) on one row of fp16 probabilities:
+ * temperature <= 0: argmax (ties to the lower index); top_k == 0 and top_p
+ * outside (0, 1): Gumbel-max over log(p)/T with the (seed, position, row)
+ * counter draw; otherwise the top min(top_k or V, 256) by (p desc, index asc),
+ * top-p against the full mass, p^(1/T), then the xorshift64* inverse-CDF draw.
+ * out_token: device uint32.  V <= 262144. */
+TF_API tf_status tf_sample(tf_context* ctx, const void* probs, uint32_t V, float temperature, uint32_t top_k,
+                           float top_p, uint64_t seed, uint32_t position, void* out_token, void* stream);
+
+/* SampleTopK64.encode (sample_topk64_stage1 / _reduce / _final, logit.metal:489-617):
+ * the top 64 by (p desc, index asc), then the same truncating draw.  V <= 262144. */
+TF_API tf_status tf_sample_topk64(tf_context* ctx, const void* probs, uint32_t V, float temperature, float top_p,
+                                  uint64_t seed, void* out_token, void* stream);
+
 /* ---- expert parallelism (routed experts sharded over GPUs) ------------------------------
  * No reference counterpart (the reference streams experts from SSD on one GPU).
  * Experts are sharded in contiguous id ranges of experts_per_rank; the
@@ -457,6 +480,42 @@ TF_API tf_status tf_ep_expert_combine(tf_context* ctx, const void* route_partial
  * h2_stride in elements (0 = d). */
 TF_API tf_status tf_ep_return_reduce(tf_context* ctx, const void* back, uint32_t world, uint32_t capacity,
                                      uint32_t T, uint32_t d, void* h2, uint32_t h2_stride, void* stream);
+
+/* ---- expert-parallel exchange over peer memory (no collective library on the data path) ----
+ * The same fixed-capacity exchange with the two all-to-alls replaced by stores
+ * into the peers' buffers over NVLink (CUDA IPC mappings of ordinary device
+ * allocations; no multicast) and per-(sender, owner) arrival counters.  Each
+ * rank allocates with tf_ep_ipc_alloc: recv (world*capacity rows of 2*d + 64
+ * bytes), back (world*capacity*d floats) and flags (tf_ep_flag_bytes), shares
+ * the 64-byte handles (e.g. an all-gather over the process group) and opens
+ * its peers' with tf_ep_ipc_open.  peer_recv / peer_back / peer_flags are
+ * DEVICE arrays of `world` pointers (entry r = rank r's buffer, this rank's
+ * own at entry rank).  One layer:
+ *   tf_ep_dispatch_p2p -> tf_ep_dispatch_unpack_p2p -> tf_moe_route_sort +
+ *   tf_moe_grouped_routed (hidden = recv) -> tf_ep_combine_p2p -> tf_ep_return_reduce_p2p.
+ * The waits are bounded (about 2 s); a timeout raises TF_ERR_TIMEOUT through
+ * tf_context_check_device.  One process per GPU: every rank must run every
+ * layer's five calls.  Buffers may be shared by consecutive layers. */
+TF_API size_t tf_ep_flag_bytes(uint32_t world);
+TF_API tf_status tf_ep_ipc_alloc(tf_context* ctx, size_t bytes, void** dev_ptr, void* ipc_handle /* 64 B out */);
+TF_API tf_status tf_ep_ipc_open(tf_context* ctx, const void* ipc_handle, void** peer_ptr);
+TF_API tf_status tf_ep_ipc_close(tf_context* ctx, void* peer_ptr);
+TF_API tf_status tf_ep_ipc_free(tf_context* ctx, void* dev_ptr);
+TF_API tf_status tf_ep_dispatch_p2p(tf_context* ctx, const void* hidden, uint32_t hidden_stride, const void* expert_ids,
+                                    const void* weights, uint32_t T, uint32_t top_k, uint32_t num_experts,
+                                    uint32_t experts_per_rank, uint32_t world, uint32_t rank, uint32_t capacity,
+                                    uint32_t d, const void* peer_recv, const void* peer_flags, void* my_flags,
+                                    void* stream);
+TF_API tf_status tf_ep_dispatch_unpack_p2p(tf_context* ctx, const void* recv, const void* my_flags, uint32_t world,
+                                           uint32_t capacity, uint32_t d, uint32_t top_k, void* expert_ids_out,
+                                           void* weights_out, void* stream);
+TF_API tf_status tf_ep_combine_p2p(tf_context* ctx, const void* route_partials, const void* expert_ids,
+                                   const void* weights, uint32_t world, uint32_t rank, uint32_t capacity,
+                                   uint32_t top_k, uint32_t d, const void* peer_back, const void* peer_flags,
+                                   void* my_flags, void* stream);
+TF_API tf_status tf_ep_return_reduce_p2p(tf_context* ctx, const void* back, const void* my_flags, uint32_t world,
+                                         uint32_t capacity, uint32_t T, uint32_t d, void* h2, uint32_t h2_stride,
+                                         void* stream);
 
 #ifdef __cplusplus
 }

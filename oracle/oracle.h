@@ -214,6 +214,13 @@ void orc_embed_int4(const uint8_t *table, const uint16_t *S, const uint16_t *B, 
 uint32_t orc_lm_head_greedy(const uint8_t *W, const uint16_t *S, const uint16_t *B, int st, const uint16_t *x_f16,
                             int vocab, int d, float *logits, int nthreads);
 
+/* ---- sampling (Metal/Sampling/logit.metal:42-617) ---------------------------- */
+void orc_softcap_softmax(const float *logits, uint16_t *probs, int V, float softcap);
+float orc_gumbel(uint64_t seed, uint32_t position, uint32_t row);
+uint32_t orc_sample(const uint16_t *probs, int V, float temperature, uint32_t top_k, float top_p, uint64_t seed,
+                    uint32_t position);
+uint32_t orc_sample_topk64(const uint16_t *probs, int V, float temperature, float top_p, uint64_t seed);
+
 #ifdef __cplusplus
 }
 #endif

@@ -111,6 +111,10 @@ def lib():
                 "orc_layer_tail": ([u16p, u16p, u16p, VP, u16p, u16p, C.c_float, I, I, C.c_float], None),
                 "orc_embed_int4": ([u8p, u16p, u16p, I, u32p, I, I, C.c_float, u16p], None),
                 "orc_lm_head_greedy": ([u8p, u16p, u16p, I, u16p, I, I, VP, I], C.c_uint32),
+                "orc_softcap_softmax": ([f32p, u16p, I, C.c_float], None),
+                "orc_gumbel": ([C.c_uint64, C.c_uint32, C.c_uint32], C.c_float),
+                "orc_sample": ([u16p, I, C.c_float, C.c_uint32, C.c_float, C.c_uint64, C.c_uint32], C.c_uint32),
+                "orc_sample_topk64": ([u16p, I, C.c_float, C.c_float, C.c_uint64], C.c_uint32),
             }
             for name, (args, res) in sig.items():
                 fn = getattr(L, name)
@@ -437,3 +441,21 @@ def lm_head_greedy(W, S, B, x_f16, vocab, d, scale_type=0, nthreads=0, want_logi
                                    scale_type, np.ascontiguousarray(x_f16, np.uint16), vocab, d, _vp(logits),
                                    _nt(nthreads))
     return (int(tok), logits) if want_logits else int(tok)
+
+
+# ------------------------------------------------------------- sampling ----
+def softcap_softmax(logits_f32, softcap: float = 30.0) -> np.ndarray:
+    lg = np.ascontiguousarray(logits_f32, np.float32).reshape(-1)
+    out = np.empty(lg.size, np.uint16)
+    lib().orc_softcap_softmax(lg, out, lg.size, softcap)
+    return out
+
+
+def sample(probs_f16, temperature: float, top_k: int = 0, top_p: float = 1.0, seed: int = 0, position: int = 0):
+    p = np.ascontiguousarray(probs_f16, np.uint16).reshape(-1)
+    return int(lib().orc_sample(p, p.size, temperature, top_k, top_p, seed & 0xFFFFFFFFFFFFFFFF, position))
+
+
+def sample_topk64(probs_f16, temperature: float, top_p: float = 1.0, seed: int = 0):
+    p = np.ascontiguousarray(probs_f16, np.uint16).reshape(-1)
+    return int(lib().orc_sample_topk64(p, p.size, temperature, top_p, seed & 0xFFFFFFFFFFFFFFFF))

@@ -227,3 +227,165 @@ uint32_t orc_lm_head_greedy(const uint8_t *W, const uint16_t *S, const uint16_t 
     if (!logits) free(y);
     return bi == 0xFFFFFFFFu ? 0u : bi;
 }
+
+/* ---- sampling (Sources/TurboFieldfare/Metal/Sampling/logit.metal:42-617) ---- */
+
+/* logit_softcap_softmax (logit.metal:52-146): z' = softcap * tanh(z / softcap),
+ * p = half(exp(z' - max z') / sum exp(z' - max z')).  Two passes in double for
+ * the reference value. */
+void orc_softcap_softmax(const float *logits, uint16_t *probs, int V, float softcap) {
+    double m = -INFINITY;
+    double *z = (double *)malloc(sizeof(double) * (size_t)V);
+    for (int i = 0; i < V; ++i) {
+        z[i] = (double)softcap * tanh((double)logits[i] / (double)softcap);
+        if (z[i] > m) m = z[i];
+    }
+    double d = 0.0;
+    for (int i = 0; i < V; ++i) d += exp(z[i] - m);
+    for (int i = 0; i < V; ++i) probs[i] = f2h((float)(exp(z[i] - m) / d));
+    free(z);
+}
+
+/* xorshift64* and uniform01 (logit.metal:148-160). */
+static uint64_t xorshift64(uint64_t *s) {
+    *s ^= *s << 13;
+    *s ^= *s >> 7;
+    *s ^= *s << 17;
+    return *s * 2685821657736338717ULL;
+}
+static float uniform01(uint64_t *s) {
+    const uint32_t bits = (uint32_t)(xorshift64(s) >> 40);
+    return (float)bits * (1.0f / 16777216.0f);
+}
+/* lmhead_splitmix64 / lmhead_gumbel_for (logit.metal:164-181). */
+static uint64_t splitmix64_mix(uint64_t x) {
+    x = x + 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+float orc_gumbel(uint64_t seed, uint32_t position, uint32_t row) {
+    const uint64_t key = seed ^ ((uint64_t)position * 0xD2B74407B1CE6E93ull) ^ (uint64_t)row;
+    const uint32_t bits = (uint32_t)(splitmix64_mix(key) >> 40);
+    const float u = ((float)bits + 0.5f) * (1.0f / 16777216.0f);
+    return -logf(-logf(u));
+}
+
+/* The truncating tail shared by `sample` (logit.metal:391-443) and
+ * sample_topk64_final (:575-616): the candidates sorted by (p desc, index
+ * asc); keep the finite ones, top-p against the full-vocabulary mass,
+ * temperature p^(1/T), one xorshift step, then the inverse-CDF draw. */
+static uint32_t truncated_draw(float *val, const uint32_t *idx, int count, int V, float temperature, float top_p,
+                               uint64_t seed) {
+    int kept = 0;
+    while (kept < count && idx[kept] < (uint32_t)V && isfinite(val[kept])) kept++;
+    if (top_p > 0.0f && top_p < 1.0f) {
+        float cum = 0.0f;
+        int cut = kept;
+        for (int i = 0; i < kept; ++i) {
+            cum += val[i];
+            if (cum >= top_p) {
+                cut = i + 1;
+                break;
+            }
+        }
+        kept = cut;
+    }
+    const float inv_t = 1.0f / temperature;
+    for (int i = 0; i < kept; ++i)
+        if (temperature != 1.0f) val[i] = powf(val[i], inv_t);
+    float surviving = 0.0f;
+    for (int i = 0; i < kept; ++i) surviving += val[i];
+    uint64_t rng = seed;
+    (void)xorshift64(&rng);
+    const float u = uniform01(&rng) * surviving;
+    float run = 0.0f;
+    uint32_t picked = idx[0];
+    for (int i = 0; i < kept; ++i) {
+        run += val[i];
+        if (u <= run) {
+            picked = idx[i];
+            break;
+        }
+    }
+    return picked;
+}
+
+static int cand_cmp(const void *a, const void *b) {
+    const float va = ((const float *)a)[0], vb = ((const float *)b)[0];
+    const uint32_t ia = ((const uint32_t *)a)[1], ib = ((const uint32_t *)b)[1];
+    if (va > vb) return -1;
+    if (va < vb) return 1;
+    return ia < ib ? -1 : (ia > ib);
+}
+
+/* sample (logit.metal:183-446): temperature <= 0 greedy argmax (ties to the
+ * lower index); top_k == 0 and no top-p: Gumbel-max over inv_t * log p;
+ * otherwise the top min(top_k or V, 256) candidates and truncated_draw. */
+uint32_t orc_sample(const uint16_t *probs, int V, float temperature, uint32_t top_k, float top_p, uint64_t seed,
+                    uint32_t position) {
+    if (temperature <= 0.0f) {
+        float best = -INFINITY;
+        uint32_t bi = 0;
+        for (int i = 0; i < V; ++i) {
+            const float p = h2f(probs[i]);
+            if (p > best) {
+                best = p;
+                bi = (uint32_t)i;
+            }
+        }
+        return bi;
+    }
+    if (top_k == 0 && (top_p <= 0.0f || top_p >= 1.0f)) {
+        const float inv_t = 1.0f / temperature;
+        float best = -INFINITY;
+        uint32_t bi = 0xFFFFFFFFu;
+        for (int i = 0; i < V; ++i) {
+            const float p = h2f(probs[i]);
+            if (!(p > 0.0f)) continue;
+            const float s = inv_t * logf(p) + orc_gumbel(seed, position, (uint32_t)i);
+            if (s > best) {
+                best = s;
+                bi = (uint32_t)i;
+            }
+        }
+        return bi == 0xFFFFFFFFu ? 0u : bi;
+    }
+    int k = top_k == 0 ? V : (int)top_k;
+    if (k > 256) k = 256;
+    if (k > V) k = V;
+    float *c = (float *)malloc(sizeof(float) * 2 * (size_t)V);
+    for (int i = 0; i < V; ++i) {
+        c[2 * i] = h2f(probs[i]);
+        ((uint32_t *)c)[2 * i + 1] = (uint32_t)i;
+    }
+    qsort(c, (size_t)V, 2 * sizeof(float), cand_cmp);
+    float val[256];
+    uint32_t idx[256];
+    for (int i = 0; i < k; ++i) {
+        val[i] = c[2 * i];
+        idx[i] = ((uint32_t *)c)[2 * i + 1];
+    }
+    free(c);
+    return truncated_draw(val, idx, k, V, temperature, top_p, seed);
+}
+
+/* SampleTopK64 (sample_topk64_stage1/_reduce/_final, logit.metal:489-617):
+ * the top 64 by (p desc, index asc), then truncated_draw. */
+uint32_t orc_sample_topk64(const uint16_t *probs, int V, float temperature, float top_p, uint64_t seed) {
+    float *c = (float *)malloc(sizeof(float) * 2 * (size_t)V);
+    for (int i = 0; i < V; ++i) {
+        c[2 * i] = h2f(probs[i]);
+        ((uint32_t *)c)[2 * i + 1] = (uint32_t)i;
+    }
+    qsort(c, (size_t)V, 2 * sizeof(float), cand_cmp);
+    const int k = V < 64 ? V : 64;
+    float val[64];
+    uint32_t idx[64];
+    for (int i = 0; i < k; ++i) {
+        val[i] = c[2 * i];
+        idx[i] = ((uint32_t *)c)[2 * i + 1];
+    }
+    free(c);
+    return truncated_draw(val, idx, k, V, temperature, top_p, seed);
+}

@@ -7,7 +7,8 @@ prefill.metal:575-596) within RelError 2e-3 (the fp32 sum is regrouped by
 owner rank, so agreement is to fp32 rounding, not bitwise).
 
 * world 1: the fixed-capacity dispatch kernels with an identity exchange (any box);
-* world 2: two GPUs over NCCL (skips with fewer than 2 GPUs), including a
+* world 2: two GPUs (skips with fewer than 2 GPUs), with the NCCL
+  all-to-alls and with the peer-memory exchange (tf_ep_*_p2p), including a
   rank whose tokens all route to its own experts and uneven token counts.
 """
 import os
@@ -63,15 +64,16 @@ def oracle_h2(host, lay, X, idx, w):
     return O.reduce_token_major(part, w.view(np.uint16), T, K, D)
 
 
-def run_rank(rank, world, T, capacity, own_only, dev):
-    from edgeexpert_b200.ep import ExpertParallelMoE
+def run_rank(rank, world, T, capacity, own_only, dev, p2p=False):
+    from edgeexpert_b200.ep import ExpertParallelMoE, P2PExchange
     from edgeexpert_b200.moe import ExpertPool
     host, lay = host_experts()
     per = E // world
     local = ExpertPool(torch.from_numpy(host[rank * per:(rank + 1) * per].reshape(-1).copy()).to(dev), lay.stride, per,
                        lay.offsets, D, F, torch.bfloat16)
     X, idx, w = tokens_for(rank, T, own_only, world)
-    ep = ExpertParallelMoE(local, E, K, capacity, D, F, device=dev)
+    x = P2PExchange(world, rank, capacity, D, device=dev) if p2p else None
+    ep = ExpertParallelMoE(local, E, K, capacity, D, F, device=dev, p2p=x)
     h2 = torch.empty(T, D, dtype=torch.float16, device=dev)
     args = (torch.from_numpy(X.view(np.float16)).to(dev), torch.from_numpy(idx).to(dev), torch.from_numpy(w).to(dev))
     ep.forward(*args, h2)
@@ -80,6 +82,10 @@ def run_rank(rank, world, T, capacity, own_only, dev):
     torch.cuda.synchronize()
     got = O.f16_to_f32(h2.cpu().numpy().view(np.uint16))
     ref = O.f16_to_f32(oracle_h2(host, lay, X, idx, w).reshape(T, D))
+    if x is not None:
+        if world > 1:
+            dist.barrier()  # no peer still writes into this rank's buffers
+        x.close()
     return O.rel_error(got, ref), bool(torch.equal(h2, h2b))
 
 
@@ -93,13 +99,13 @@ def test_expert_parallel_world1_matches_oracle(cuda):
     assert device_flags() == 0, f"flags raised by the EP layer (before it: {before:#x})"
 
 
-def device_flags() -> int:
+def device_flags(device: int = 0) -> int:
     """The context's device error flags, read and cleared without raising."""
     import ctypes as C
 
     from edgeexpert_b200._lib import Context, lib
     flags = C.c_uint32(0)
-    lib().tf_context_check_device(Context.get(0).handle, C.c_void_p(0), C.byref(flags))
+    lib().tf_context_check_device(Context.get(device).handle, C.c_void_p(0), C.byref(flags))
     return flags.value
 
 
@@ -116,7 +122,9 @@ def _worker(rank, world, port, results):
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
     try:
         T = [40, 23][rank]
-        results[rank] = run_rank(rank, world, T, 40, own_only=(rank == 1), dev=dev)
+        results[(rank, "nccl")] = run_rank(rank, world, T, 40, own_only=(rank == 1), dev=dev)
+        results[(rank, "p2p")] = run_rank(rank, world, T, 40, own_only=(rank == 1), dev=dev, p2p=True)
+        results[(rank, "flags")] = device_flags(rank)
     finally:
         dist.destroy_process_group()
 
@@ -129,6 +137,8 @@ def test_expert_parallel_two_gpus_matches_oracle(cuda):
     results = mgr.dict()
     mp.spawn(_worker, args=(world, _free_port(), results), nprocs=world, join=True)
     for r in range(world):
-        err, det = results[r]
-        assert err < FP16_TOL, f"rank {r}: rel error {err}"
-        assert det, f"rank {r}: not deterministic"
+        for mode in ("nccl", "p2p"):
+            err, det = results[(r, mode)]
+            assert err < FP16_TOL, f"rank {r} {mode}: rel error {err}"
+            assert det, f"rank {r} {mode}: not deterministic"
+        assert results[(r, "flags")] == 0

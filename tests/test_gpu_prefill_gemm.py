@@ -166,13 +166,14 @@ def skewed_routing(T, K, E, seed):
     return idx, w
 
 
-@pytest.mark.parametrize("path", ["gemm", "gemv"])
+@pytest.mark.parametrize("path", ["gemm", "gemv", "engine"])
 @pytest.mark.parametrize("T,K,E,D,F,st", [(37, 4, 16, 128, 64, 0), (300, 2, 2, 128, 64, 0), (64, 8, 16, 2816, 704, 0),
-                                          (9, 8, 32, 256, 128, 1), (64, 8, 128, 2816, 704, 0)])
+                                          (9, 8, 32, 256, 128, 1), (64, 8, 128, 2816, 704, 0),
+                                          (256, 8, 128, 2816, 704, 0), (40, 2, 2, 2816, 704, 1)])
 def test_grouped_routed_and_reduce(cuda, T, K, E, D, F, st, path, monkeypatch):
-    """Both device paths: tcgen05 GEMMs (many tokens per expert) and the
-    streaming engine (few tokens per expert, batched decode; config 2 is
-    T = 64, K = 8 over 128 experts)."""
+    """Every device path: tcgen05 GEMMs (many tokens per expert), the grouped
+    ring-streamed kernel (few tokens per expert, batched decode; config 2 is
+    T = 64, K = 8 over 128 experts) and the older streaming-engine policy."""
     monkeypatch.setenv("TFCUDA_GROUPED", path)
     ex = Experts(E, D, F, st, f"g-{E}-{D}-{F}-{st}")
     idx, w = skewed_routing(T, K, E, T + E)
@@ -194,7 +195,7 @@ def test_grouped_routed_and_reduce(cuda, T, K, E, D, F, st, path, monkeypatch):
     assert np.array_equal(f16(h2).reshape(-1), h2_ref)
 
 
-@pytest.mark.parametrize("path", ["gemm", "gemv"])
+@pytest.mark.parametrize("path", ["gemm", "gemv", "engine"])
 def test_grouped_routed_empty_routes(cuda, path, monkeypatch):
     """A route table with no groups runs no tile; T = 0 touches nothing."""
     monkeypatch.setenv("TFCUDA_GROUPED", path)
