@@ -4,18 +4,18 @@
 // 336-440,598-670, encoded by PrefillGroupedRoutedMoE.encodeStreamedBatched,
 // Kernels/Prefill/MoE/PrefillGroupedRoutedMoE.swift:446-527).
 //
-// MODE 0 (gate/up): a job is (expert group, pass of <= TP tokens, tile of 128
+// MODE 0 (gate/up): a job is (expert group, pass of <= TP tokens, tile of 120
 // features).  Warp w owns features 8w..8w+7 of the tile: the MMA's A rows
 // 0-7 are their gate rows and rows 8-15 their up rows, so a lane ends with
 // gate and up of the same feature and token and forms act = half(gelu(g) * u)
 // in registers: acts[pair][f] in sorted-pair order.
-// MODE 1 (down): a job is (group, pass, 256 rows of down); warp w owns rows
+// MODE 1 (down): a job is (group, pass, 240 rows of down); warp w owns rows
 // 16w..16w+15 and writes route_partials[(token * top_k + rank)][row] =
 // half(sum) from registers.
 //
 // Data movement: one loader thread puts the weight stages (3-D TMA, 128-byte
-// swizzle, 4 groups x 256 rows = 32 KB per stage) into a ring and prefetches
-// each tile's scale/bias rows into L2; the 16 consumer warps read their
+// swizzle, 4 groups x 240 rows = 30 KB per stage) into a ring and prefetches
+// each tile's scale/bias rows into L2; the 15 consumer warps read their
 // scales from L2 into registers one stage ahead.  A CTA works through a
 // contiguous range of jobs (tile innermost), so the pass's token rows are
 // staged into shared memory once per (group, pass).
@@ -33,17 +33,22 @@ using namespace tf;
 
 namespace {
 
-constexpr int kGsBox = 128 * 128;               // one TMA box: 128 rows x 128 B (4 groups)
-constexpr int kGsStage = 2 * kGsBox;            // 4 groups x 256 rows
-constexpr int kGsMaxR = 6;
-constexpr int kGsConsumers = 16;
+// 15 consumer warps + the loader warp = 16 warps: 4 per sub-partition, so a
+// thread may hold 128 registers
+constexpr int kGsConsumers = 15;
+constexpr int kGsRowsW0 = 8;                        // MODE 0: features per warp (8 gate + 8 up rows)
+constexpr int kGsTile0 = kGsConsumers * kGsRowsW0;  // 120 features
+constexpr int kGsTile1 = kGsConsumers * 16;         // MODE 1: 240 rows
+constexpr int kGsBox = kGsTile0 * 128;              // one TMA box: 120 rows x 128 B (4 groups)
+constexpr int kGsStage = 2 * kGsBox;                // 4 groups x 240 rows (30 KB, a multiple of 1 KB)
+constexpr int kGsMaxR = 7;
 constexpr int kGsThreads = 32 * (1 + kGsConsumers);
 constexpr int kGsMaxGroups = 256;
 constexpr size_t kGsSmemLimit = 232448;
 constexpr uint32_t kGsSpin = 1u << 21;
 
 struct GsParams {
-    CUtensorMap map0;  // MODE 0: gate codes [E][F][D/2]; MODE 1: down codes [E][D][F/2]; box 128 B x 128 rows
+    CUtensorMap map0;  // MODE 0: gate codes [E][F][D/2], box 128 B x 120 rows; MODE 1: down [E][D][F/2], 128 x 240
     CUtensorMap map1;  // MODE 0: up codes
     const uint8_t* pool;
     unsigned long long stride;
@@ -68,16 +73,17 @@ struct GsBars {
 };
 
 struct GsLayout {
-    uint32_t xs, xsum, xcorr, bars, total;
+    uint32_t xs, xc, bars, total;
 };
 
+// [ring: R stages][token rows: TP x x_words_stride(K) words][per group and
+// token {1024 * sum(staged x), sum(x)}: K/64 x TP float2][barriers]
 __host__ __device__ inline GsLayout gs_layout(int K, int R, int TP) {
     const int ngK = K / 64;
     GsLayout L;
     L.xs = (uint32_t)R * kGsStage;
-    L.xsum = L.xs + (uint32_t)TP * x_words_stride(K) * 4;
-    L.xcorr = L.xsum + (uint32_t)TP * ngK * 4;
-    L.bars = L.xcorr + (uint32_t)TP * ngK * 4;
+    L.xc = L.xs + (uint32_t)TP * x_words_stride(K) * 4;
+    L.bars = L.xc + (uint32_t)TP * ngK * 8;
     L.total = ((L.bars + (uint32_t)sizeof(GsBars) + 15) & ~15u) + 1024;
     return L;
 }
@@ -205,6 +211,24 @@ __device__ __forceinline__ void stage_words_gather(const GsParams& p, uint32_t* 
     }
 }
 
+// Per (group, token) {1024 * sum of the staged values, true sum}: one warp per
+// (token, group); odd pairs hold x/16, so the true sum is s + 15 * odd.
+__device__ __forceinline__ void stage_xc(const uint32_t* xs, int ws, int ntok, int ngK, int TP, float2* xc, int ctid) {
+    const int warp = ctid >> 5, lane = ctid & 31;
+    for (int i = warp; i < ntok * ngK; i += kGsConsumers) {
+        const int tk = i / ngK, G = i - tk * ngK;
+        const uint32_t w = xs[tk * ws + G * 32 + lane];
+        const __half2 h = *reinterpret_cast<const __half2*>(&w);
+        float s = __low2float(h) + __high2float(h);
+        float odd = (lane & 1) ? s : 0.f;
+        for (int off = 16; off; off >>= 1) {
+            s += __shfl_xor_sync(0xffffffffu, s, off);
+            odd += __shfl_xor_sync(0xffffffffu, odd, off);
+        }
+        if (lane == 0) xc[G * TP + tk] = make_float2(1024.f * s, s + 15.f * odd);
+    }
+}
+
 template <typename ST>
 __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __grid_constant__ GsParams p) {
     extern __shared__ uint8_t gs_raw[];
@@ -212,14 +236,13 @@ __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __g
     const GsLayout L = gs_layout(p.K, p.R, p.TP);
     uint8_t* ring = sm;
     uint32_t* xs = reinterpret_cast<uint32_t*>(sm + L.xs);
-    float* xsum = reinterpret_cast<float*>(sm + L.xsum);
-    float* xcorr = reinterpret_cast<float*>(sm + L.xcorr);
+    float2* xc = reinterpret_cast<float2*>(sm + L.xc);
     GsBars& sh = *reinterpret_cast<GsBars*>(sm + L.bars);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int ngK = p.K >> 6, nst = (ngK + 3) >> 2, R = p.R, TP = p.TP;
     const int ws = x_words_stride(p.K);
     const int rows_out = p.mode == 0 ? p.F : p.D;  // output rows per expert
-    const int tile_rows = p.mode == 0 ? 128 : 256;
+    const int tile_rows = p.mode == 0 ? kGsTile0 : kGsTile1;
 
     griddep_wait();  // the groups / acts come from the previous launch
     const int ng = min((int)__ldg(p.n_groups), kGsMaxGroups);
@@ -285,15 +308,14 @@ __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __g
                         tma_load_3d(dst, &p.map0, st * 128, r0, (int)gr.expert, &sh.full[slot]);
                         tma_load_3d(dst + kGsBox, &p.map1, st * 128, r0, (int)gr.expert, &sh.full[slot]);
                     } else {
-                        tma_load_3d(dst, &p.map0, st * 128, r0, (int)gr.expert, &sh.full[slot]);
-                        tma_load_3d(dst + kGsBox, &p.map0, st * 128, r0 + 128, (int)gr.expert, &sh.full[slot]);
+                        tma_load_3d(dst, &p.map0, st * 128, r0, (int)gr.expert, &sh.full[slot]);  // 240 rows
                     }
                 }
                 if (!ok) break;
             }
         }
     } else {
-        // ---------------- 16 consumer warps ----------------
+        // ---------------- 15 consumer warps ----------------
         const int w = warp - 1;
         const int g = lane >> 2, t = lane & 3;
         const int ctid = tid - 32;
@@ -314,7 +336,7 @@ __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __g
                 if (ctid == 0) sh.stop = *reinterpret_cast<volatile int*>(&sh.abort_flag);
                 stage_words_gather(p, xs, ws, p0, ntok, nblk * 8, ctid);
                 consumer_bar();
-                stage_xsum_smem(xs, ws, nblk * 8, p.K, xsum, xcorr, true, ctid, kGsConsumers * 32);
+                stage_xc(xs, ws, nblk * 8, ngK, TP, xc, ctid);
                 consumer_bar();
                 staged_group = J.group;
                 staged_pass = J.pass;
@@ -367,8 +389,8 @@ __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __g
                                 mma16816(cb, pa0[2], pb0[2], pa0[3], pb0[3], x0.z, x0.w);
                                 mma16816(c, pa1[0], pb1[0], pa1[1], pb1[1], x1.x, x1.y);
                                 mma16816(cb, pa1[2], pb1[2], pa1[3], pb1[3], x1.z, x1.w);
-                                const int c0 = (b * 8 + 2 * t) * ngK + G, c1 = c0 + ngK;
-                                const float xc0 = xcorr[c0], xc1 = xcorr[c1], xs0 = xsum[c0], xs1 = xsum[c1];
+                                const float4 xv = *reinterpret_cast<const float4*>(xc + G * TP + b * 8 + 2 * t);
+                                const float xc0 = xv.x, xs0 = xv.y, xc1 = xv.z, xs1 = xv.w;
                                 const float sa = scale_at<ST>(scl[0], j), ba = scale_at<ST>(scl[1], j);
                                 const float sb = scale_at<ST>(scl[2], j), bb = scale_at<ST>(scl[3], j);
                                 acc[b][0] = fmaf(sa, (c[0] + cb[0]) - xc0, fmaf(ba, xs0, acc[b][0]));
@@ -411,7 +433,7 @@ __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __g
 }
 
 bool gs_map(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows, uint64_t depth,
-            uint64_t depth_stride) {
+            uint64_t depth_stride, uint32_t box_rows) {
     memset(m, 0, sizeof(*m));
     EncodeTiledFn fn = encode_tiled_fn();
     if (!fn || (reinterpret_cast<uintptr_t>(base) & 15u) || row_bytes % 16 || rows == 0 || depth == 0) return false;
@@ -419,7 +441,7 @@ bool gs_map(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows,
     if (ds % 16 || ds >= (1ull << 40)) return false;
     cuuint64_t dims[3] = {row_bytes, rows, depth};
     cuuint64_t strides[2] = {row_bytes, ds};
-    cuuint32_t box[3] = {128, 128, 1};
+    cuuint32_t box[3] = {128, box_rows, 1};
     cuuint32_t es[3] = {1, 1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -485,7 +507,7 @@ tf_status grouped_stream(tf_context* ctx, const uint8_t* pool, uint64_t stride, 
     p.top_k = (int)top_k;
     p.T = (int)T;
     p.err = ctx->d_err;
-    // phase 1: gate/up over K = d, 128 features per job
+    // phase 1: gate/up over K = d, 120 features per job
     p.mode = 0;
     p.K = (int)d;
     p.x = hidden;
@@ -494,13 +516,13 @@ tf_status grouped_stream(tf_context* ctx, const uint8_t* pool, uint64_t stride, 
     p.ob0 = off->gate_b;
     p.os1 = off->up_s;
     p.ob1 = off->up_b;
-    p.ntile = (int)((f + 127) / 128);
-    if (!gs_map(&p.map0, pool + off->gate_w, d / 2, f, num_experts, stride) ||
-        !gs_map(&p.map1, pool + off->up_w, d / 2, f, num_experts, stride))
+    p.ntile = (int)((f + kGsTile0 - 1) / kGsTile0);
+    if (!gs_map(&p.map0, pool + off->gate_w, d / 2, f, num_experts, stride, kGsTile0) ||
+        !gs_map(&p.map1, pool + off->up_w, d / 2, f, num_experts, stride, kGsTile0))
         return TF_ERR_UNSUPPORTED_SHAPE;
     tf_status rc = st == TF_SCALE_BF16 ? launch_gs<__nv_bfloat16>(ctx, p, s, name) : launch_gs<__half>(ctx, p, s, name);
     if (rc != TF_OK) return rc;
-    // phase 2: down over K = f on the acts, 256 rows per job
+    // phase 2: down over K = f on the acts, 240 rows per job
     p.mode = 1;
     p.K = (int)f;
     p.x = acts;
@@ -508,8 +530,8 @@ tf_status grouped_stream(tf_context* ctx, const uint8_t* pool, uint64_t stride, 
     p.os0 = off->down_s;
     p.ob0 = off->down_b;
     p.os1 = p.ob1 = 0;
-    p.ntile = (int)((d + 255) / 256);
-    if (!gs_map(&p.map0, pool + off->down_w, f / 2, d, num_experts, stride)) return TF_ERR_UNSUPPORTED_SHAPE;
+    p.ntile = (int)((d + kGsTile1 - 1) / kGsTile1);
+    if (!gs_map(&p.map0, pool + off->down_w, f / 2, d, num_experts, stride, kGsTile1)) return TF_ERR_UNSUPPORTED_SHAPE;
     memset(&p.map1, 0, sizeof(p.map1));
     return st == TF_SCALE_BF16 ? launch_gs<__nv_bfloat16>(ctx, p, s, name) : launch_gs<__half>(ctx, p, s, name);
 }

@@ -928,7 +928,7 @@ tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64_t expe
     // hit expert's weights once with up to 8 tokens per MMA column block; many
     // (prefill): the tcgen05 GEMMs.  TFCUDA_GROUPED=gemv|gemm forces one.
     const char* env = getenv("TFCUDA_GROUPED");
-    bool gemv = (uint64_t)P <= 12ull * num_experts;
+    bool gemv = (uint64_t)P <= 24ull * num_experts;  // measured crossover with the tcgen05 GEMMs
     bool engine = false;
     if (env && env[0] == 'g' && env[1] == 'e' && env[2] == 'm') gemv = env[3] == 'v';
     if (env && env[0] == 'e' && env[1] == 'n') gemv = engine = true;
