@@ -107,6 +107,10 @@ _PROTOS = {
                        _U32, _I, _P], _I),
     "tf_moe_phase2": ([_P, _P, _U64, _U32, _P, C.POINTER(_P), C.POINTER(ExpertOffsets), _P, _P, _P, _P, _U32,
                        _U32, _U32, _I, _P], _I),
+    "tf_moe_phase1_bits": ([_P, _U32, _P, _U64, _U32, _P, C.POINTER(_P), C.POINTER(ExpertOffsets), _P, _P, _U32,
+                            _U32, _U32, _I, _P], _I),
+    "tf_moe_phase2_bits": ([_P, _U32, _P, _U64, _U32, _P, C.POINTER(_P), C.POINTER(ExpertOffsets), _P, _P, _P, _P,
+                            _U32, _U32, _U32, _I, _P], _I),
     "tf_shared_expert": ([_P, _P, C.POINTER(AffineMatrix), C.POINTER(AffineMatrix), C.POINTER(AffineMatrix),
                           _P, _P, _I, _P], _I),
     "tf_moe_decode_layer": ([_P, C.POINTER(MoELayer), _P, _P, _P, _P, _P, _P, _P], _I),

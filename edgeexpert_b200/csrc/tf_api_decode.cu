@@ -6,6 +6,7 @@
 #include "tf_context.cuh"
 #include "tf_fused.cuh"
 #include "tf_gemv_tc.cuh"
+#include "tf_lowbit.cuh"
 
 using namespace tf;
 
@@ -89,13 +90,17 @@ tf_status gemv_common(tf_context* ctx, uint32_t bits, const void* W, const void*
     tf_status s = check_ctx(ctx);
     if (s) return s;
     if (!W || !S || !B || !x || !y) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
-    if (bits != 4 && bits != 8) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: bits must be 4 or 8", name);
+    if (bits != 2 && bits != 3 && bits != 4 && bits != 8)
+        return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: bits must be 2, 3, 4 or 8", name);
     if (st != TF_SCALE_BF16 && st != TF_SCALE_F16) return fail(ctx, TF_ERR_INVALID_ARG, "%s: unknown scale type", name);
     if (m == 0 || n == 0 || batch == 0 || ntok == 0) return fail(ctx, TF_ERR_INVALID_ARG, "%s: zero dimension", name);
     if (n % 64) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: N must be a multiple of 64, got %u", name, n);
     if (ntok > 8) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: at most 8 tokens per call, got %u", name, ntok);
     if (!aligned2(W) || !aligned2(S) || !aligned2(B) || !aligned2(x) || !aligned2(y))
         return fail(ctx, TF_ERR_MISALIGNED, "%s: buffers must be 2-byte aligned", name);
+    if (bits == 2 || bits == 3)  // tf_lowbit.cu
+        return lowbit_gemv(ctx, bits, W, S, B, wbs, sbs, batch, x, ntok, xrs, y, nullptr, yrs, ybs, m, n, st,
+                           static_cast<cudaStream_t>(stream), name);
     // One token of int4 over at least one 128-row tile per SM: the ring-streamed
     // integer GEMV (tf_gemv_tc.cu).  TFCUDA_GEMV (read per call): "engine"
     // keeps the streaming engine, "stream" / "tc" force the integer / the
@@ -205,6 +210,7 @@ tf_status tf_context_create(int device, tf_context** out) {
     cudaError_t e = cudaSuccess;
     e = e ? e : cudaMalloc(&ctx->d_err, 4 * sizeof(uint32_t));
     e = e ? e : cudaMalloc(&ctx->d_logits, sizeof(float) * kMaxRouterExperts * 64);
+    e = e ? e : cudaMalloc(&ctx->d_rt_logits, sizeof(float) * kRtLogitsCap);
     e = e ? e : cudaMalloc(&ctx->d_ticket, sizeof(unsigned int) * 64);
     e = e ? e : cudaMalloc(&ctx->d_flags, sizeof(unsigned int) * 32 * 1024);
     e = e ? e : cudaMalloc(&ctx->d_idx, sizeof(uint32_t) * kMaxTopKDecode);
@@ -236,6 +242,7 @@ void tf_context_destroy(tf_context* ctx) {
     cudaSetDevice(ctx->device);
     cudaFree(ctx->d_err);
     cudaFree(ctx->d_logits);
+    cudaFree(ctx->d_rt_logits);
     cudaFree(ctx->d_ticket);
     cudaFree(ctx->d_flags);
     cudaFree(ctx->d_idx);

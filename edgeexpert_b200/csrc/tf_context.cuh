@@ -19,6 +19,7 @@ struct tf_context {
     // Device workspace (allocated once at create time).
     uint32_t* d_err = nullptr;         // error bits raised by kernels
     float* d_logits = nullptr;         // [kMaxRouterExperts] router logits
+    float* d_rt_logits = nullptr;      // [kRtLogitsCap] batched-router logits scratch
     unsigned int* d_ticket = nullptr;  // router selection ticket (always left 0), barrier count
     unsigned int* d_flags = nullptr;   // fused-layer barrier release flags, 128 B apart
     uint32_t* d_idx = nullptr;         // [8] decode routing ids
@@ -43,6 +44,7 @@ constexpr int kMaxF = 4096;
 constexpr int kMaxFs = 16384;
 constexpr int kMaxTopKDecode = 8;
 constexpr int kMaxLmTokens = 256;
+constexpr size_t kRtLogitsCap = 1u << 20;  // floats: 4096 tokens x 256 experts
 constexpr int kCandCap = 65536;  // 256 tiles x 256 candidates: a 262144-entry vocabulary
 
 inline tf_status fail(tf_context* ctx, tf_status s, const char* fmt, ...) {

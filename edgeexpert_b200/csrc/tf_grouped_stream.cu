@@ -22,8 +22,8 @@
 // Arithmetic (the engine's offset-folded path): codes -> fp16 1024 + q and
 // 1024 + 16q (dq4_folded), the tokens' fp16 rows staged in octet-pair order
 // with the odd pairs divided by 16 as the MMA's N columns (8 tokens per MMA),
-// mma.sync m16n8k16 f16 -> f32 per group; per group and token
-// acc += s * (dot - 1024 * sum(staged x)) + b * sum(x) in fp32.
+// mma.sync m16n8k16 f16 -> f32 per group with the accumulator started at
+// -1024 * sum(staged x); per group and token acc += s * dot + b * sum(x) in fp32.
 // Every wait is bounded; a timeout raises kErrMbarTimeout and all roles leave.
 #include "tf_context.cuh"
 #include "tf_gemv_tc.cuh"
@@ -211,7 +211,7 @@ __device__ __forceinline__ void stage_words_gather(const GsParams& p, uint32_t* 
     }
 }
 
-// Per (group, token) {1024 * sum of the staged values, true sum}: one warp per
+// Per (group, token) {-1024 * sum of the staged values, true sum}: one warp per
 // (token, group); odd pairs hold x/16, so the true sum is s + 15 * odd.
 __device__ __forceinline__ void stage_xc(const uint32_t* xs, int ws, int ntok, int ngK, int TP, float2* xc, int ctid) {
     const int warp = ctid >> 5, lane = ctid & 31;
@@ -225,7 +225,7 @@ __device__ __forceinline__ void stage_xc(const uint32_t* xs, int ws, int ntok, i
             s += __shfl_xor_sync(0xffffffffu, s, off);
             odd += __shfl_xor_sync(0xffffffffu, odd, off);
         }
-        if (lane == 0) xc[G * TP + tk] = make_float2(1024.f * s, s + 15.f * odd);
+        if (lane == 0) xc[G * TP + tk] = make_float2(-1024.f * s, s + 15.f * odd);
     }
 }
 
@@ -384,19 +384,20 @@ __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __g
                                 const uint4* xp =
                                     reinterpret_cast<const uint4*>(xs + (b * 8 + g) * ws + (G * 8 + 2 * t) * 4);
                                 const uint4 x0 = xp[0], x1 = xp[1];
-                                float c[4] = {0.f, 0.f, 0.f, 0.f}, cb[4] = {0.f, 0.f, 0.f, 0.f};
-                                mma16816(c, pa0[0], pb0[0], pa0[1], pb0[1], x0.x, x0.y);
-                                mma16816(cb, pa0[2], pb0[2], pa0[3], pb0[3], x0.z, x0.w);
-                                mma16816(c, pa1[0], pb1[0], pa1[1], pb1[1], x1.x, x1.y);
-                                mma16816(cb, pa1[2], pb1[2], pa1[3], pb1[3], x1.z, x1.w);
                                 const float4 xv = *reinterpret_cast<const float4*>(xc + G * TP + b * 8 + 2 * t);
-                                const float xc0 = xv.x, xs0 = xv.y, xc1 = xv.z, xs1 = xv.w;
+                                const float xs0 = xv.y, xs1 = xv.w;
+                                // the chain starts at -1024 * sum(staged x) and ends at the group's dot
+                                float c[4] = {xv.x, xv.z, xv.x, xv.z};
+                                mma16816(c, pa0[0], pb0[0], pa0[1], pb0[1], x0.x, x0.y);
+                                mma16816(c, pa0[2], pb0[2], pa0[3], pb0[3], x0.z, x0.w);
+                                mma16816(c, pa1[0], pb1[0], pa1[1], pb1[1], x1.x, x1.y);
+                                mma16816(c, pa1[2], pb1[2], pa1[3], pb1[3], x1.z, x1.w);
                                 const float sa = scale_at<ST>(scl[0], j), ba = scale_at<ST>(scl[1], j);
                                 const float sb = scale_at<ST>(scl[2], j), bb = scale_at<ST>(scl[3], j);
-                                acc[b][0] = fmaf(sa, (c[0] + cb[0]) - xc0, fmaf(ba, xs0, acc[b][0]));
-                                acc[b][1] = fmaf(sa, (c[1] + cb[1]) - xc1, fmaf(ba, xs1, acc[b][1]));
-                                acc[b][2] = fmaf(sb, (c[2] + cb[2]) - xc0, fmaf(bb, xs0, acc[b][2]));
-                                acc[b][3] = fmaf(sb, (c[3] + cb[3]) - xc1, fmaf(bb, xs1, acc[b][3]));
+                                acc[b][0] = fmaf(sa, c[0], fmaf(ba, xs0, acc[b][0]));
+                                acc[b][1] = fmaf(sa, c[1], fmaf(ba, xs1, acc[b][1]));
+                                acc[b][2] = fmaf(sb, c[2], fmaf(bb, xs0, acc[b][2]));
+                                acc[b][3] = fmaf(sb, c[3], fmaf(bb, xs1, acc[b][3]));
                             }
                         }
                     }

@@ -2,14 +2,17 @@
 // (prefill_router_gemma4_block, Sources/TurboFieldfare/Metal/Prefill/prefill.metal:478-573;
 //  PrefillRouter.encodeGemma4Block, Kernels/Prefill/MoE/PrefillRouter.swift:37-89).
 //
-// One CTA serves 8 tokens.  x~ = float(half h) * float(bf16 es) is staged per
-// token as two fp16 terms (hi, lo), giving 16 MMA columns (token t -> columns
-// 2t, 2t+1) in two 8-column groups.  Each warp takes 16-expert tiles and
-// streams the int8 router rows from L2 straight into MMA fragments (codes
-// exact in fp16), reusing each fragment for both column groups, and folds the
-// per-group scale/bias in fp32.  Then every token selects its top-k by rank
-// (logit desc, id asc -- the reference's insertion order), softmax over the
-// k, times the per-expert gain.
+// Logits: a CTA serves 8 tokens and `tpc` 16-expert tiles.  x~ = float(half
+// h) * float(bf16 es) is staged per token as two fp16 terms (hi, lo), giving
+// 16 MMA columns (token t -> columns 2t, 2t+1) in two 8-column groups.  The
+// CTA's warps take its tiles and split K between them; each streams the int8
+// router rows from L2 straight into MMA fragments (codes exact in fp16),
+// reusing each fragment for both column groups, and folds the per-group
+// scale/bias in fp32; the K slices are added in slice order.  A second launch
+// selects every token's top-k (logit desc, id asc -- the reference's
+// insertion order), softmax over the k, times the per-expert gain.
+#include <algorithm>
+
 #include "tf_context.cuh"
 
 using namespace tf;
@@ -19,6 +22,7 @@ namespace {
 constexpr int kRtTok = 8;          // tokens per CTA
 constexpr int kRtCG = kRtTok / 4;  // 8-column MMA groups
 constexpr int kRtThreads = 256;
+constexpr int kRtWarps = kRtThreads / 32;
 constexpr int kRtMaxE = 256;
 constexpr int kRtMaxK = 64;
 constexpr int kRtSmemMax = 200 * 1024;  // d = 2816 needs ~104 KB: two CTAs per SM
@@ -26,16 +30,13 @@ constexpr int kRtSmemMax = 200 * 1024;  // d = 2816 needs ~104 KB: two CTAs per 
 template <typename ST>
 __global__ void __launch_bounds__(kRtThreads) prefill_router_kernel(
     const uint8_t* __restrict__ W, const ST* __restrict__ S, const ST* __restrict__ B, const __half* __restrict__ H,
-    int hstride, const __nv_bfloat16* __restrict__ es, const __nv_bfloat16* __restrict__ pes, uint32_t* out_idx,
-    __half* out_w, float* out_logits, int T, int E, int D, int K) {
+    int hstride, const __nv_bfloat16* __restrict__ es, float* __restrict__ logits_out, int T, int E, int D, int tpc) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int ws = x_words_stride(D);
     const int ng = D / kGroup;
-    uint32_t* xs = reinterpret_cast<uint32_t*>(smem);                         // [2*kRtTok][ws]
-    float* xsum = reinterpret_cast<float*>(xs + 2 * kRtTok * ws);               // [kRtTok][ng]
-    float* logits = xsum + kRtTok * ng;                                         // [kRtTok][256]
-    float* sel = logits + kRtTok * kRtMaxE;                                     // [kRtTok][64] selected logits
-    uint32_t* selid = reinterpret_cast<uint32_t*>(sel + kRtTok * kRtMaxK);      // [kRtTok][64]
+    uint32_t* xs = reinterpret_cast<uint32_t*>(smem);            // [2*kRtTok][ws]
+    float* xsum = reinterpret_cast<float*>(xs + 2 * kRtTok * ws);  // [kRtTok][ng]
+    float* red = xsum + kRtTok * ng;                               // [warp][kRtTok][16] slice partials
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int t0 = blockIdx.x * kRtTok;
     const int ntok = min(kRtTok, T - t0);
@@ -86,9 +87,12 @@ __global__ void __launch_bounds__(kRtThreads) prefill_router_kernel(
     }
     __syncthreads();
 
-    // logits: warp per 16-expert tile
+    // logits: this CTA's tpc 16-expert tiles, kRtWarps / tpc warps (K slices,
+    // groups slice, slice + ksw, ...) per tile
+    const int ksw = kRtWarps / tpc;
+    const int tile = blockIdx.y * tpc + warp / ksw, slice = warp % ksw;
     const int g = lane >> 2, t = lane & 3;
-    for (int tile = warp; tile * 16 < E; tile += blockDim.x / 32) {
+    if (tile * 16 < E) {
         const int rA = tile * 16 + g, rB = rA + 8;
         const bool va = rA < E, vb = rB < E;
         const uint8_t* wA = W + (size_t)(va ? rA : 0) * D;
@@ -106,13 +110,13 @@ __global__ void __launch_bounds__(kRtThreads) prefill_router_kernel(
             sc[2] = vb ? scale_to_float(S[(size_t)rB * ng + G]) : 0.f;
             sc[3] = vb ? scale_to_float(B[(size_t)rB * ng + G]) : 0.f;
         };
-        uint4 qa, qb;
-        float sc[4];
-        ldw(0, qa, qb, sc);
-        for (int G = 0; G < ng; ++G) {
+        uint4 qa = make_uint4(0, 0, 0, 0), qb = qa;
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+        if (slice < ng) ldw(slice, qa, qb, sc);
+        for (int G = slice; G < ng; G += ksw) {
             uint4 nqa = qa, nqb = qb;
             float nsc[4] = {0.f, 0.f, 0.f, 0.f};
-            if (G + 1 < ng) ldw(G + 1, nqa, nqb, nsc);
+            if (G + ksw < ng) ldw(G + ksw, nqa, nqb, nsc);
             uint32_t pa0[4], pa1[4], pb0[4], pb1[4];
             dq8(qa.x, qa.y, pa0);
             dq8(qa.z, qa.w, pa1);
@@ -142,42 +146,73 @@ __global__ void __launch_bounds__(kRtThreads) prefill_router_kernel(
         }
 #pragma unroll
         for (int cg = 0; cg < kRtCG; ++cg) {
-            if (va) logits[(4 * cg + t) * kRtMaxE + rA] = accA[cg];
-            if (vb) logits[(4 * cg + t) * kRtMaxE + rB] = accB[cg];
-            if (out_logits && 4 * cg + t < ntok) {  // optional caller copy, [T][E]
-                if (va) out_logits[(size_t)(t0 + 4 * cg + t) * E + rA] = accA[cg];
-                if (vb) out_logits[(size_t)(t0 + 4 * cg + t) * E + rB] = accB[cg];
+            red[(warp * kRtTok + 4 * cg + t) * 16 + g] = accA[cg];
+            red[(warp * kRtTok + 4 * cg + t) * 16 + g + 8] = accB[cg];
+        }
+    }
+    __syncthreads();
+    // slices summed in slice order; logits [T][E] in global memory
+    for (int i = tid; i < tpc * kRtTok * 16; i += blockDim.x) {
+        const int tl = i / (kRtTok * 16), tok = (i / 16) % kRtTok, row = i % 16;
+        const int e = (blockIdx.y * tpc + tl) * 16 + row;
+        if (e >= E || tok >= ntok) continue;
+        float v = 0.f;
+        for (int sl = 0; sl < ksw; ++sl) v += red[((tl * ksw + sl) * kRtTok + tok) * 16 + row];
+        logits_out[(size_t)(t0 + tok) * E + e] = v;
+    }
+}
+
+// Per token (one warp each): top-k by (logit desc, id asc) -- the
+// reference's insertion order -- softmax over the k, times the gain.
+__global__ void __launch_bounds__(256) router_select_kernel(const float* __restrict__ logits, int T, int E, int K,
+                                                            const __nv_bfloat16* __restrict__ pes, uint32_t* out_idx,
+                                                            __half* out_w) {
+    __shared__ float sv[8][kRtMaxK];
+    __shared__ uint32_t si[8][kRtMaxK];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tk = blockIdx.x * 8 + warp;
+    if (tk >= T) return;
+    float v[kRtMaxE / 32];
+    uint32_t taken = 0;
+#pragma unroll
+    for (int j = 0; j < kRtMaxE / 32; ++j) {
+        const int e = lane + 32 * j;
+        v[j] = e < E ? logits[(size_t)tk * E + e] : 0.f;
+        if (e >= E) taken |= 1u << j;
+    }
+    for (int r = 0; r < K; ++r) {
+        float bv = 0.f;
+        int be = -1;
+#pragma unroll
+        for (int j = 0; j < kRtMaxE / 32; ++j) {
+            const int e = lane + 32 * j;
+            if (!(taken >> j & 1u) && (be < 0 || v[j] > bv)) {  // e ascending: ties keep the lower id
+                bv = v[j];
+                be = e;
             }
         }
-    }
-    __syncthreads();
-
-    // per-token rank selection
-    for (int i = tid; i < kRtTok * E; i += blockDim.x) {
-        const int tk = i / E, e = i - tk * E;
-        if (tk >= ntok) continue;
-        const float v = logits[tk * kRtMaxE + e];
-        int rank = 0;
-        for (int j = 0; j < E; ++j) {
-            const float o = logits[tk * kRtMaxE + j];
-            rank += (o > v || (o == v && j < e)) ? 1 : 0;
+        for (int off = 16; off; off >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+            const int oe = __shfl_xor_sync(0xffffffffu, be, off);
+            if (oe >= 0 && (be < 0 || ov > bv || (ov == bv && oe < be))) {
+                bv = ov;
+                be = oe;
+            }
         }
-        if (rank < K) {
-            sel[tk * kRtMaxK + rank] = v;
-            selid[tk * kRtMaxK + rank] = (uint32_t)e;
+        if (be >= 0 && (be & 31) == lane) taken |= 1u << (be >> 5);
+        if (lane == 0) {
+            sv[warp][r] = bv;
+            si[warp][r] = (uint32_t)be;
         }
     }
-    __syncthreads();
-    for (int i = tid; i < kRtTok * K; i += blockDim.x) {
-        const int tk = i / K, r = i - tk * K;
-        if (tk >= ntok) continue;
-        const float vmax = sel[tk * kRtMaxK];
-        float sum = 0.f;
-        for (int j = 0; j < K; ++j) sum += expf(sel[tk * kRtMaxK + j] - vmax);
-        const uint32_t e = selid[tk * kRtMaxK + r];
-        out_idx[(size_t)(t0 + tk) * K + r] = e;
-        out_w[(size_t)(t0 + tk) * K + r] =
-            __float2half_rn(expf(sel[tk * kRtMaxK + r] - vmax) / sum * __bfloat162float(pes[e]));
+    __syncwarp();
+    const float vmax = sv[warp][0];
+    float sum = 0.f;
+    for (int j = 0; j < K; ++j) sum += expf(sv[warp][j] - vmax);
+    for (int r = lane; r < K; r += 32) {
+        const uint32_t e = si[warp][r];
+        out_idx[(size_t)tk * K + r] = e;
+        out_w[(size_t)tk * K + r] = __float2half_rn(expf(sv[warp][r] - vmax) / sum * __bfloat162float(pes[e]));
     }
 }
 
@@ -204,36 +239,45 @@ static tf_status router_batched(tf_context* ctx, const void* W, const void* S, c
     if ((reinterpret_cast<uintptr_t>(W) & 15u) || (d % 16) || !aligned2(S) || !aligned2(B) || !aligned2(hidden))
         return fail(ctx, TF_ERR_MISALIGNED, "%s: router weights must be 16-byte aligned", name);
     const size_t smem = (size_t)2 * kRtTok * x_words_stride((int)d) * 4 + (size_t)kRtTok * (d / 64) * 4 +
-                        (size_t)kRtTok * kRtMaxE * 4 + (size_t)kRtTok * kRtMaxK * 8;
-    const dim3 grid((T + kRtTok - 1) / kRtTok);
+                        (size_t)kRtWarps * kRtTok * 16 * 4;
+    if (smem > (size_t)kRtSmemMax) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: d too large", name);
     cudaStream_t cs = static_cast<cudaStream_t>(stream);
-    auto run = [&](auto* kernel) -> tf_status {
-        static bool configured[64] = {};
-        if (!configured[ctx->device & 63]) {
-            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kRtSmemMax);
-            if (e != cudaSuccess) return cuda_check(ctx, e, name);
-            configured[ctx->device & 63] = true;
-        }
-        if (smem > (size_t)kRtSmemMax) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: d too large", name);
-        return TF_OK;
-    };
-    tf_status s;
-    if (st == TF_SCALE_F16) {
-        s = run(prefill_router_kernel<__half>);
-        if (s) return s;
-        prefill_router_kernel<__half><<<grid, kRtThreads, smem, cs>>>(
-            static_cast<const uint8_t*>(W), static_cast<const __half*>(S), static_cast<const __half*>(B),
-            static_cast<const __half*>(hidden), (int)hidden_stride, static_cast<const __nv_bfloat16*>(es),
-            static_cast<const __nv_bfloat16*>(pes), static_cast<uint32_t*>(out_indices), static_cast<__half*>(out_weights),
-            out_logits, (int)T, (int)E, (int)d, (int)top_k);
-    } else {
-        s = run(prefill_router_kernel<__nv_bfloat16>);
-        if (s) return s;
-        prefill_router_kernel<__nv_bfloat16><<<grid, kRtThreads, smem, cs>>>(
-            static_cast<const uint8_t*>(W), static_cast<const __nv_bfloat16*>(S), static_cast<const __nv_bfloat16*>(B),
-            static_cast<const __half*>(hidden), (int)hidden_stride, static_cast<const __nv_bfloat16*>(es),
-            static_cast<const __nv_bfloat16*>(pes), static_cast<uint32_t*>(out_indices), static_cast<__half*>(out_weights),
-            out_logits, (int)T, (int)E, (int)d, (int)top_k);
+    static bool configured[2][64] = {};
+    const void* kfn = st == TF_SCALE_F16 ? reinterpret_cast<const void*>(&prefill_router_kernel<__half>)
+                                         : reinterpret_cast<const void*>(&prefill_router_kernel<__nv_bfloat16>);
+    if (!configured[st][ctx->device & 63]) {
+        cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kRtSmemMax);
+        if (e != cudaSuccess) return cuda_check(ctx, e, name);
+        configured[st][ctx->device & 63] = true;
+    }
+    // Logits go to the caller's array when given, else to the context's
+    // scratch in token chunks that fit it.  Expert tiles are spread over
+    // CTAs (tpc tiles each, the rest of the CTA's warps split K) until the
+    // grid covers about two CTAs per SM.
+    const int tiles = (int)((E + 15) / 16);
+    const uint32_t chunk = out_logits ? T : (uint32_t)(kRtLogitsCap / E) / kRtTok * kRtTok;
+    for (uint32_t c0 = 0; c0 < T; c0 += chunk) {
+        const uint32_t Tc = std::min(chunk, T - c0);
+        float* lg = out_logits ? out_logits : ctx->d_rt_logits;
+        const long long gx = (Tc + kRtTok - 1) / kRtTok;
+        int tpc = kRtWarps;
+        while (tpc > 1 && gx * ((tiles + tpc - 1) / tpc) < 2ll * ctx->num_sms) tpc >>= 1;
+        const dim3 grid((unsigned)gx, (unsigned)((tiles + tpc - 1) / tpc));
+        const __half* h = static_cast<const __half*>(hidden) + (size_t)c0 * hidden_stride;
+        float* lgc = lg + (out_logits ? (size_t)c0 * E : 0);
+        if (st == TF_SCALE_F16)
+            prefill_router_kernel<__half><<<grid, kRtThreads, smem, cs>>>(
+                static_cast<const uint8_t*>(W), static_cast<const __half*>(S), static_cast<const __half*>(B), h,
+                (int)hidden_stride, static_cast<const __nv_bfloat16*>(es), lgc, (int)Tc, (int)E, (int)d, tpc);
+        else
+            prefill_router_kernel<__nv_bfloat16><<<grid, kRtThreads, smem, cs>>>(
+                static_cast<const uint8_t*>(W), static_cast<const __nv_bfloat16*>(S),
+                static_cast<const __nv_bfloat16*>(B), h, (int)hidden_stride, static_cast<const __nv_bfloat16*>(es),
+                lgc, (int)Tc, (int)E, (int)d, tpc);
+        router_select_kernel<<<(Tc + 7) / 8, 256, 0, cs>>>(lgc, (int)Tc, (int)E, (int)top_k,
+                                                            static_cast<const __nv_bfloat16*>(pes),
+                                                            static_cast<uint32_t*>(out_indices) + (size_t)c0 * top_k,
+                                                            static_cast<__half*>(out_weights) + (size_t)c0 * top_k);
     }
     return cuda_check(ctx, cudaGetLastError(), name);
 }

@@ -51,12 +51,14 @@ class ExpertLayout:
         return o, n
 
 
-def expert_layout(d: int, f: int, page: int = PAGE) -> ExpertLayout:
+def expert_layout(d: int, f: int, page: int = PAGE, bits: int = 4) -> ExpertLayout:
+    """Blob order gate{W,s,b}, up{W,s,b}, down{W,s,b}, each 16-byte aligned;
+    `bits` 2/3/4 sets the packed weight size (rows * cols * bits / 8)."""
     off = {}
     cur = 0
     for proj, rows, cols in (("gate", f, d), ("up", f, d), ("down", d, f)):
         off[f"{proj}_w"] = cur
-        cur = _align(cur + rows * cols // 2)
+        cur = _align(cur + rows * cols * bits // 8)
         off[f"{proj}_s"] = cur
         cur = _align(cur + rows * (cols // 64) * 2)
         off[f"{proj}_b"] = cur

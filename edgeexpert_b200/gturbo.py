@@ -114,7 +114,9 @@ def _shape_of(entry: ExpertEntry) -> tuple[int, int, int]:
 
 def load_layer_host(directory, layer: int, layout: PackedLayout | None = None):
     """One layer's experts as a host byte pool in logical order:
-    (pool uint8 [E * stride], stride, tf_expert_offsets, d, f, scale dtype name)."""
+    (pool uint8 [E * stride], stride, tf_expert_offsets, d, f, scale dtype name).
+    2/3/4-bit routed experts (the rebits output keeps the same layout with
+    smaller weight tensors); `bits` is the gate tensor's "bits" field."""
     from .format import expert_layout
     layout = layout or read_layout(directory)
     entries = layout.experts[layer]
@@ -122,7 +124,7 @@ def load_layer_host(directory, layer: int, layout: PackedLayout | None = None):
         if role not in entries[0].tensors:
             raise LayoutError(f"layout.json: expert tensor {role} missing")
     d, f, bits = _shape_of(entries[0])
-    if bits != 4:
+    if bits not in (2, 3, 4):
         raise LayoutError(f"layout.json: {bits}-bit routed experts are not supported by this loader")
     sdtype = entries[0].tensors["gate_scales"]["dtype"].lower()
     data = np.fromfile(Path(directory) / "packed_experts" / layout.files[layer], dtype=np.uint8)
@@ -142,7 +144,7 @@ def load_layer_host(directory, layer: int, layout: PackedLayout | None = None):
             pool[e.expert * stride:(e.expert + 1) * stride] = data[e.offset:e.offset + stride]
         offsets = ExpertOffsets(*src_off)
     else:  # 16-byte realignment of every sub-tensor
-        lay = expert_layout(d, f)
+        lay = expert_layout(d, f, bits=bits)
         stride = lay.stride
         pool = np.zeros(E * stride, np.uint8)
         dst_off = [getattr(lay.offsets, n) for n in OFFSET_FIELDS]
@@ -160,7 +162,9 @@ def load_layer_pool(directory, layer: int, device, layout: PackedLayout | None =
     import torch
 
     from .moe import ExpertPool
+    layout = layout or read_layout(directory)
     pool, stride, offsets, d, f, sdtype = load_layer_host(directory, layer, layout)
+    bits = _shape_of(layout.experts[layer][0])[2]
     blob = torch.from_numpy(pool).to(device)
     sd = torch.float16 if sdtype in ("f16", "fp16", "float16") else torch.bfloat16
-    return ExpertPool(blob, stride, len(pool) // stride, offsets, d, f, sd)
+    return ExpertPool(blob, stride, len(pool) // stride, offsets, d, f, sd, bits)

@@ -50,6 +50,7 @@ class ExpertPool:
     d: int
     f: int
     scale_dtype: torch.dtype = torch.bfloat16
+    bits: int = 4  # packed routed-weight width: 4, or 2 / 3 (the rebits output)
 
 
 class MoE:
@@ -92,18 +93,30 @@ class MoE:
     def _stype(dt):
         return 1 if dt == torch.float16 else 0
 
-    def encode_routed_phase1(self, experts, x, acts, d: int, f: int, top_k: int, expert_ids=None, stream=None):
+    def encode_routed_phase1(self, experts, x, acts, d: int, f: int, top_k: int, expert_ids=None, stream=None,
+                             bits: int = 4):
+        """bits 2 / 3: moe_phase1_gate_up_act_b2/_b3 (the `bits` argument of MoE.swift:244)."""
         pool, stride, ne, ids, blobs, off, sdt = self._source(experts, expert_ids, top_k)
-        st = lib().tf_moe_phase1(self.ctx.handle, pool, stride, ne, ids, blobs, C.byref(off), ptr(x), ptr(acts),
-                                 d, f, top_k, self._stype(sdt), stream_ptr(stream))
+        if bits == 4:
+            st = lib().tf_moe_phase1(self.ctx.handle, pool, stride, ne, ids, blobs, C.byref(off), ptr(x), ptr(acts),
+                                     d, f, top_k, self._stype(sdt), stream_ptr(stream))
+        else:
+            st = lib().tf_moe_phase1_bits(self.ctx.handle, bits, pool, stride, ne, ids, blobs, C.byref(off), ptr(x),
+                                          ptr(acts), d, f, top_k, self._stype(sdt), stream_ptr(stream))
         self.ctx.check(st, "MoE.encodeRoutedPersistentPhase1U16Load")
 
     def encode_routed_phase2_reduce(self, experts, acts, routing_weights, residual, y, d: int, f: int, top_k: int,
-                                    expert_ids=None, stream=None):
+                                    expert_ids=None, stream=None, bits: int = 4):
+        """bits 2 / 3: moe_phase2_down_reduce_b2/_b3 (the `bits` argument of MoE.swift:324)."""
         pool, stride, ne, ids, blobs, off, sdt = self._source(experts, expert_ids, top_k)
-        st = lib().tf_moe_phase2(self.ctx.handle, pool, stride, ne, ids, blobs, C.byref(off), ptr(acts),
-                                 ptr(routing_weights), ptr(residual), ptr(y), d, f, top_k, self._stype(sdt),
-                                 stream_ptr(stream))
+        if bits == 4:
+            st = lib().tf_moe_phase2(self.ctx.handle, pool, stride, ne, ids, blobs, C.byref(off), ptr(acts),
+                                     ptr(routing_weights), ptr(residual), ptr(y), d, f, top_k, self._stype(sdt),
+                                     stream_ptr(stream))
+        else:
+            st = lib().tf_moe_phase2_bits(self.ctx.handle, bits, pool, stride, ne, ids, blobs, C.byref(off),
+                                          ptr(acts), ptr(routing_weights), ptr(residual), ptr(y), d, f, top_k,
+                                          self._stype(sdt), stream_ptr(stream))
         self.ctx.check(st, "MoE.encodeRoutedPersistentPhase2Reduce")
 
 

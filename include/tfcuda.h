@@ -89,7 +89,9 @@ TF_API tf_status tf_int8_gemv(tf_context* ctx, const void* W, const void* scales
 /* Batched form of the two above: `batch` matrices at W + i*w_stride_bytes
  * (scales/biases at + i*sb_stride_elems elements), a shared activation block
  * of `ntok` (1..8) tokens x[t*x_row_stride + k], outputs
- * y[i*y_batch_stride + t*y_row_stride + row].  bits in {4, 8}.
+ * y[i*y_batch_stride + t*y_row_stride + row].  bits in {2, 3, 4, 8}: 2- and
+ * 3-bit rows are LSB-first packed, n/4 and 3n/8 bytes (the *_b3 GEMVs,
+ * dequant_int4.metal:512-717; W 16-byte (2-bit) / 8-byte (3-bit) aligned).
  * (No single reference counterpart: it is the GemvBench loop,
  * Tests/TurboFieldfare/Core/Kernels/Quant/GemvBench.swift:20-107, and the
  * T-token repeated-GEMV path, PrefillSharedExpert.swift:43-58, in one launch.) */
@@ -176,6 +178,24 @@ TF_API tf_status tf_moe_phase2(tf_context* ctx, const void* pool, uint64_t exper
                         const void* expert_ids, const void* const* blobs, const tf_expert_offsets* offsets,
                         const void* acts, const void* routing_weights, const void* residual, void* y,
                         uint32_t d, uint32_t f, uint32_t top_k, tf_scale_type st, void* stream);
+
+/* The same two phases for 2- and 3-bit routed experts (the rebits output):
+ * MoE.encodeRoutedPersistentPhase1U16Load / encodeRoutedPersistentPhase2Reduce
+ * with bits = 2 or 3 (MoE.swift:234-362; moe_phase1_gate_up_act_b2/_b3 and
+ * moe_phase2_down_reduce_b2/_b3, moe.metal:644-1180).  Arguments and results
+ * as tf_moe_phase1 / tf_moe_phase2; gate/up rows are d*bits/8 bytes and down
+ * rows f*bits/8 bytes, LSB-first packed; weight sub-tensor offsets, pool,
+ * stride and blobs 8-byte (3-bit) or 16-byte (2-bit) aligned.  bits = 4
+ * calls tf_moe_phase1 / tf_moe_phase2. */
+TF_API tf_status tf_moe_phase1_bits(tf_context* ctx, uint32_t bits, const void* pool, uint64_t expert_stride,
+                                    uint32_t num_experts, const void* expert_ids, const void* const* blobs,
+                                    const tf_expert_offsets* offsets, const void* x, void* acts, uint32_t d,
+                                    uint32_t f, uint32_t top_k, tf_scale_type st, void* stream);
+TF_API tf_status tf_moe_phase2_bits(tf_context* ctx, uint32_t bits, const void* pool, uint64_t expert_stride,
+                                    uint32_t num_experts, const void* expert_ids, const void* const* blobs,
+                                    const tf_expert_offsets* offsets, const void* acts, const void* routing_weights,
+                                    const void* residual, void* y, uint32_t d, uint32_t f, uint32_t top_k,
+                                    tf_scale_type st, void* stream);
 
 /* SharedExpertProjection (Sources/TurboFieldfare/Kernels/MoE/SharedExpertInt8.swift:9-31). */
 typedef struct {

@@ -118,6 +118,17 @@ void orc_moe_phase2(const uint8_t *const *blobs, const orc_expert_offsets *off,
                     int scale_type, const uint16_t *acts_f16, const uint16_t *w_f16,
                     const uint16_t *residual_f16, uint16_t *y_f16, float *y_f32,
                     int D, int F, int top_k, int nthreads);
+/* 2/3-bit kernel-order rows (moe.metal:644-757, dequant_int4.metal:512-583)
+ * and the routed phases built on them (moe.metal:950-1180).  Rows are
+ * LSB-first packed: 2-bit n/4 bytes, 3-bit 3n/8 bytes; bits in {2, 3}. */
+void orc_lowbit_gemv_kernel_order(const uint8_t *W, const uint16_t *S, const uint16_t *B, int scale_type,
+                                  int bits, const uint16_t *x_f16, float *y_f32, uint16_t *y_f16, int m, int n,
+                                  int nthreads);
+void orc_moe_phase1_bits(const uint8_t *const *blobs, const orc_expert_offsets *off, int scale_type, int bits,
+                         const uint16_t *x_f16, uint16_t *acts_f16, int D, int F, int top_k, int nthreads);
+void orc_moe_phase2_bits(const uint8_t *const *blobs, const orc_expert_offsets *off, int scale_type, int bits,
+                         const uint16_t *acts_f16, const uint16_t *w_f16, const uint16_t *residual_f16,
+                         uint16_t *y_f16, float *y_f32, int D, int F, int top_k, int nthreads);
 /* Shared expert.  bits 4: g=half(gemv), u=half(gemv), act=half(gelu(g)*u),
  * y=half(down.act).  bits 8: same rounding of g/u (int8 fused kernel).
  * act_out (may be NULL) receives act as fp16 bits; y_f32 the unrounded y. */

@@ -94,6 +94,10 @@ def lib():
                 "orc_moe_phase1": ([C.POINTER(VP), C.POINTER(Offsets), I, u16p, u16p, I, I, I, I], None),
                 "orc_moe_phase2": ([C.POINTER(VP), C.POINTER(Offsets), I, u16p, u16p, VP, u16p, f32p, I, I, I, I],
                                    None),
+                "orc_lowbit_gemv_kernel_order": ([u8p, u16p, u16p, I, I, u16p, f32p, u16p, I, I, I], None),
+                "orc_moe_phase1_bits": ([C.POINTER(VP), C.POINTER(Offsets), I, I, u16p, u16p, I, I, I, I], None),
+                "orc_moe_phase2_bits": ([C.POINTER(VP), C.POINTER(Offsets), I, I, u16p, u16p, VP, u16p, f32p, I, I,
+                                         I, I], None),
                 "orc_shared_expert": ([u8p, u16p, u16p, u8p, u16p, u16p, u8p, u16p, u16p, I, I, u16p, u16p, u16p,
                                        f32p, I, I, I], None),
                 "orc_group_pairs": ([VP, I, I, I, I, I, VP, I, VP, u32p, u32p, VP, C.POINTER(I), VP, C.POINTER(I),
@@ -295,6 +299,38 @@ def moe_phase2(blobs, off: Offsets, acts_f16, w_f16, residual_f16, D: int, F: in
     lib().orc_moe_phase2(_blob_ptrs(blobs), C.byref(off), scale_type, np.ascontiguousarray(acts_f16, np.uint16),
                          np.ascontiguousarray(w_f16, np.uint16), None if res is None else res.ctypes.data, y16, y32,
                          D, F, k, _nt(nthreads))
+    return y16, y32
+
+
+def lowbit_gemv_kernel_order(W, S, B, x_f16, bits: int, scale_type: int = 0, nthreads: int = 0):
+    """moe_int2/int3 row order (moe.metal:644-757): (fp32 [m], fp16 bits [m])."""
+    m = W.shape[0]
+    n = S.shape[1] * 64
+    y32 = np.empty(m, np.float32)
+    y16 = np.empty(m, np.uint16)
+    lib().orc_lowbit_gemv_kernel_order(np.ascontiguousarray(W), np.ascontiguousarray(S), np.ascontiguousarray(B),
+                                       scale_type, bits, np.ascontiguousarray(x_f16, np.uint16), y32, y16, m, n,
+                                       _nt(nthreads))
+    return y32, y16
+
+
+def moe_phase1_bits(blobs, off: Offsets, x_f16, D: int, F: int, bits: int, scale_type: int = 0, nthreads: int = 0):
+    k = len(blobs)
+    acts = np.empty(k * F, np.uint16)
+    lib().orc_moe_phase1_bits(_blob_ptrs(blobs), C.byref(off), scale_type, bits,
+                              np.ascontiguousarray(x_f16, np.uint16), acts, D, F, k, _nt(nthreads))
+    return acts
+
+
+def moe_phase2_bits(blobs, off: Offsets, acts_f16, w_f16, residual_f16, D: int, F: int, bits: int,
+                    scale_type: int = 0, nthreads: int = 0):
+    k = len(blobs)
+    y16 = np.empty(D, np.uint16)
+    y32 = np.empty(D, np.float32)
+    res = None if residual_f16 is None else np.ascontiguousarray(residual_f16, np.uint16)
+    lib().orc_moe_phase2_bits(_blob_ptrs(blobs), C.byref(off), scale_type, bits,
+                              np.ascontiguousarray(acts_f16, np.uint16), np.ascontiguousarray(w_f16, np.uint16),
+                              None if res is None else res.ctypes.data, y16, y32, D, F, k, _nt(nthreads))
     return y16, y32
 
 

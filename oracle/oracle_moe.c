@@ -376,3 +376,136 @@ void orc_int4_qmm(const uint8_t *W, const uint16_t *S, const uint16_t *B, int st
         }
     free(X);
 }
+
+/* ---------------- 2/3-bit routed decode (moe.metal:644-1180) --------------- */
+/* Kernel-order row of moe_int2_gemv_row_simd_dev_vec / moe_int3_gemv_row_simd_dev_vec
+ * (moe.metal:644-757; the same lane scheme as dequant_int4_gemv_simd_body_b3,
+ * dequant_int4.metal:512-583): 32 lanes; full blocks of 4 groups where lane l
+ * owns the 8 codes at blk*256 + 8l (2-bit: the u16 at blk*64 + 2l; 3-bit: the
+ * 3 bytes at blk*96 + 3l), an fma chain for the dot, a left-to-right sum of
+ * the 8 activations, acc = fma(s, dot, acc); acc = fma(b, sum, acc); the
+ * groups past the last full block with 2 codes per lane; butterfly lane sum. */
+static float lowbit_row_lanes(const uint8_t *wr, const uint16_t *sr, const uint16_t *br, int st, int bits,
+                              const float *x, int n) {
+    const int ng = n / 64, full = ng / 4;
+    float acc[32];
+    for (int lane = 0; lane < 32; ++lane) {
+        float a = 0.0f;
+        for (int blk = 0; blk < full; ++blk) {
+            const int g = blk * 4 + (lane >> 3);
+            const float s = orc_scale_to_float(sr[g], st), b = orc_scale_to_float(br[g], st);
+            uint32_t v;
+            if (bits == 2) {
+                const int bb = blk * 64 + lane * 2;
+                v = (uint32_t)wr[bb] | ((uint32_t)wr[bb + 1] << 8);
+            } else {
+                const int bb = blk * 96 + lane * 3;
+                v = (uint32_t)wr[bb] | ((uint32_t)wr[bb + 1] << 8) | ((uint32_t)wr[bb + 2] << 16);
+            }
+            const uint32_t mask = (1u << bits) - 1u;
+            const float *e = x + blk * 256 + lane * 8;
+            float dot = 0.0f;
+            for (int i = 0; i < 8; ++i) dot = fmaf((float)((v >> (bits * i)) & mask), e[i], dot);
+            const float sum = e[0] + e[1] + e[2] + e[3] + e[4] + e[5] + e[6] + e[7];
+            a = fmaf(s, dot, a);
+            a = fmaf(b, sum, a);
+        }
+        for (int g = full * 4; g < ng; ++g) {
+            const float s = orc_scale_to_float(sr[g], st), b = orc_scale_to_float(br[g], st);
+            const int c0 = g * 64 + lane * 2;
+            uint32_t q0, q1;
+            if (bits == 2) {
+                const uint8_t byte = wr[g * 16 + lane / 2];
+                const int sh = 4 * (lane & 1);
+                q0 = (byte >> sh) & 3u;
+                q1 = (byte >> (sh + 2)) & 3u;
+            } else {
+                const int bbit = c0 * 3, b0 = bbit / 8, bsh = bbit % 8;
+                const uint32_t v = (uint32_t)wr[b0] | ((uint32_t)wr[b0 + 1] << 8);
+                q0 = (v >> bsh) & 7u;
+                q1 = (v >> (bsh + 3)) & 7u;
+            }
+            const float x0 = x[c0], x1 = x[c0 + 1];
+            float dot = fmaf((float)q0, x0, 0.0f);
+            dot = fmaf((float)q1, x1, dot);
+            a = fmaf(s, dot, a);
+            a = fmaf(b, x0 + x1, a);
+        }
+        acc[lane] = a;
+    }
+    for (int off = 16; off >= 1; off >>= 1)
+        for (int l = 0; l < 32; ++l)
+            if ((l & off) == 0) acc[l] += acc[l | off];
+    return acc[0];
+}
+
+void orc_lowbit_gemv_kernel_order(const uint8_t *W, const uint16_t *S, const uint16_t *B, int st, int bits,
+                                  const uint16_t *x16, float *y32, uint16_t *y16, int m, int n, int nthreads) {
+    float *x = (float *)malloc(sizeof(float) * (size_t)n);
+    orc_f16_to_f32_array(x16, x, (size_t)n);
+    const size_t rb = orc_packed_row_bytes(n, bits);
+    const int ng = n / 64;
+    (void)nthreads;
+#ifdef _OPENMP
+#pragma omp parallel for schedule(static) num_threads(nthreads > 0 ? nthreads : 1)
+#endif
+    for (int r = 0; r < m; ++r) {
+        const float v = lowbit_row_lanes(W + rb * (size_t)r, S + (size_t)r * ng, B + (size_t)r * ng, st, bits, x, n);
+        if (y32) y32[r] = v;
+        if (y16) y16[r] = orc_f16_bits(v);
+    }
+    free(x);
+}
+
+/* moe_phase1_gate_up_act_b2/_b3 (moe.metal:950-1064): per (slot, f) the gate
+ * and up rows in kernel order, acts = half(gelu_tanh(g) * u). */
+void orc_moe_phase1_bits(const uint8_t *const *blobs, const orc_expert_offsets *o, int st, int bits,
+                         const uint16_t *x16, uint16_t *acts, int D, int F, int top_k, int nthreads) {
+    float *x = (float *)malloc(sizeof(float) * (size_t)D);
+    orc_f16_to_f32_array(x16, x, (size_t)D);
+    const int ng = D / 64;
+    const size_t rb = orc_packed_row_bytes(D, bits);
+    (void)nthreads;
+#ifdef _OPENMP
+#pragma omp parallel for schedule(static) num_threads(nthreads > 0 ? nthreads : 1)
+#endif
+    for (int rowg = 0; rowg < top_k * F; ++rowg) {
+        const int slot = rowg / F, f = rowg % F;
+        const uint8_t *b = blobs[slot];
+        const float g = lowbit_row_lanes(b + o->gate_w + (size_t)f * rb, BLOB_U16(b, o->gate_s) + (size_t)f * ng,
+                                         BLOB_U16(b, o->gate_b) + (size_t)f * ng, st, bits, x, D);
+        const float u = lowbit_row_lanes(b + o->up_w + (size_t)f * rb, BLOB_U16(b, o->up_s) + (size_t)f * ng,
+                                         BLOB_U16(b, o->up_b) + (size_t)f * ng, st, bits, x, D);
+        acts[(size_t)slot * F + f] = orc_f16_bits(orc_gelu_tanh(g) * u);
+    }
+    free(x);
+}
+
+/* moe_phase2_down_reduce_b2/_b3 (moe.metal:1108-1180): partial[slot] =
+ * float(w_slot) * down_slot[d].acts_slot (kernel-order row);
+ * y[d] = half(residual[d] + partial[0] + partial[1] + ...). */
+void orc_moe_phase2_bits(const uint8_t *const *blobs, const orc_expert_offsets *o, int st, int bits,
+                         const uint16_t *acts16, const uint16_t *w16, const uint16_t *res16, uint16_t *y16,
+                         float *y32, int D, int F, int top_k, int nthreads) {
+    float *acts = (float *)malloc(sizeof(float) * (size_t)top_k * F);
+    orc_f16_to_f32_array(acts16, acts, (size_t)top_k * F);
+    const int ng = F / 64;
+    const size_t rb = orc_packed_row_bytes(F, bits);
+    (void)nthreads;
+#ifdef _OPENMP
+#pragma omp parallel for schedule(static) num_threads(nthreads > 0 ? nthreads : 1)
+#endif
+    for (int d = 0; d < D; ++d) {
+        float acc = res16 ? orc_f16_to_float(res16[d]) : 0.0f;
+        for (int s = 0; s < top_k; ++s) {
+            const uint8_t *b = blobs[s];
+            const float v = lowbit_row_lanes(b + o->down_w + (size_t)d * rb, BLOB_U16(b, o->down_s) + (size_t)d * ng,
+                                             BLOB_U16(b, o->down_b) + (size_t)d * ng, st, bits,
+                                             acts + (size_t)s * F, F);
+            acc += orc_f16_to_float(w16[s]) * v;
+        }
+        if (y32) y32[d] = acc;
+        if (y16) y16[d] = orc_f16_bits(acc);
+    }
+    free(acts);
+}
