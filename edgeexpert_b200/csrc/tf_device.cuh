@@ -62,7 +62,12 @@ __device__ __forceinline__ bool tf_check_align(const void* p, unsigned a, uint32
 #define TF_ALIGNED(p, a, err, site) true
 #endif
 
-__device__ __forceinline__ float scale_to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
+// bf16 -> fp32 is exact as a 16-bit shift; written as integer ops so it stays
+// on the ALU pipe inside the streaming loops (no conversion instruction)
+__device__ __forceinline__ float bf16_bits_to_float(uint32_t bits) { return __uint_as_float(bits << 16); }
+__device__ __forceinline__ float scale_to_float(__nv_bfloat16 v) {
+    return bf16_bits_to_float((uint32_t)__bfloat16_as_ushort(v));
+}
 __device__ __forceinline__ float scale_to_float(__half v) { return __half2float(v); }
 
 template <typename ST>

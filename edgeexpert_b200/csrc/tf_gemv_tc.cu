@@ -402,6 +402,11 @@ __global__ void __launch_bounds__(kGtThreads, 1) gemv_tc_kernel(const __grid_con
 // SPLIT = 2: 16 consumers, the warps w and w + 8 of a row tile take the
 // stage's first and second TMA box (groups 0-3 / 4-7) and add their row sums
 // through shared memory at the job's end.
+// Exact int -> float for |v| < 2^22 with integer and FMA-pipe operations
+// (1.5 * 2^23 as the magic), keeping the conversion unit out of the loop.
+// The group dots it converts are at most 15 * 128 * 64 in magnitude.
+__device__ __forceinline__ float i2f_small(int v) { return __int_as_float(v + 0x4B400000) - 12582912.0f; }
+
 template <int SPLIT>
 struct GsCfg {
     static constexpr int kConsumers = 8 * SPLIT;
@@ -483,7 +488,8 @@ __global__ void __launch_bounds__(GsCfg<SPLIT>::kThreads, 1) gemv_stream_kernel(
         const int g = lane >> 2, t = lane & 3;
         const uint4* zeros = reinterpret_cast<const uint4*>(xb - 32);
         constexpr uint32_t kLo = 0x0F0F0F0Fu;
-        uint32_t q = 0;
+        uint32_t q = 0, rph = 0;
+        int rslot = 0;
         int jl = 0;
         bool ok = true;
         for (int job = blockIdx.x; ok && job < p.jobs; job += gridDim.x, ++jl) {
@@ -496,8 +502,12 @@ __global__ void __launch_bounds__(GsCfg<SPLIT>::kThreads, 1) gemv_stream_kernel(
             const ST* bB = bA + 8 * ngK;
             float accA = 0.f, accB = 0.f;
             for (int st = 0; st < nst; ++st, ++q) {
-                const int slot = (int)(q % (uint32_t)R);
-                if (!(ok = gwait(&sh.full[slot], (q / R) & 1u, sh.abort_flag, p.err, __LINE__, gt_info(jl, q)))) break;
+                const int slot = rslot;
+                if (!(ok = gwait(&sh.full[slot], rph, sh.abort_flag, p.err, __LINE__, gt_info(jl, q)))) break;
+                if (++rslot == R) {  // ring position without a division per stage
+                    rslot = 0;
+                    rph ^= 1u;
+                }
                 const uint8_t* rowA = ring + slot * kGtStage + (16 * w + g) * 128;
                 const int ng = min(8, ngK - 8 * st);
                 // one block of 4 groups = one TMA box (k): two interleaved MMA
@@ -528,10 +538,10 @@ __global__ void __launch_bounds__(GsCfg<SPLIT>::kThreads, 1) gemv_stream_kernel(
                     if (4 * k + t < ng) {
                         const int G = 8 * st + 4 * k + t;
                         const float xc = xsc[G], xm = xsum[G];
-                        const int dA = 128 * (c[0][0] + c[1][0]) + (c[0][1] + c[1][1]);
-                        const int dB = 128 * (c[0][2] + c[1][2]) + (c[0][3] + c[1][3]);
-                        accA += scale_to_float(sA[G]) * ((float)dA * xc) + scale_to_float(bA[G]) * xm;
-                        accB += scale_to_float(sB[G]) * ((float)dB * xc) + scale_to_float(bB[G]) * xm;
+                        const float dA = fmaf(128.f, i2f_small(c[0][0] + c[1][0]), i2f_small(c[0][1] + c[1][1]));
+                        const float dB = fmaf(128.f, i2f_small(c[0][2] + c[1][2]), i2f_small(c[0][3] + c[1][3]));
+                        accA += scale_to_float(sA[G]) * (dA * xc) + scale_to_float(bA[G]) * xm;
+                        accB += scale_to_float(sB[G]) * (dB * xc) + scale_to_float(bB[G]) * xm;
                     }
                 };
                 if constexpr (SPLIT == 2) {

@@ -284,7 +284,8 @@ __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __g
     if (warp == 0) {
         // ---------------- loader (one thread) ----------------
         if (lane == 0) {
-            uint32_t q = 0;
+            int slot = 0;
+            uint32_t ph = 0;  // ring position as (slot, wrap parity): no division in the loop
             for (int job = j0; job < j1; ++job) {
                 const GsJob J = gs_decode(sh, ng, job, p.ntile);
                 const tf_moe_group gr = p.groups[J.group];
@@ -299,9 +300,8 @@ __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __g
                     prefetch_l2(blob + p.ob1 + (size_t)r0 * ngK * 2, sb);
                 }
                 bool ok = true;
-                for (int st = 0; st < nst; ++st, ++q) {
-                    const int slot = (int)(q % (uint32_t)R);
-                    if (!(ok = gs_wait(&sh.empty[slot], ((q / R) & 1) ^ 1, sh.abort_flag, p.err, __LINE__))) break;
+                for (int st = 0; st < nst; ++st) {
+                    if (!(ok = gs_wait(&sh.empty[slot], ph ^ 1u, sh.abort_flag, p.err, __LINE__))) break;
                     uint8_t* dst = ring + slot * kGsStage;
                     mbar_arrive_expect_tx(&sh.full[slot], kGsStage);
                     if (p.mode == 0) {
@@ -309,6 +309,10 @@ __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __g
                         tma_load_3d(dst + kGsBox, &p.map1, st * 128, r0, (int)gr.expert, &sh.full[slot]);
                     } else {
                         tma_load_3d(dst, &p.map0, st * 128, r0, (int)gr.expert, &sh.full[slot]);  // 240 rows
+                    }
+                    if (++slot == R) {
+                        slot = 0;
+                        ph ^= 1u;
                     }
                 }
                 if (!ok) break;
@@ -323,7 +327,8 @@ __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __g
         // up row 8w+g (box 1); MODE 1 rows 16w+g and 16w+g+8
         const int offA = p.mode == 0 ? (8 * w + g) * 128 : (16 * w + g) * 128;
         const int offB = p.mode == 0 ? kGsBox + (8 * w + g) * 128 : (16 * w + g + 8) * 128;
-        uint32_t q = 0;
+        int slot = 0;
+        uint32_t ph = 0;
         int staged_group = -1, staged_pass = -1;
         for (int job = j0; job < j1; ++job) {
             const GsJob J = gs_decode(sh, ng, job, p.ntile);
@@ -361,10 +366,9 @@ __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __g
             uint2 scl[4], nscl[4];
             load_scales<ST>(sA, bA, sB, bB, 0, ngK, vec, scl);
             bool ok = true;
-            for (int st = 0; st < nst; ++st, ++q) {
+            for (int st = 0; st < nst; ++st) {
                 if (st + 1 < nst) load_scales<ST>(sA, bA, sB, bB, 4 * (st + 1), ngK, vec, nscl);
-                const int slot = (int)(q % (uint32_t)R);
-                if (!(ok = gs_wait(&sh.full[slot], (q / R) & 1u, sh.abort_flag, p.err, __LINE__))) break;
+                if (!(ok = gs_wait(&sh.full[slot], ph, sh.abort_flag, p.err, __LINE__))) break;
                 const uint8_t* sbase = ring + slot * kGsStage;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
@@ -404,6 +408,10 @@ __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __g
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sh.empty[slot]);
+                if (++slot == R) {
+                    slot = 0;
+                    ph ^= 1u;
+                }
 #pragma unroll
                 for (int a = 0; a < 4; ++a) scl[a] = nscl[a];
             }

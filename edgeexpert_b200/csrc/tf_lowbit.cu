@@ -142,7 +142,7 @@ __device__ __forceinline__ float lb_half_of(uint32_t w, const ST* p) {
     if constexpr (std::is_same<ST, __half>::value)
         return __half2float(__ushort_as_half(h));
     else
-        return __bfloat162float(__ushort_as_bfloat16(h));
+        return bf16_bits_to_float(h);
 }
 
 template <int BITS, typename ST>

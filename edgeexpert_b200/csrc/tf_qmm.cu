@@ -31,6 +31,8 @@
 // so a lane pair holds both operands of GELU(g)*u after one shuffle.  Routed
 // rows are first gathered into sorted-pair order (gather_rows_kernel) so that
 // every expert's tokens are one contiguous TMA range.
+#include <type_traits>
+
 #include "tf_context.cuh"
 #include "tf_gemv_tc.cuh"
 #include "tf_umma.cuh"
@@ -60,11 +62,14 @@ constexpr uint32_t kQSpin = 1u << 24;
 
 // CG = CTAs per MMA (1: one SM, 128 x N tiles; 2: a CTA pair, 256 x N tiles,
 // each CTA holding half of the weight rows and half of the token rows).
-template <int CG>
+// TN = tokens per tile: 256, or 64 for few tokens per tile (a smaller
+// activation stage buys a deeper load ring and dequantised-operand ring).
+template <int CG, int TN = kTN>
 struct QCfg {
-    static constexpr int kStages = CG == 2 ? 9 : 5;  // load ring: raw weights + token rows + scales
-    static constexpr int kAStages = 2;               // dequantised operand ring
-    static constexpr int kBRows = kTN / CG;          // token rows staged per CTA
+    static constexpr int kTN = TN;
+    static constexpr int kStages = TN == 256 ? (CG == 2 ? 9 : 5) : (CG == 2 ? 14 : 12);  // load ring
+    static constexpr int kAStages = TN == 256 ? 2 : 4;  // dequantised operand ring
+    static constexpr int kBRows = TN / CG;              // token rows staged per CTA
     static constexpr int kBStage = kBRows * 128;
     static constexpr int kSStage = kTM * 4;          // fp16 scale | bias per weight row
     static constexpr int kScaleAhead = 8;            // scale loads in flight (k-blocks)
@@ -94,13 +99,16 @@ struct QmmParams {
     float* y32;  // dense plain mode: fp32 output instead of y (NULL = fp16 y)
     long long ldy;
     int round_gu;  // gate/up rounded to fp16 before GELU (shared expert)
+    int small_tiles;  // grouped: 64-token tiles (few tokens per expert expected)
     uint32_t* err;
 };
 
-template <int CG>
+template <int CG, int TN = kTN>
 struct QShared {
-    static constexpr int S = QCfg<CG>::kStages;
-    static constexpr int SA = QCfg<CG>::kAStages;
+    static constexpr int S = QCfg<CG, TN>::kStages;
+    static constexpr int SA = QCfg<CG, TN>::kAStages;
+    static constexpr int kCG = CG;
+    static constexpr int kTileN = TN;
     uint64_t rawfull[S];  // this CTA's raw weight bytes landed
     uint64_t bfull[S];    // (leader) activation bytes of the pair landed
     uint64_t empty[S];    // MMAs reading the stage's token rows retired (both CTAs)
@@ -121,13 +129,15 @@ struct QShared {
     int gexpert[kMaxGroups];
 };
 
-template <int CG>
+template <int CG, int TN = kTN>
 constexpr size_t qsmem_bytes() {
-    using C = QCfg<CG>;
+    using C = QCfg<CG, TN>;
     return 1024 + (size_t)C::kAStages * kAStage +
-           (size_t)C::kStages * (C::kBStage + kRawStage + C::kSStage) + sizeof(QShared<CG>);
+           (size_t)C::kStages * (C::kBStage + kRawStage + C::kSStage) + sizeof(QShared<CG, TN>);
 }
 static_assert(qsmem_bytes<1>() <= 232448 && qsmem_bytes<2>() <= 232448, "shared memory");
+static_assert(qsmem_bytes<1, 64>() <= 232448, "shared memory");
+static_assert(QCfg<1, 64>::kBRows % kBBoxRows == 0, "a token stage holds whole activation boxes");
 
 struct QTile {
     int feat0;
@@ -141,8 +151,9 @@ __device__ __forceinline__ bool grouped(int mode) { return mode == kGroupedGateU
 // output features covered by one tile
 __device__ __forceinline__ int feat_per_tile(int mode, int cg) { return (gate_up(mode) ? kTM / 2 : kTM) * cg; }
 
-template <int CG>
-__device__ __forceinline__ bool decode_tile(const QmmParams& p, const QShared<CG>& sh, int idx, QTile& t) {
+template <class SH>
+__device__ __forceinline__ bool decode_tile(const QmmParams& p, const SH& sh, int idx, QTile& t) {
+    constexpr int CG = SH::kCG, kTN = SH::kTileN;
     if (idx >= sh.total) return false;
     const int fpt = feat_per_tile(p.mode, CG);
     const int nft = (p.nfeat + fpt - 1) / fpt;
@@ -172,8 +183,8 @@ __device__ __forceinline__ bool decode_tile(const QmmParams& p, const QShared<CG
 }
 
 // Bounded wait that gives up early once another role of this CTA has given up.
-template <int CG>
-__device__ __forceinline__ bool qwait(uint64_t* bar, uint32_t parity, QShared<CG>& sh, uint32_t* err) {
+template <class SH>
+__device__ __forceinline__ bool qwait(uint64_t* bar, uint32_t parity, SH& sh, uint32_t* err) {
     for (uint32_t i = 0; i < kQSpin; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 255u) == 255u && *reinterpret_cast<volatile int*>(&sh.abort_flag)) return false;
@@ -215,18 +226,15 @@ __device__ __forceinline__ void tma_load_3d_u8(void* dst, const void* tmap, int 
         : "memory");
 }
 
-// fp16 bits of a bf16 / fp16 scale or bias
+// fp16 bits of raw bf16 / fp16 scale or bias bits
 template <typename ST>
-__device__ __forceinline__ uint32_t scale_bits_f16(const ST* p);
-template <>
-__device__ __forceinline__ uint32_t scale_bits_f16<__half>(const __half* p) {
-    return (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(p));
+__device__ __forceinline__ uint32_t scale_raw_f16(uint32_t raw) {
+    if constexpr (std::is_same<ST, __half>::value)
+        return raw;
+    else
+        return (uint32_t)__half_as_ushort(__float2half_rn(__uint_as_float(raw << 16)));
 }
-template <>
-__device__ __forceinline__ uint32_t scale_bits_f16<__nv_bfloat16>(const __nv_bfloat16* p) {
-    const unsigned short b = __ldg(reinterpret_cast<const unsigned short*>(p));
-    return (uint32_t)__half_as_ushort(__float2half_rn(__uint_as_float((uint32_t)b << 16)));
-}
+
 
 // 8 nibbles (elements 8c..8c+7, low nibble first) -> 4 half2 in k order,
 // w_k = fma(q_k, s, b) rounded once to fp16.
@@ -250,20 +258,20 @@ struct QCursor {
     QTile t;
 };
 
-template <int CG>
-__device__ __forceinline__ void cursor_start(const QmmParams& p, const QShared<CG>& sh, QCursor& c) {
-    c.idx = blockIdx.x / CG;
+template <class SH>
+__device__ __forceinline__ void cursor_start(const QmmParams& p, const SH& sh, QCursor& c) {
+    c.idx = blockIdx.x / SH::kCG;
     c.kb = 0;
-    c.valid = decode_tile<CG>(p, sh, c.idx, c.t);
+    c.valid = decode_tile(p, sh, c.idx, c.t);
 }
 
-template <int CG>
-__device__ __forceinline__ void cursor_next(const QmmParams& p, const QShared<CG>& sh, QCursor& c, int nkb) {
+template <class SH>
+__device__ __forceinline__ void cursor_next(const QmmParams& p, const SH& sh, QCursor& c, int nkb) {
     if (!c.valid) return;
     if (++c.kb == nkb) {
         c.kb = 0;
-        c.idx += gridDim.x / CG;
-        c.valid = decode_tile<CG>(p, sh, c.idx, c.t);
+        c.idx += gridDim.x / SH::kCG;
+        c.valid = decode_tile(p, sh, c.idx, c.t);
     }
 }
 
@@ -287,9 +295,10 @@ __device__ __forceinline__ const ST* scale_row(const QmmParams& p, const QTile& 
     return reinterpret_cast<const ST*>(base + off) + (size_t)f * (p.K >> 6);
 }
 
-template <typename ST, int CG>
+template <typename ST, int CG, int TN>
 __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant__ QmmParams p) {
-    using Cfg = QCfg<CG>;
+    using Cfg = QCfg<CG, TN>;
+    constexpr int kTN = TN;
     constexpr int S = Cfg::kStages;
     constexpr int SA = Cfg::kAStages;
     extern __shared__ uint8_t q_smem_raw[];
@@ -298,7 +307,7 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
     uint8_t* Bs = As + SA * kAStage;
     uint8_t* Ws = Bs + S * Cfg::kBStage;
     uint32_t* Ss = reinterpret_cast<uint32_t*>(Ws + S * kRawStage);
-    QShared<CG>& sh = *reinterpret_cast<QShared<CG>*>(reinterpret_cast<uint8_t*>(Ss) + S * Cfg::kSStage);
+    QShared<CG, TN>& sh = *reinterpret_cast<QShared<CG, TN>*>(reinterpret_cast<uint8_t*>(Ss) + S * Cfg::kSStage);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rank = CG == 2 ? (int)cluster_ctarank() : 0;
     const bool leader = rank == 0;
@@ -396,8 +405,8 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
         for (int it = 0; it < iters; ++it) {
             const int s = it % S, a = it % SA;
             const uint32_t ps = (uint32_t)(it / S) & 1u, pa = (uint32_t)(it / SA) & 1u;
-            if (!qwait<CG>(&sh.rawfull[s], ps, sh, p.err) || !qwait<CG>(&sh.sfull[s], ps, sh, p.err) ||
-                !qwait<CG>(&sh.aempty[a], pa ^ 1u, sh, p.err))
+            if (!qwait(&sh.rawfull[s], ps, sh, p.err) || !qwait(&sh.sfull[s], ps, sh, p.err) ||
+                !qwait(&sh.aempty[a], pa ^ 1u, sh, p.err))
                 break;
             const uint4 q = lds128(smem_u32(Ws + s * kRawStage + rr * 32 + h * 16));
             const uint32_t sb = Ss[s * kTM + r];
@@ -424,12 +433,15 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
         constexpr int D = Cfg::kScaleAhead;
         const int r0 = (warp - kScaleWarp) * 64 + lane;  // rows r0, r0 + 32
         QCursor lc;
-        cursor_start<CG>(p, sh, lc);
+        cursor_start(p, sh, lc);
         const int units = gridDim.x / CG, u0 = blockIdx.x / CG;
         const int iters = (sh.total > u0 ? (sh.total - u0 + units - 1) / units : 0) * nkb;
         const ST* ps[2] = {nullptr, nullptr};
         const ST* pb[2] = {nullptr, nullptr};
-        auto fetch = [&](uint32_t v[2]) {
+        // the ring holds the raw 16-bit loads: nothing reads a loaded
+        // register until its k-block is consumed D blocks later, so the loads
+        // stay in flight (converting at fetch time would wait for each one)
+        auto fetch = [&](uint32_t v[4]) {
             if (lc.valid && lc.kb == 0) {
 #pragma unroll
                 for (int i = 0; i < 2; ++i) {
@@ -438,12 +450,14 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
                 }
             }
 #pragma unroll
-            for (int i = 0; i < 2; ++i)
-                v[i] = (lc.valid && ps[i]) ? (scale_bits_f16<ST>(ps[i] + lc.kb) | (scale_bits_f16<ST>(pb[i] + lc.kb) << 16))
-                                           : 0u;
-            cursor_next<CG>(p, sh, lc, nkb);
+            for (int i = 0; i < 2; ++i) {
+                const bool ok = lc.valid && ps[i];
+                v[2 * i] = ok ? (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(ps[i] + lc.kb)) : 0u;
+                v[2 * i + 1] = ok ? (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(pb[i] + lc.kb)) : 0u;
+            }
+            cursor_next(p, sh, lc, nkb);
         };
-        uint32_t ring[D][2];
+        uint32_t ring[D][4];
 #pragma unroll
         for (int j = 0; j < D; ++j) fetch(ring[j]);
         bool live = true;
@@ -452,10 +466,11 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
             for (int j = 0; j < D; ++j) {
                 const int it = it0 + j;
                 if (it >= iters) break;
-                const uint32_t c0 = ring[j][0], c1 = ring[j][1];
+                const uint32_t c0 = scale_raw_f16<ST>(ring[j][0]) | (scale_raw_f16<ST>(ring[j][1]) << 16);
+                const uint32_t c1 = scale_raw_f16<ST>(ring[j][2]) | (scale_raw_f16<ST>(ring[j][3]) << 16);
                 fetch(ring[j]);
                 const int s = it % S;
-                if (!qwait<CG>(&sh.sempty[s], (((uint32_t)(it / S)) & 1u) ^ 1u, sh, p.err)) {
+                if (!qwait(&sh.sempty[s], (((uint32_t)(it / S)) & 1u) ^ 1u, sh, p.err)) {
                     live = false;
                     break;
                 }
@@ -472,11 +487,11 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
             prefetch_tmap(&p.wmap0);
             if (gate_up(p.mode)) prefetch_tmap(&p.wmap1);
             QCursor cur;
-            cursor_start<CG>(p, sh, cur);
+            cursor_start(p, sh, cur);
             int it = 0;
             while (cur.valid) {
                 const int s = it % S;
-                if (!qwait<CG>(&sh.empty[s], ((uint32_t)(it / S) & 1u) ^ 1u, sh, p.err)) break;
+                if (!qwait(&sh.empty[s], ((uint32_t)(it / S) & 1u) ^ 1u, sh, p.err)) break;
                 // raw int4 weight rows of this CTA -> local barrier
                 mbar_arrive_expect_tx(&sh.rawfull[s], (uint32_t)kRawStage);
                 uint8_t* w = Ws + s * kRawStage;
@@ -506,7 +521,7 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
                                     &sh.bfull[s]);
                 }
                 ++it;
-                cursor_next<CG>(p, sh, cur, nkb);
+                cursor_next(p, sh, cur, nkb);
             }
         }
         __syncwarp();
@@ -517,9 +532,9 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
             bool live = true;
             for (int idx = blockIdx.x / CG; live; idx += gridDim.x / CG, ++lt) {
                 QTile t;
-                if (!decode_tile<CG>(p, sh, idx, t)) break;
+                if (!decode_tile(p, sh, idx, t)) break;
                 const int acc = lt & 1;
-                if (!qwait<CG>(&sh.tempty[acc], (((uint32_t)lt >> 1) & 1u) ^ 1u, sh, p.err)) {
+                if (!qwait(&sh.tempty[acc], (((uint32_t)lt >> 1) & 1u) ^ 1u, sh, p.err)) {
                     live = false;
                     break;
                 }
@@ -529,8 +544,8 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
                 const uint32_t d = tmem + (uint32_t)(acc * kAccCols);
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
                     const int s = it % S, a = it % SA;
-                    if (!qwait<CG>(&sh.afull[a], (uint32_t)(it / SA) & 1u, sh, p.err) ||
-                        !qwait<CG>(&sh.bfull[s], (uint32_t)(it / S) & 1u, sh, p.err)) {
+                    if (!qwait(&sh.afull[a], (uint32_t)(it / SA) & 1u, sh, p.err) ||
+                        !qwait(&sh.bfull[s], (uint32_t)(it / S) & 1u, sh, p.err)) {
                         live = false;
                         break;
                     }
@@ -587,9 +602,9 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
         int lt = 0;
         for (int idx = blockIdx.x / CG;; idx += gridDim.x / CG, ++lt) {
             QTile t;
-            if (!decode_tile<CG>(p, sh, idx, t)) break;
+            if (!decode_tile(p, sh, idx, t)) break;
             const int acc = lt & 1;
-            if (!qwait<CG>(&sh.tfull[acc], ((uint32_t)lt >> 1) & 1u, sh, p.err)) break;
+            if (!qwait(&sh.tfull[acc], ((uint32_t)lt >> 1) & 1u, sh, p.err)) break;
             tc_fence_after();
             const uint32_t tbase = tmem + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * kAccCols);
             const int f = cta_feat0<CG>(p, t, rank) + (gu ? (row >> 1) : row);
@@ -718,10 +733,11 @@ __global__ void reduce_token_major_kernel(const __half* __restrict__ partials, c
     }
 }
 
-template <typename ST, int CG>
+template <typename ST, int CG, int TN>
 tf_status launch_qmm_cg(tf_context* ctx, const QmmParams& p, cudaStream_t stream, const char* name) {
-    const void* fn = reinterpret_cast<const void*>(&qmm_kernel<ST, CG>);
-    const int smem = (int)qsmem_bytes<CG>();
+    constexpr int kTN = TN;
+    const void* fn = reinterpret_cast<const void*>(&qmm_kernel<ST, CG, TN>);
+    const int smem = (int)qsmem_bytes<CG, TN>();
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return cuda_check(ctx, e, name);
     // persistent: one CTA (pair) per SM (pair); dense problems never need more
@@ -744,19 +760,34 @@ tf_status launch_qmm_cg(tf_context* ctx, const QmmParams& p, cudaStream_t stream
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = CG == 2 ? 1 : 0;
-    return cuda_check(ctx, cudaLaunchKernelEx(&cfg, qmm_kernel<ST, CG>, p), name);
+    return cuda_check(ctx, cudaLaunchKernelEx(&cfg, qmm_kernel<ST, CG, TN>, p), name);
 }
 
 // One SM per tile by default (measured faster on B200: 590 vs 400 TFLOP/s on
 // the 4096 x 2112 x 2816 shape); TFCUDA_QMM_PAIR=1 selects CTA pairs with
 // 2-SM MMAs (same arithmetic).  Read per call.
+// Token tiles of 64 (deeper rings) when 256-token tiles would leave SMs idle
+// (dense) or the caller expects few tokens per expert (grouped, p.small_tiles);
+// TFCUDA_QMM_TN=64 / 256 forces one (read per call).
 tf_status launch_qmm(tf_context* ctx, const QmmParams& p, tf_scale_type st, cudaStream_t stream, const char* name) {
     const char* env = getenv("TFCUDA_QMM_PAIR");
     const bool pair = env && env[0] == '1';
-    if (st == TF_SCALE_BF16)
-        return pair ? launch_qmm_cg<__nv_bfloat16, 2>(ctx, p, stream, name)
-                    : launch_qmm_cg<__nv_bfloat16, 1>(ctx, p, stream, name);
-    return pair ? launch_qmm_cg<__half, 2>(ctx, p, stream, name) : launch_qmm_cg<__half, 1>(ctx, p, stream, name);
+    bool small = p.small_tiles != 0;
+    if (p.mode == kDensePlain || p.mode == kDenseGateUp) {
+        const int fpt = (p.mode == kDenseGateUp ? kTM / 2 : kTM) * (pair ? 2 : 1);
+        small = p.T <= kTN && (long long)((p.nfeat + fpt - 1) / fpt) < ctx->num_sms / (pair ? 2 : 1);
+    }
+    const char* tn = getenv("TFCUDA_QMM_TN");
+    if (tn) small = atoi(tn) == 64;
+    // (64-token tiles only on one SM: a CTA pair would stage 32 token rows per
+    // CTA, less than one 64-row activation box)
+#define TF_QMM_GO(ST_)                                                                                    \
+    return pair ? launch_qmm_cg<ST_, 2, 256>(ctx, p, stream, name)                                        \
+                : (small ? launch_qmm_cg<ST_, 1, 64>(ctx, p, stream, name)                               \
+                         : launch_qmm_cg<ST_, 1, 256>(ctx, p, stream, name));
+    if (st == TF_SCALE_BF16) TF_QMM_GO(__nv_bfloat16)
+    TF_QMM_GO(__half)
+#undef TF_QMM_GO
 }
 
 bool scale_type_ok(tf_scale_type st) { return st == TF_SCALE_BF16 || st == TF_SCALE_F16; }
@@ -984,6 +1015,7 @@ tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64_t expe
     p.y = static_cast<__half*>(act_scratch);
     p.ldy = f;
     p.err = ctx->d_err;
+    p.small_tiles = (uint64_t)P <= 64ull * num_experts ? 1 : 0;  // about 64 pairs per expert or fewer
     // the routed rows in sorted-pair order are staged in the partials buffer
     // (same [T*top_k][d] shape; the down projection overwrites it afterwards)
     if (!make_raw_map(&p.wmap0, pb + off->gate_w, d / 2, f, num_experts, expert_stride) ||
