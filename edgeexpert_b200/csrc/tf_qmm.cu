@@ -60,6 +60,20 @@ constexpr int kTmemCols = 512;
 constexpr int kMaxGroups = 256;
 constexpr uint32_t kQSpin = 1u << 24;
 
+// Optional per-role timestamps of CTA 0 (SM clock), for pipeline studies:
+// built only with -DTF_QMM_TRACE, read back with tf_debug_qmm_trace.
+#ifdef TF_QMM_TRACE
+__device__ unsigned long long g_qmm_trace[8][512];
+#define QTRACE(ev, i)                                                              \
+    do {                                                                           \
+        if (blockIdx.x == 0 && (i) < 512) g_qmm_trace[ev][i] = (unsigned long long)clock64(); \
+    } while (0)
+#else
+#define QTRACE(ev, i) \
+    do {              \
+    } while (0)
+#endif
+
 // CG = CTAs per MMA (1: one SM, 128 x N tiles; 2: a CTA pair, 256 x N tiles,
 // each CTA holding half of the weight rows and half of the token rows).
 // TN = tokens per tile: 256, or 64 for few tokens per tile (a smaller
@@ -405,9 +419,13 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
         for (int it = 0; it < iters; ++it) {
             const int s = it % S, a = it % SA;
             const uint32_t ps = (uint32_t)(it / S) & 1u, pa = (uint32_t)(it / SA) & 1u;
-            if (!qwait(&sh.rawfull[s], ps, sh, p.err) || !qwait(&sh.sfull[s], ps, sh, p.err) ||
-                !qwait(&sh.aempty[a], pa ^ 1u, sh, p.err))
-                break;
+            const bool tr = warp == kAWarp0 && lane == 0;
+            if (!qwait(&sh.rawfull[s], ps, sh, p.err)) break;
+            if (tr) QTRACE(1, it);
+            if (!qwait(&sh.sfull[s], ps, sh, p.err)) break;
+            if (tr) QTRACE(2, it);
+            if (!qwait(&sh.aempty[a], pa ^ 1u, sh, p.err)) break;
+            if (tr) QTRACE(3, it);
             const uint4 q = lds128(smem_u32(Ws + s * kRawStage + rr * 32 + h * 16));
             const uint32_t sb = Ss[s * kTM + r];
             const uint32_t s2 = (sb & 0xFFFFu) * 0x10001u, b2 = (sb >> 16) * 0x10001u;
@@ -422,6 +440,7 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
+                if (warp == kAWarp0) QTRACE(4, it);
                 arrive_leader<CG>(&sh.afull[a]);
                 mbar_arrive(&sh.sempty[s]);
             }
@@ -474,6 +493,7 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
                     live = false;
                     break;
                 }
+                if (warp == kScaleWarp && lane == 0) QTRACE(6, it);
                 Ss[s * kTM + r0] = c0;
                 Ss[s * kTM + r0 + 32] = c1;
                 __syncwarp();
@@ -492,6 +512,7 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
             while (cur.valid) {
                 const int s = it % S;
                 if (!qwait(&sh.empty[s], ((uint32_t)(it / S) & 1u) ^ 1u, sh, p.err)) break;
+                QTRACE(0, it);
                 // raw int4 weight rows of this CTA -> local barrier
                 mbar_arrive_expect_tx(&sh.rawfull[s], (uint32_t)kRawStage);
                 uint8_t* w = Ws + s * kRawStage;
@@ -549,6 +570,7 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
                         live = false;
                         break;
                     }
+                    if (lane == 0) QTRACE(5, it);
                     tc_fence_after();
                     if (lane == 0) {
                         const uint64_t ad = make_sw128_desc(As + a * kAStage);
@@ -605,6 +627,7 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
             if (!decode_tile(p, sh, idx, t)) break;
             const int acc = lt & 1;
             if (!qwait(&sh.tfull[acc], ((uint32_t)lt >> 1) & 1u, sh, p.err)) break;
+            if (warp == 0 && lane == 0) QTRACE(7, lt);
             tc_fence_after();
             const uint32_t tbase = tmem + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * kAccCols);
             const int f = cta_feat0<CG>(p, t, rank) + (gu ? (row >> 1) : row);
@@ -1081,3 +1104,9 @@ tf_status int4_qmm_f32(tf_context* ctx, const void* weights, const void* scales,
 }
 
 }  // namespace tf
+
+#ifdef TF_QMM_TRACE
+extern "C" TF_API int tf_debug_qmm_trace(unsigned long long* out) {
+    return (int)cudaMemcpyFromSymbol(out, g_qmm_trace, sizeof(g_qmm_trace));
+}
+#endif
