@@ -161,13 +161,14 @@ inline bool make_weight_map(CUtensorMap* m, const void* base, uint64_t row_bytes
 // 2-D fp16 activation map [rows][cols] with row pitch `ld` elements, boxes of
 // 64 columns (128 B) x 64 rows in the 128-byte swizzle (the K-major operand
 // layout of tcgen05.mma).  Out-of-range rows read as zero.
-inline bool make_act_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t ld) {
+inline bool make_act_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t ld,
+                         uint32_t box_rows = 64) {
     memset(m, 0, sizeof(*m));
     EncodeTiledFn fn = encode_tiled_fn();
     if (!fn || !aligned16(base) || cols == 0 || rows == 0 || (ld * 2) % 16 || ld < cols) return false;
     cuuint64_t dims[2] = {cols, rows};
     cuuint64_t strides[1] = {ld * 2};
-    cuuint32_t box[2] = {64, 64};
+    cuuint32_t box[2] = {64, box_rows};
     cuuint32_t es[2] = {1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -176,9 +177,9 @@ inline bool make_act_map(CUtensorMap* m, const void* base, uint64_t cols, uint64
 
 // 3-D uint8 map over packed int4 weight rows [depth][rows][row_bytes]
 // (depth = experts of a pool, depth_stride = blob stride), boxes of 32 bytes
-// (one 64-element quantisation group) x 64 rows, unswizzled.
+// (one 64-element quantisation group) x box_rows rows, unswizzled.
 inline bool make_raw_map(CUtensorMap* m, const void* base, uint64_t row_bytes, uint64_t rows, uint64_t depth,
-                         uint64_t depth_stride) {
+                         uint64_t depth_stride, uint32_t box_rows = 64) {
     memset(m, 0, sizeof(*m));
     EncodeTiledFn fn = encode_tiled_fn();
     if (!fn || !aligned16(base) || row_bytes % 32 || rows == 0 || depth == 0) return false;
@@ -186,7 +187,7 @@ inline bool make_raw_map(CUtensorMap* m, const void* base, uint64_t row_bytes, u
     if (ds % 16 || ds >= (1ull << 40)) return false;
     cuuint64_t dims[3] = {row_bytes, rows, depth};
     cuuint64_t strides[2] = {row_bytes, ds};
-    cuuint32_t box[3] = {32, 64, 1};
+    cuuint32_t box[3] = {32, box_rows, 1};
     cuuint32_t es[3] = {1, 1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,

@@ -92,7 +92,8 @@ struct QCfg {
 enum QMode : int { kDensePlain = 0, kDenseGateUp = 1, kGroupedGateUp = 2, kGroupedDown = 3 };
 
 struct QmmParams {
-    CUtensorMap xmap;   // activations [rows][K] fp16
+    CUtensorMap xmap;   // activations [rows][K] fp16, 64-row boxes
+    CUtensorMap xmap256;  // the same with 256-row boxes (one TMA per k-block for a full tile), if xbig
     CUtensorMap wmap0;  // packed weights (plain / gate), [depth][rows][K/2] uint8
     CUtensorMap wmap1;  // packed weights (up)
     int mode;
@@ -114,6 +115,8 @@ struct QmmParams {
     long long ldy;
     int round_gu;  // gate/up rounded to fp16 before GELU (shared expert)
     int small_tiles;  // grouped: 64-token tiles (few tokens per expert expected)
+    int xbig;         // xmap256 is valid
+    int wbig;         // plain modes: wmap0 has 128-row boxes (one TMA per k-block)
     uint32_t* err;
 };
 
@@ -336,10 +339,10 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
             mbar_init(&sh.bfull[s], CG);
             mbar_init(&sh.empty[s], 1);
             mbar_init(&sh.sfull[s], kScaleWarps);
-            mbar_init(&sh.sempty[s], kAWarps);
+            mbar_init(&sh.sempty[s], kAWarps / SA);
         }
         for (int a = 0; a < SA; ++a) {
-            mbar_init(&sh.afull[a], kAWarps * CG);
+            mbar_init(&sh.afull[a], (kAWarps / SA) * CG);
             mbar_init(&sh.aempty[a], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -412,35 +415,57 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
         // k-blocks of this CTA: nkb per tile, tiles blockIdx/CG, + units, ...
         const int units = gridDim.x / CG, u0 = blockIdx.x / CG;
         const int iters = (sh.total > u0 ? (sh.total - u0 + units - 1) / units : 0) * nkb;
-        const int at = tid - kAWarp0 * 32;  // 0..255
-        const int r = at >> 1, h = at & 1;
-        // raw rows: plain = r; gate/up = gate rows 0-63, up rows 64-127
-        const int rr = gate_up(p.mode) ? ((r & 1) * 64 + (r >> 1)) : r;
-        for (int it = 0; it < iters; ++it) {
-            const int s = it % S, a = it % SA;
+        // SA groups of kAWarps / SA warps: group a dequantises the k-blocks
+        // it = a, a + SA, ... (operand buffer a), so SA k-blocks are in
+        // flight at once and each group's barrier round trips overlap the
+        // others' work; a thread covers kUnits (row, half-row) units.
+        constexpr int kGW = kAWarps / SA;          // warps per group
+        constexpr int kUnits = 256 / (32 * kGW);   // 16-byte raw units per thread
+        const int grp = (warp - kAWarp0) / kGW;
+        const int gt = ((warp - kAWarp0) % kGW) * 32 + lane;
+        for (int it = grp; it < iters; it += SA) {
+            const int s = it % S, a = grp;
             const uint32_t ps = (uint32_t)(it / S) & 1u, pa = (uint32_t)(it / SA) & 1u;
-            const bool tr = warp == kAWarp0 && lane == 0;
+            const bool tr = (warp - kAWarp0) % kGW == 0 && lane == 0;
             if (!qwait(&sh.rawfull[s], ps, sh, p.err)) break;
             if (tr) QTRACE(1, it);
             if (!qwait(&sh.sfull[s], ps, sh, p.err)) break;
             if (tr) QTRACE(2, it);
             if (!qwait(&sh.aempty[a], pa ^ 1u, sh, p.err)) break;
             if (tr) QTRACE(3, it);
-            const uint4 q = lds128(smem_u32(Ws + s * kRawStage + rr * 32 + h * 16));
-            const uint32_t sb = Ss[s * kTM + r];
-            const uint32_t s2 = (sb & 0xFFFFu) * 0x10001u, b2 = (sb >> 16) * 0x10001u;
             const uint32_t dst = smem_u32(As + a * kAStage);
-            const uint32_t wv[4] = {q.x, q.y, q.z, q.w};
+            uint4 q[kUnits];
+            uint32_t sb[kUnits];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                uint32_t o[4];
-                dq8_natural(wv[i], s2, b2, o);
-                sts128(dst + sw128(r, h * 4 + i), o[0], o[1], o[2], o[3]);
+            for (int u = 0; u < kUnits; ++u) {
+                const int at = gt + u * 32 * kGW;  // 0..255
+                const int r = at >> 1, h = at & 1;
+                // raw rows: plain = r; gate/up = gate rows 0-63, up rows 64-127
+                const int rr = gate_up(p.mode) ? ((r & 1) * 64 + (r >> 1)) : r;
+                q[u] = lds128(smem_u32(Ws + s * kRawStage + rr * 32 + h * 16));
+                sb[u] = Ss[s * kTM + r];
+            }
+#pragma unroll
+            for (int u = 0; u < kUnits; ++u) {
+                const int at = gt + u * 32 * kGW;
+                const int r = at >> 1, h = at & 1;
+                const uint32_t s2 = (sb[u] & 0xFFFFu) * 0x10001u, b2 = (sb[u] >> 16) * 0x10001u;
+                const uint32_t wv[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    uint32_t o[4];
+                    dq8_natural(wv[i], s2, b2, o);
+                    sts128(dst + sw128(r, h * 4 + i), o[0], o[1], o[2], o[3]);
+                }
             }
             fence_proxy_async_smem();
+            // the leader's warps also wait for the stage's token rows, so a
+            // full afull implies a full bfull: the MMA thread (the serial step
+            // of the pipeline) then waits on one barrier per k-block
+            if (leader && !qwait(&sh.bfull[s], ps, sh, p.err)) break;
             __syncwarp();
             if (lane == 0) {
-                if (warp == kAWarp0) QTRACE(4, it);
+                if ((warp - kAWarp0) % kGW == 0) QTRACE(4, it);
                 arrive_leader<CG>(&sh.afull[a]);
                 mbar_arrive(&sh.sempty[s]);
             }
@@ -493,7 +518,6 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
                     live = false;
                     break;
                 }
-                if (warp == kScaleWarp && lane == 0) QTRACE(6, it);
                 Ss[s * kTM + r0] = c0;
                 Ss[s * kTM + r0 + 32] = c1;
                 __syncwarp();
@@ -504,6 +528,7 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
         // ================= TMA loader (one thread) =================
         if (lane == 0) {
             prefetch_tmap(&p.xmap);
+            if (p.xbig) prefetch_tmap(&p.xmap256);
             prefetch_tmap(&p.wmap0);
             if (gate_up(p.mode)) prefetch_tmap(&p.wmap1);
             QCursor cur;
@@ -520,6 +545,8 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
                 if (gate_up(p.mode)) {
                     tma_load_3d_u8(w, &p.wmap0, cur.kb * 32, fb, z, &sh.rawfull[s]);
                     tma_load_3d_u8(w + kRawStage / 2, &p.wmap1, cur.kb * 32, fb, z, &sh.rawfull[s]);
+                } else if (p.wbig) {
+                    tma_load_3d_u8(w, &p.wmap0, cur.kb * 32, fb, z, &sh.rawfull[s]);  // 128 rows
                 } else {
                     tma_load_3d_u8(w, &p.wmap0, cur.kb * 32, fb, z, &sh.rawfull[s]);
                     tma_load_3d_u8(w + kRawStage / 2, &p.wmap0, cur.kb * 32, fb + 64, z, &sh.rawfull[s]);
@@ -535,6 +562,12 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
                     mbar_arrive_expect_tx_cluster(lb, (uint32_t)(nbox * kBBoxRows * 128));
                     for (int i = 0; i < nbox; ++i)
                         tma_load_2d_pair(dst + i * kBBoxRows * 128, &p.xmap, cur.kb * 64, brow0 + i * kBBoxRows, lb);
+                } else if (Cfg::kBRows >= 256 && p.xbig && nbox > 1) {
+                    // one 256-row box: the same swizzled image as four 64-row boxes,
+                    // one TMA issue instead of four (the loader thread is the
+                    // pipeline's serial step at one k-block per iteration)
+                    mbar_arrive_expect_tx(&sh.bfull[s], 256u * 128u);
+                    tma_load_2d(dst, &p.xmap256, cur.kb * 64, brow0, &sh.bfull[s]);
                 } else {
                     mbar_arrive_expect_tx(&sh.bfull[s], (uint32_t)(nbox * kBBoxRows * 128));
                     for (int i = 0; i < nbox; ++i)
@@ -565,8 +598,7 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
                 const uint32_t d = tmem + (uint32_t)(acc * kAccCols);
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
                     const int s = it % S, a = it % SA;
-                    if (!qwait(&sh.afull[a], (uint32_t)(it / SA) & 1u, sh, p.err) ||
-                        !qwait(&sh.bfull[s], (uint32_t)(it / S) & 1u, sh, p.err)) {
+                    if (!qwait(&sh.afull[a], (uint32_t)(it / SA) & 1u, sh, p.err)) {
                         live = false;
                         break;
                     }
@@ -591,6 +623,7 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
                             umma_commit(&sh.empty[s]);
                             umma_commit(&sh.aempty[a]);
                         }
+                        QTRACE(7, it);
                     }
                     __syncwarp();
                 }
@@ -627,7 +660,6 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
             if (!decode_tile(p, sh, idx, t)) break;
             const int acc = lt & 1;
             if (!qwait(&sh.tfull[acc], ((uint32_t)lt >> 1) & 1u, sh, p.err)) break;
-            if (warp == 0 && lane == 0) QTRACE(7, lt);
             tc_fence_after();
             const uint32_t tbase = tmem + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * kAccCols);
             const int f = cta_feat0<CG>(p, t, rank) + (gu ? (row >> 1) : row);
@@ -818,8 +850,9 @@ bool scale_type_ok(tf_scale_type st) { return st == TF_SCALE_BF16 || st == TF_SC
 
 // Dense weight matrix [n][k] as a one-deep raw map plus scale/bias addresses.
 bool dense_weights(QmmParams& p, CUtensorMap* m, const void* w, uint32_t rows, uint32_t k, const void* sc,
-                   const void* bi, int which) {
-    if (!make_raw_map(m, w, k / 2, rows, 1, 0)) return false;
+                   const void* bi, int which, bool big_box = false) {
+    if (!make_raw_map(m, w, k / 2, rows, 1, 0, big_box ? 128u : 64u)) return false;
+    if (big_box) p.wbig = 1;
     if (which == 0) {
         p.os0 = reinterpret_cast<uint64_t>(sc);
         p.ob0 = reinterpret_cast<uint64_t>(bi);
@@ -881,8 +914,10 @@ static tf_status qmm_dense(tf_context* ctx, const void* weights, const void* sca
     p.K = (int)k;
     p.nfeat = (int)n;
     p.T = (int)t;
-    if (!dense_weights(p, &p.wmap0, weights, n, k, scales, biases, 0) || !make_act_map(&p.xmap, x, k, t, x_stride))
+    if (!dense_weights(p, &p.wmap0, weights, n, k, scales, biases, 0, n >= 128) ||
+        !make_act_map(&p.xmap, x, k, t, x_stride))
         return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: tensor map rejected", name);
+    p.xbig = t >= 256 && make_act_map(&p.xmap256, x, k, t, x_stride, 256) ? 1 : 0;
     p.y = static_cast<__half*>(y);
     p.y32 = y32;
     p.ldy = y_stride;
@@ -933,6 +968,7 @@ tf_status tf_prefill_shared_expert(tf_context* ctx, const void* x, uint32_t x_st
         !dense_weights(p, &p.wmap1, up->weights, f, d, up->scales, up->biases, 1) ||
         !make_act_map(&p.xmap, x, d, t, x_stride))
         return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: tensor map rejected", name);
+    p.xbig = t >= 256 && make_act_map(&p.xmap256, x, d, t, x_stride, 256) ? 1 : 0;
     p.y = static_cast<__half*>(act_scratch);
     p.ldy = f;
     p.round_gu = 1;
@@ -944,9 +980,10 @@ tf_status tf_prefill_shared_expert(tf_context* ctx, const void* x, uint32_t x_st
     q.K = (int)f;
     q.nfeat = (int)d;
     q.T = (int)t;
-    if (!dense_weights(q, &q.wmap0, down->weights, d, f, down->scales, down->biases, 0) ||
+    if (!dense_weights(q, &q.wmap0, down->weights, d, f, down->scales, down->biases, 0, d >= 128) ||
         !make_act_map(&q.xmap, act_scratch, f, t, f))
         return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: tensor map rejected", name);
+    q.xbig = t >= 256 && make_act_map(&q.xmap256, act_scratch, f, t, f, 256) ? 1 : 0;
     q.y = static_cast<__half*>(y);
     q.ldy = y_stride;
     q.err = ctx->d_err;
@@ -1038,13 +1075,13 @@ tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64_t expe
     p.y = static_cast<__half*>(act_scratch);
     p.ldy = f;
     p.err = ctx->d_err;
-    p.small_tiles = (uint64_t)P <= 64ull * num_experts ? 1 : 0;  // about 64 pairs per expert or fewer
     // the routed rows in sorted-pair order are staged in the partials buffer
     // (same [T*top_k][d] shape; the down projection overwrites it afterwards)
     if (!make_raw_map(&p.wmap0, pb + off->gate_w, d / 2, f, num_experts, expert_stride) ||
         !make_raw_map(&p.wmap1, pb + off->up_w, d / 2, f, num_experts, expert_stride) ||
         !make_act_map(&p.xmap, route_partials, d, P, d))
         return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: tensor map rejected", name);
+    p.xbig = P >= 256 && make_act_map(&p.xmap256, route_partials, d, P, d, 256) ? 1 : 0;
     QmmParams q = p;
     q.mode = kGroupedDown;
     q.K = (int)f;
@@ -1053,9 +1090,11 @@ tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64_t expe
     q.ob0 = off->down_b;
     q.y = static_cast<__half*>(route_partials);
     q.ldy = d;
-    if (!make_raw_map(&q.wmap0, pb + off->down_w, f / 2, d, num_experts, expert_stride) ||
+    q.wbig = d >= 128 ? 1 : 0;
+    if (!make_raw_map(&q.wmap0, pb + off->down_w, f / 2, d, num_experts, expert_stride, q.wbig ? 128u : 64u) ||
         !make_act_map(&q.xmap, act_scratch, f, P, f))
         return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: tensor map rejected", name);
+    q.xbig = P >= 256 && make_act_map(&q.xmap256, act_scratch, f, P, f, 256) ? 1 : 0;
     {
         const long long n = (long long)P * (d / 8);
         const int grid = (int)std::min<long long>((n + 255) / 256, (long long)ctx->num_sms * 8);
