@@ -211,6 +211,7 @@ tf_status tf_context_create(int device, tf_context** out) {
     e = e ? e : cudaMalloc(&ctx->d_err, 4 * sizeof(uint32_t));
     e = e ? e : cudaMalloc(&ctx->d_logits, sizeof(float) * kMaxRouterExperts * 64);
     e = e ? e : cudaMalloc(&ctx->d_rt_logits, sizeof(float) * kRtLogitsCap);
+    e = e ? e : cudaMalloc(&ctx->d_qmm_part, sizeof(float) * kQmmPartCap);
     e = e ? e : cudaMalloc(&ctx->d_ticket, sizeof(unsigned int) * 64);
     e = e ? e : cudaMalloc(&ctx->d_flags, sizeof(unsigned int) * 32 * 1024);
     e = e ? e : cudaMalloc(&ctx->d_idx, sizeof(uint32_t) * kMaxTopKDecode);
@@ -243,6 +244,7 @@ void tf_context_destroy(tf_context* ctx) {
     cudaFree(ctx->d_err);
     cudaFree(ctx->d_logits);
     cudaFree(ctx->d_rt_logits);
+    cudaFree(ctx->d_qmm_part);
     cudaFree(ctx->d_ticket);
     cudaFree(ctx->d_flags);
     cudaFree(ctx->d_idx);

@@ -20,6 +20,7 @@ struct tf_context {
     uint32_t* d_err = nullptr;         // error bits raised by kernels
     float* d_logits = nullptr;         // [kMaxRouterExperts] router logits
     float* d_rt_logits = nullptr;      // [kRtLogitsCap] batched-router logits scratch
+    float* d_qmm_part = nullptr;       // [kQmmPartCap] split-K partial sums of the dense GEMMs
     unsigned int* d_ticket = nullptr;  // router selection ticket (always left 0), barrier count
     unsigned int* d_flags = nullptr;   // fused-layer barrier release flags, 128 B apart
     uint32_t* d_idx = nullptr;         // [8] decode routing ids
@@ -45,6 +46,7 @@ constexpr int kMaxFs = 16384;
 constexpr int kMaxTopKDecode = 8;
 constexpr int kMaxLmTokens = 256;
 constexpr size_t kRtLogitsCap = 1u << 20;  // floats: 4096 tokens x 256 experts
+constexpr size_t kQmmPartCap = 8u << 20;   // floats (32 MB)
 constexpr int kCandCap = 65536;  // 256 tiles x 256 candidates: a 262144-entry vocabulary
 
 inline tf_status fail(tf_context* ctx, tf_status s, const char* fmt, ...) {

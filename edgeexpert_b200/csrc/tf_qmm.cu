@@ -116,6 +116,9 @@ struct QmmParams {
     int round_gu;  // gate/up rounded to fp16 before GELU (shared expert)
     int small_tiles;  // grouped: 64-token tiles (few tokens per expert expected)
     int xbig;         // xmap256 is valid
+    int ksplit;       // dense: K split over this many CTAs (tiles x ksplit jobs), >= 1
+    float* part;      // ksplit > 1: fp32 partials [ksplit][T][ldp] (gate/up interleaved per feature)
+    long long ldp;
     int wbig;         // plain modes: wmap0 has 128-row boxes (one TMA per k-block)
     uint32_t* err;
 };
@@ -161,6 +164,8 @@ struct QTile {
     int row0;  // dense: first token row; grouped: first sorted pair
     int cnt;   // tokens / pairs in the tile
     int expert;
+    int split;  // dense split-K: which K slice
+    int kb0;    // first k-block of the slice
 };
 
 __device__ __forceinline__ bool gate_up(int mode) { return mode == kDenseGateUp || mode == kGroupedGateUp; }
@@ -175,11 +180,14 @@ __device__ __forceinline__ bool decode_tile(const QmmParams& p, const SH& sh, in
     const int fpt = feat_per_tile(p.mode, CG);
     const int nft = (p.nfeat + fpt - 1) / fpt;
     if (!grouped(p.mode)) {
-        const int tt = idx / nft, ft = idx - tt * nft;
+        const int tile = idx / p.ksplit, sp = idx - tile * p.ksplit;
+        const int tt = tile / nft, ft = tile - tt * nft;
         t.feat0 = ft * fpt;
         t.row0 = tt * kTN;
         t.cnt = min(kTN, p.T - t.row0);
         t.expert = 0;
+        t.split = sp;
+        t.kb0 = sp * ((p.K >> 6) / p.ksplit);
         return true;
     }
     // largest g with prefix[g] <= idx
@@ -196,6 +204,8 @@ __device__ __forceinline__ bool decode_tile(const QmmParams& p, const SH& sh, in
     t.row0 = sh.gstart[g] + tt * q;
     t.cnt = min(q, c - tt * q);
     t.expert = sh.gexpert[g];
+    t.split = 0;
+    t.kb0 = 0;
     return true;
 }
 
@@ -328,7 +338,7 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rank = CG == 2 ? (int)cluster_ctarank() : 0;
     const bool leader = rank == 0;
-    const int nkb = p.K >> 6;
+    const int nkb = (p.K >> 6) / p.ksplit;  // k-blocks per job
     const int fpt = feat_per_tile(p.mode, CG);
     const int nft = (p.nfeat + fpt - 1) / fpt;
 
@@ -356,7 +366,7 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
     if (!grouped(p.mode)) {
         if (tid == 0) {
             sh.ng = 0;
-            sh.total = ((p.T + kTN - 1) / kTN) * nft;
+            sh.total = ((p.T + kTN - 1) / kTN) * nft * p.ksplit;
         }
     } else if (warp == 0) {
         const int ng = min((int)*p.n_groups, kMaxGroups);
@@ -496,8 +506,8 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
 #pragma unroll
             for (int i = 0; i < 2; ++i) {
                 const bool ok = lc.valid && ps[i];
-                v[2 * i] = ok ? (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(ps[i] + lc.kb)) : 0u;
-                v[2 * i + 1] = ok ? (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(pb[i] + lc.kb)) : 0u;
+                v[2 * i] = ok ? (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(ps[i] + lc.t.kb0 + lc.kb)) : 0u;
+                v[2 * i + 1] = ok ? (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(pb[i] + lc.t.kb0 + lc.kb)) : 0u;
             }
             cursor_next(p, sh, lc, nkb);
         };
@@ -543,13 +553,13 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
                 uint8_t* w = Ws + s * kRawStage;
                 const int z = cur.t.expert, fb = cta_feat0<CG>(p, cur.t, rank);
                 if (gate_up(p.mode)) {
-                    tma_load_3d_u8(w, &p.wmap0, cur.kb * 32, fb, z, &sh.rawfull[s]);
-                    tma_load_3d_u8(w + kRawStage / 2, &p.wmap1, cur.kb * 32, fb, z, &sh.rawfull[s]);
+                    tma_load_3d_u8(w, &p.wmap0, (cur.t.kb0 + cur.kb) * 32, fb, z, &sh.rawfull[s]);
+                    tma_load_3d_u8(w + kRawStage / 2, &p.wmap1, (cur.t.kb0 + cur.kb) * 32, fb, z, &sh.rawfull[s]);
                 } else if (p.wbig) {
-                    tma_load_3d_u8(w, &p.wmap0, cur.kb * 32, fb, z, &sh.rawfull[s]);  // 128 rows
+                    tma_load_3d_u8(w, &p.wmap0, (cur.t.kb0 + cur.kb) * 32, fb, z, &sh.rawfull[s]);  // 128 rows
                 } else {
-                    tma_load_3d_u8(w, &p.wmap0, cur.kb * 32, fb, z, &sh.rawfull[s]);
-                    tma_load_3d_u8(w + kRawStage / 2, &p.wmap0, cur.kb * 32, fb + 64, z, &sh.rawfull[s]);
+                    tma_load_3d_u8(w, &p.wmap0, (cur.t.kb0 + cur.kb) * 32, fb, z, &sh.rawfull[s]);
+                    tma_load_3d_u8(w + kRawStage / 2, &p.wmap0, (cur.t.kb0 + cur.kb) * 32, fb + 64, z, &sh.rawfull[s]);
                 }
                 // this CTA's token rows -> the leader's barrier
                 const int N = max(16, (cur.t.cnt + 15) & ~15);
@@ -561,17 +571,17 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
                     const uint32_t lb = mapa_shared(&sh.bfull[s], 0);
                     mbar_arrive_expect_tx_cluster(lb, (uint32_t)(nbox * kBBoxRows * 128));
                     for (int i = 0; i < nbox; ++i)
-                        tma_load_2d_pair(dst + i * kBBoxRows * 128, &p.xmap, cur.kb * 64, brow0 + i * kBBoxRows, lb);
+                        tma_load_2d_pair(dst + i * kBBoxRows * 128, &p.xmap, (cur.t.kb0 + cur.kb) * 64, brow0 + i * kBBoxRows, lb);
                 } else if (Cfg::kBRows >= 256 && p.xbig && nbox > 1) {
                     // one 256-row box: the same swizzled image as four 64-row boxes,
                     // one TMA issue instead of four (the loader thread is the
                     // pipeline's serial step at one k-block per iteration)
                     mbar_arrive_expect_tx(&sh.bfull[s], 256u * 128u);
-                    tma_load_2d(dst, &p.xmap256, cur.kb * 64, brow0, &sh.bfull[s]);
+                    tma_load_2d(dst, &p.xmap256, (cur.t.kb0 + cur.kb) * 64, brow0, &sh.bfull[s]);
                 } else {
                     mbar_arrive_expect_tx(&sh.bfull[s], (uint32_t)(nbox * kBBoxRows * 128));
                     for (int i = 0; i < nbox; ++i)
-                        tma_load_2d(dst + i * kBBoxRows * 128, &p.xmap, cur.kb * 64, brow0 + i * kBBoxRows,
+                        tma_load_2d(dst + i * kBBoxRows * 128, &p.xmap, (cur.t.kb0 + cur.kb) * 64, brow0 + i * kBBoxRows,
                                     &sh.bfull[s]);
                 }
                 ++it;
@@ -668,7 +678,14 @@ __global__ void __launch_bounds__(kQThreads, 1) qmm_kernel(const __grid_constant
                 float v[32];
                 tmem_ld32(tbase + (uint32_t)(cc * 32), v);
                 const int colbase = cc * 32;
-                if (gu) {
+                if (p.part) {
+                    // split-K slice: raw fp32 sums, gate/up interleaved by row
+                    const long long pc = gu ? 2ll * cta_feat0<CG>(p, t, rank) + row : (long long)f;
+                    float* pr = p.part + ((long long)t.split * p.T + t.row0 + colbase) * p.ldp + pc;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (fok && colbase + j < t.cnt) pr[(long long)j * p.ldp] = v[j];
+                } else if (gu) {
                     const bool even = (lane & 1) == 0;
 #pragma unroll
                     for (int jj = 0; jj < 16; ++jj) {
@@ -800,7 +817,8 @@ tf_status launch_qmm_cg(tf_context* ctx, const QmmParams& p, cudaStream_t stream
     long long units = ctx->num_sms / CG;
     if (p.mode == kDensePlain || p.mode == kDenseGateUp) {
         const int fpt = (p.mode == kDenseGateUp ? kTM / 2 : kTM) * CG;
-        units = std::min<long long>(units, (long long)((p.T + kTN - 1) / kTN) * ((p.nfeat + fpt - 1) / fpt));
+        units = std::min<long long>(units,
+                                    (long long)((p.T + kTN - 1) / kTN) * ((p.nfeat + fpt - 1) / fpt) * p.ksplit);
     }
     if (units <= 0) return TF_OK;
     cudaLaunchConfig_t cfg = {};
@@ -821,12 +839,10 @@ tf_status launch_qmm_cg(tf_context* ctx, const QmmParams& p, cudaStream_t stream
 // One SM per tile by default (measured faster on B200: 590 vs 400 TFLOP/s on
 // the 4096 x 2112 x 2816 shape); TFCUDA_QMM_PAIR=1 selects CTA pairs with
 // 2-SM MMAs (same arithmetic).  Read per call.
-// Token tiles of 64 (deeper rings) when 256-token tiles would leave SMs idle
-// (dense) or the caller expects few tokens per expert (grouped, p.small_tiles);
-// TFCUDA_QMM_TN=64 / 256 forces one (read per call).
-tf_status launch_qmm(tf_context* ctx, const QmmParams& p, tf_scale_type st, cudaStream_t stream, const char* name) {
-    const char* env = getenv("TFCUDA_QMM_PAIR");
-    const bool pair = env && env[0] == '1';
+// Token tiles of 64 (deeper rings) when one 256-token tile would leave SMs
+// idle (dense) or the caller expects few tokens per expert (grouped,
+// p.small_tiles); TFCUDA_QMM_TN=64 / 256 forces one (read per call).
+bool use_small_tiles(const tf_context* ctx, const QmmParams& p, bool pair) {
     bool small = p.small_tiles != 0;
     if (p.mode == kDensePlain || p.mode == kDenseGateUp) {
         const int fpt = (p.mode == kDenseGateUp ? kTM / 2 : kTM) * (pair ? 2 : 1);
@@ -834,8 +850,19 @@ tf_status launch_qmm(tf_context* ctx, const QmmParams& p, tf_scale_type st, cuda
     }
     const char* tn = getenv("TFCUDA_QMM_TN");
     if (tn) small = atoi(tn) == 64;
-    // (64-token tiles only on one SM: a CTA pair would stage 32 token rows per
-    // CTA, less than one 64-row activation box)
+    return small && !pair;  // 64-token tiles only on one SM (see QCfg)
+}
+
+bool use_pair() {
+    const char* env = getenv("TFCUDA_QMM_PAIR");
+    return env && env[0] == '1';
+}
+
+tf_status launch_qmm(tf_context* ctx, const QmmParams& p0, tf_scale_type st, cudaStream_t stream, const char* name) {
+    QmmParams p = p0;
+    if (p.ksplit < 1) p.ksplit = 1;
+    const bool pair = use_pair();
+    const bool small = use_small_tiles(ctx, p, pair);
 #define TF_QMM_GO(ST_)                                                                                    \
     return pair ? launch_qmm_cg<ST_, 2, 256>(ctx, p, stream, name)                                        \
                 : (small ? launch_qmm_cg<ST_, 1, 64>(ctx, p, stream, name)                               \
@@ -843,6 +870,77 @@ tf_status launch_qmm(tf_context* ctx, const QmmParams& p, tf_scale_type st, cuda
     if (st == TF_SCALE_BF16) TF_QMM_GO(__nv_bfloat16)
     TF_QMM_GO(__half)
 #undef TF_QMM_GO
+}
+
+// Split-K for a dense problem whose tiles leave most SMs idle (the shared
+// expert and the LM head at a few tokens): K slices of >= 3 k-blocks over
+// extra CTAs, fp32 partials in the context scratch, then qmm_split_reduce
+// adds the slices in slice order. Returns 1 (no split) otherwise;
+// TFCUDA_QMM_SPLIT=0 turns it off (read per call).
+int choose_ksplit(const tf_context* ctx, const QmmParams& p) {
+    const char* env = getenv("TFCUDA_QMM_SPLIT");
+    if (env && env[0] == '0') return 1;
+    const bool pair = use_pair();
+    if (pair) return 1;
+    const int tn = use_small_tiles(ctx, p, pair) ? 64 : kTN;
+    const int fpt = p.mode == kDenseGateUp ? kTM / 2 : kTM;
+    const long long tiles = (long long)((p.T + tn - 1) / tn) * ((p.nfeat + fpt - 1) / fpt);
+    const long long ldp = p.mode == kDenseGateUp ? 2ll * p.nfeat : p.nfeat;
+    const int nkb = p.K >> 6;
+    int best = 1;
+    for (int sp = 2; sp <= 16; ++sp) {
+        if (nkb % sp || nkb / sp < 3) continue;
+        if (tiles * sp > (long long)ctx->num_sms * 3 / 2) break;
+        if ((long long)sp * p.T * ldp > (long long)kQmmPartCap) break;
+        best = sp;
+    }
+    return best;
+}
+
+__global__ void __launch_bounds__(256) qmm_split_reduce_kernel(const float* __restrict__ part, int S, int T,
+                                                               int nfeat, long long ldp, int gu, int round_gu,
+                                                               __half* __restrict__ y, float* __restrict__ y32,
+                                                               long long ldy) {
+    const long long n = (long long)T * nfeat;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const int t = (int)(i / nfeat), f = (int)(i - (long long)t * nfeat);
+        if (gu) {
+            float g = 0.f, u = 0.f;
+            for (int sp = 0; sp < S; ++sp) {
+                const float2 gv = *reinterpret_cast<const float2*>(part + ((long long)sp * T + t) * ldp + 2 * f);
+                g += gv.x;
+                u += gv.y;
+            }
+            if (round_gu) {
+                g = __half2float(__float2half_rn(g));
+                u = __half2float(__float2half_rn(u));
+            }
+            y[(long long)t * ldy + f] = __float2half_rn(gelu_tanh(g) * u);
+        } else {
+            float v = 0.f;
+            for (int sp = 0; sp < S; ++sp) v += part[((long long)sp * T + t) * ldp + f];
+            if (y32)
+                y32[(long long)t * ldy + f] = v;
+            else
+                y[(long long)t * ldy + f] = __float2half_rn(v);
+        }
+    }
+}
+
+// One dense launch, split over K when that fills the GPU better.
+tf_status launch_dense(tf_context* ctx, QmmParams p, tf_scale_type st, cudaStream_t stream, const char* name) {
+    p.ksplit = choose_ksplit(ctx, p);
+    if (p.ksplit == 1) return launch_qmm(ctx, p, st, stream, name);
+    p.part = ctx->d_qmm_part;
+    p.ldp = p.mode == kDenseGateUp ? 2ll * p.nfeat : p.nfeat;
+    tf_status rc = launch_qmm(ctx, p, st, stream, name);
+    if (rc != TF_OK) return rc;
+    const long long n = (long long)p.T * p.nfeat;
+    const int grid = (int)std::min<long long>((n + 255) / 256, (long long)ctx->num_sms * 8);
+    qmm_split_reduce_kernel<<<grid, 256, 0, stream>>>(p.part, p.ksplit, p.T, p.nfeat, p.ldp,
+                                                      p.mode == kDenseGateUp ? 1 : 0, p.round_gu, p.y, p.y32,
+                                                      p.ldy);
+    return cuda_check(ctx, cudaGetLastError(), name);
 }
 
 bool scale_type_ok(tf_scale_type st) { return st == TF_SCALE_BF16 || st == TF_SCALE_F16; }
@@ -922,7 +1020,7 @@ static tf_status qmm_dense(tf_context* ctx, const void* weights, const void* sca
     p.y32 = y32;
     p.ldy = y_stride;
     p.err = ctx->d_err;
-    return launch_qmm(ctx, p, st, static_cast<cudaStream_t>(stream), name);
+    return launch_dense(ctx, p, st, static_cast<cudaStream_t>(stream), name);
 }
 
 tf_status tf_int4_qmm(tf_context* ctx, const void* weights, const void* scales, const void* biases, const void* x,
@@ -973,7 +1071,7 @@ tf_status tf_prefill_shared_expert(tf_context* ctx, const void* x, uint32_t x_st
     p.ldy = f;
     p.round_gu = 1;
     p.err = ctx->d_err;
-    tf_status rc = launch_qmm(ctx, p, st, s, name);
+    tf_status rc = launch_dense(ctx, p, st, s, name);
     if (rc != TF_OK) return rc;
     QmmParams q{};
     q.mode = kDensePlain;
@@ -987,7 +1085,7 @@ tf_status tf_prefill_shared_expert(tf_context* ctx, const void* x, uint32_t x_st
     q.y = static_cast<__half*>(y);
     q.ldy = y_stride;
     q.err = ctx->d_err;
-    return launch_qmm(ctx, q, st, s, name);
+    return launch_dense(ctx, q, st, s, name);
 }
 
 tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64_t expert_stride, uint32_t num_experts,
