@@ -15,6 +15,8 @@
 // the norms, a split-KV grid sized to the SM count for attention (each CTA
 // reads one KV head's chunk once for all the query heads that share it), and
 // the ring-streamed GEMV / tcgen05 GEMM with fp32 output for the LM head.
+#include <initializer_list>
+
 #include "tf_context.cuh"
 #include "tf_gemv_tc.cuh"
 
@@ -139,38 +141,57 @@ __global__ void __launch_bounds__(kAttnThreads) attention_partial_kernel(
     const int seg_w = hd < 256 ? hd : 256;
     const bool lane_on = lane * 8 < seg_w;
 
-    // scores: warp w takes positions w, w+8, ...; lane holds 8 consecutive dims
-    for (int j = warp; j < np; j += kAttnWarps) {
-        const __half* kr = Kt + (long long)(p0 + j) * pstride;
-        float s[kAttnMaxGroup];
+    // scores: warp w takes positions w, w+8, ...; lane holds 8 consecutive
+    // dims.  Four positions' rows are loaded before any is used, so each warp
+    // keeps four 16-byte loads per lane in flight (the chunk is latency-bound
+    // otherwise: one dependent round trip per position).
+    constexpr int kPf = 4;
+    for (int j0 = warp; j0 < np; j0 += kPf * kAttnWarps) {
+        uint4 kv4[kPf][kAttnMaxHeadDim / 256];
 #pragma unroll
-        for (int g = 0; g < kAttnMaxGroup; ++g) s[g] = 0.f;
-        for (int seg = 0; seg < nseg; ++seg) {
-            if (!lane_on) continue;
-            const int e0 = seg * 256 + lane * 8;
-            const uint4 kv4 = __ldcs(reinterpret_cast<const uint4*>(kr + e0));
-            const __half2* kh = reinterpret_cast<const __half2*>(&kv4);
-            float kf[8];
+        for (int k = 0; k < kPf; ++k) {
+            const int j = j0 + k * kAttnWarps;
+            const __half* kr = Kt + (long long)(p0 + min(j, np - 1)) * pstride;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const float2 f2 = __half22float2(kh[u]);
-                kf[2 * u] = f2.x;
-                kf[2 * u + 1] = f2.y;
+            for (int seg = 0; seg < kAttnMaxHeadDim / 256; ++seg)
+                kv4[k][seg] = (seg < nseg && lane_on && j < np)
+                                  ? __ldcs(reinterpret_cast<const uint4*>(kr + seg * 256 + lane * 8))
+                                  : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int k = 0; k < kPf; ++k) {
+            const int j = j0 + k * kAttnWarps;
+            if (j >= np) break;
+            float s[kAttnMaxGroup];
+#pragma unroll
+            for (int g = 0; g < kAttnMaxGroup; ++g) s[g] = 0.f;
+#pragma unroll
+            for (int seg = 0; seg < kAttnMaxHeadDim / 256; ++seg) {
+                if (seg >= nseg || !lane_on) continue;
+                const int e0 = seg * 256 + lane * 8;
+                const __half2* kh = reinterpret_cast<const __half2*>(&kv4[k][seg]);
+                float kf[8];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float2 f2 = __half22float2(kh[u]);
+                    kf[2 * u] = f2.x;
+                    kf[2 * u + 1] = f2.y;
+                }
+#pragma unroll
+                for (int g = 0; g < kAttnMaxGroup; ++g) {
+                    if (g >= G) break;
+                    const float* qg = qs + g * hd + e0;
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) s[g] = fmaf(qg[u], kf[u], s[g]);
+                }
             }
 #pragma unroll
             for (int g = 0; g < kAttnMaxGroup; ++g) {
                 if (g >= G) break;
-                const float* qg = qs + g * hd + e0;
-#pragma unroll
-                for (int u = 0; u < 8; ++u) s[g] = fmaf(qg[u], kf[u], s[g]);
+                float v = s[g];
+                for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (lane == 0) sc[g * kAttnMaxChunk + j] = v * scale;
             }
-        }
-#pragma unroll
-        for (int g = 0; g < kAttnMaxGroup; ++g) {
-            if (g >= G) break;
-            float v = s[g];
-            for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0) sc[g * kAttnMaxChunk + j] = v * scale;
         }
     }
     __syncthreads();
@@ -202,22 +223,33 @@ __global__ void __launch_bounds__(kAttnThreads) attention_partial_kernel(
             for (int u = 0; u < 8; ++u) acc[g][u] = 0.f;
         const int e0 = seg * 256 + lane * 8;
         if (lane_on) {
-            for (int j = warp; j < np; j += kAttnWarps) {
-                const uint4 vv = __ldcs(reinterpret_cast<const uint4*>(Vt + (long long)(p0 + j) * pstride + e0));
-                const __half2* vh = reinterpret_cast<const __half2*>(&vv);
-                float vf[8];
+            for (int j0 = warp; j0 < np; j0 += kPf * kAttnWarps) {
+                uint4 vv[kPf];  // four rows in flight, used in position order
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const float2 f2 = __half22float2(vh[u]);
-                    vf[2 * u] = f2.x;
-                    vf[2 * u + 1] = f2.y;
+                for (int k = 0; k < kPf; ++k) {
+                    const int j = j0 + k * kAttnWarps;
+                    vv[k] = j < np ? __ldcs(reinterpret_cast<const uint4*>(Vt + (long long)(p0 + j) * pstride + e0))
+                                   : make_uint4(0, 0, 0, 0);
                 }
 #pragma unroll
-                for (int g = 0; g < kAttnMaxGroup; ++g) {
-                    if (g >= G) break;
-                    const float e = sc[g * kAttnMaxChunk + j];
+                for (int k = 0; k < kPf; ++k) {
+                    const int j = j0 + k * kAttnWarps;
+                    if (j >= np) break;
+                    const __half2* vh = reinterpret_cast<const __half2*>(&vv[k]);
+                    float vf[8];
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) acc[g][u] = fmaf(e, vf[u], acc[g][u]);
+                    for (int u = 0; u < 4; ++u) {
+                        const float2 f2 = __half22float2(vh[u]);
+                        vf[2 * u] = f2.x;
+                        vf[2 * u + 1] = f2.y;
+                    }
+#pragma unroll
+                    for (int g = 0; g < kAttnMaxGroup; ++g) {
+                        if (g >= G) break;
+                        const float e = sc[g * kAttnMaxChunk + j];
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) acc[g][u] = fmaf(e, vf[u], acc[g][u]);
+                    }
                 }
             }
         }
@@ -358,6 +390,158 @@ __global__ void __launch_bounds__(kNormThreads) layer_tail_kernel(
     }
 }
 
+// ---------------------------------------------------------------------------
+// Register-resident forms of the three row norms for d % 8 == 0 and 16-byte
+// aligned rows: a thread holds 8 consecutive elements of every operand (one
+// 16-byte load each, issued together), so a row costs one memory round trip
+// and the block reductions instead of one pass over memory per step.  Same
+// element-wise arithmetic and roundings as the kernels above.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void ld8h(const __half* p, bool on, float v[8]) {
+    uint4 q = on ? __ldg(reinterpret_cast<const uint4*>(p)) : make_uint4(0, 0, 0, 0);
+    const __half2* h = reinterpret_cast<const __half2*>(&q);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(h[j]);
+        v[2 * j] = f.x;
+        v[2 * j + 1] = f.y;
+    }
+}
+__device__ __forceinline__ void ld8b(const __nv_bfloat16* p, bool on, float v[8]) {
+    uint4 q = on ? __ldg(reinterpret_cast<const uint4*>(p)) : make_uint4(0, 0, 0, 0);
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        v[2 * j] = bf16_bits_to_float(w[j] & 0xFFFFu);
+        v[2 * j + 1] = bf16_bits_to_float(w[j] >> 16);
+    }
+}
+__device__ __forceinline__ void st8h(__half* p, const float v[8]) {
+    uint4 q;
+    __half2* h = reinterpret_cast<__half2*>(&q);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+    *reinterpret_cast<uint4*>(p) = q;
+}
+__device__ __forceinline__ float rh(float v) { return __half2float(__float2half_rn(v)); }
+
+__global__ void __launch_bounds__(1024) rmsnorm_vec_kernel(const __half* __restrict__ x, long long ldx,
+                                                           const __nv_bfloat16* __restrict__ w,
+                                                           __half* __restrict__ out, long long ldo, int d,
+                                                           float eps) {
+    __shared__ float red[32];
+    const int i = threadIdx.x * 8;
+    const bool on = i < d;
+    float xv[8], wv[8];
+    ld8h(x + (long long)blockIdx.x * ldx + i, on, xv);
+    if (w) ld8b(w + i, on, wv);
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc = fmaf(xv[j], xv[j], acc);
+    const float inv = rms_inv_of(block_sum(acc, red), d, eps);
+    if (!on) return;
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = w ? (xv[j] * inv) * wv[j] : xv[j] * inv;
+    st8h(out + (long long)blockIdx.x * ldo + i, o);
+}
+
+__global__ void __launch_bounds__(1024) post_attn_setup_vec_kernel(
+    __half* __restrict__ hidden, const __half* __restrict__ attn, __half* __restrict__ dense_x,
+    __half* __restrict__ routed_x, __half* __restrict__ router_x, const __nv_bfloat16* __restrict__ w_post_attn,
+    const __nv_bfloat16* __restrict__ w_pre_ffn, const __nv_bfloat16* __restrict__ w_pre_ffn2, int d, float eps) {
+    __shared__ float red[32];
+    const long long r = blockIdx.x;
+    const int i = threadIdx.x * 8;
+    const bool on = i < d;
+    float a[8], h[8], wa[8], w1[8], w2[8];
+    ld8h(attn + r * d + i, on, a);
+    ld8h(hidden + r * d + i, on, h);
+    ld8b(w_post_attn + i, on, wa);
+    if (dense_x) ld8b(w_pre_ffn + i, on, w1);
+    if (routed_x) ld8b(w_pre_ffn2 + i, on, w2);
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc = fmaf(a[j], a[j], acc);
+    const float inv_a = rms_inv_of(block_sum(acc, red), d, eps);
+    acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        h[j] = rh(h[j] + rh(a[j] * inv_a * wa[j]));
+        acc = fmaf(h[j], h[j], acc);
+    }
+    const float inv_h = rms_inv_of(block_sum(acc, red), d, eps);
+    if (!on) return;
+    st8h(hidden + r * d + i, h);
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) h[j] *= inv_h;
+    if (dense_x) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = h[j] * w1[j];
+        st8h(dense_x + r * d + i, o);
+    }
+    if (routed_x) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = h[j] * w2[j];
+        st8h(routed_x + r * d + i, o);
+    }
+    if (router_x) st8h(router_x + r * d + i, h);
+}
+
+__global__ void __launch_bounds__(1024) layer_tail_vec_kernel(
+    const __half* __restrict__ h2, const __half* __restrict__ h1, __half* __restrict__ hidden,
+    const __nv_bfloat16* __restrict__ w1, const __nv_bfloat16* __restrict__ w2, const __nv_bfloat16* __restrict__ w,
+    float layer_scalar, int d, float eps) {
+    __shared__ float red[32];
+    const long long r = blockIdx.x;
+    const int i = threadIdx.x * 8;
+    const bool on = i < d;
+    float t[8], v2[8], hv[8], a1[8], a2[8], a3[8];
+    ld8h(h1 + r * d + i, on, t);
+    ld8h(h2 + r * d + i, on, v2);
+    ld8h(hidden + r * d + i, on, hv);
+    if (w1) ld8b(w1 + i, on, a1);
+    ld8b(w2 + i, on, a2);
+    ld8b(w + i, on, a3);
+    if (w1) {
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc = fmaf(t[j], t[j], acc);
+        const float inv1 = rms_inv_of(block_sum(acc, red), d, eps);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) t[j] = rh(t[j] * inv1 * a1[j]);
+    }
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc = fmaf(v2[j], v2[j], acc);
+    const float inv2 = rms_inv_of(block_sum(acc, red), d, eps);
+    acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        t[j] = rh(t[j] + rh(v2[j] * inv2 * a2[j]));
+        acc = fmaf(t[j], t[j], acc);
+    }
+    const float inv12 = rms_inv_of(block_sum(acc, red), d, eps);
+    if (!on) return;
+    const float hs = rh(layer_scalar);
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = rh(hv[j] + rh(t[j] * inv12 * a3[j])) * hs;
+    st8h(hidden + r * d + i, o);
+}
+
+// the register-resident kernels' preconditions: whole 16-byte vectors per row
+inline bool vec_rows_ok(uint32_t d, std::initializer_list<const void*> ptrs, std::initializer_list<uint64_t> strides) {
+    if (d % 8 || d > 8192) return false;
+    for (const void* p : ptrs)
+        if (p && (reinterpret_cast<uintptr_t>(p) & 15u)) return false;
+    for (uint64_t st : strides)
+        if (st % 8) return false;
+    return true;
+}
+inline unsigned vec_threads(uint32_t d) { return (unsigned)(((d / 8) + 31) / 32 * 32); }
+
 template <typename ST>
 __global__ void embed_int4_kernel(const uint8_t* __restrict__ table, const ST* __restrict__ S,
                                   const ST* __restrict__ B, const uint32_t* __restrict__ tokens, int vocab, int d,
@@ -462,9 +646,14 @@ tf_status tf_rmsnorm(tf_context* ctx, const void* x, uint32_t x_stride, const vo
     if (rows == 0) return TF_OK;
     if (!x || !out) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
     if (!aligned2(x) || !aligned2(out) || !aligned2(weight)) return fail(ctx, TF_ERR_MISALIGNED, "%s: misaligned", name);
-    rmsnorm_kernel<<<rows, kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const __half*>(x), x_stride, static_cast<const __nv_bfloat16*>(weight), static_cast<__half*>(out),
-        out_stride, (int)d, eps);
+    if (vec_rows_ok(d, {x, out, weight}, {x_stride, out_stride}))
+        rmsnorm_vec_kernel<<<rows, vec_threads(d), 0, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const __half*>(x), x_stride, static_cast<const __nv_bfloat16*>(weight),
+            static_cast<__half*>(out), out_stride, (int)d, eps);
+    else
+        rmsnorm_kernel<<<rows, kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const __half*>(x), x_stride, static_cast<const __nv_bfloat16*>(weight),
+            static_cast<__half*>(out), out_stride, (int)d, eps);
     return cuda_check(ctx, cudaGetLastError(), name);
 }
 
@@ -557,6 +746,13 @@ tf_status tf_post_attn_setup(tf_context* ctx, void* hidden, const void* attn, vo
     if (rows == 0) return TF_OK;
     if (!hidden || !attn || !w_post_attn || (dense_x && !w_pre_ffn) || (routed_x && !w_pre_ffn2))
         return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
+    if (vec_rows_ok(d, {hidden, attn, dense_x, routed_x, router_x, w_post_attn, w_pre_ffn, w_pre_ffn2}, {}))
+        post_attn_setup_vec_kernel<<<rows, vec_threads(d), 0, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<__half*>(hidden), static_cast<const __half*>(attn), static_cast<__half*>(dense_x),
+            static_cast<__half*>(routed_x), static_cast<__half*>(router_x),
+            static_cast<const __nv_bfloat16*>(w_post_attn), static_cast<const __nv_bfloat16*>(w_pre_ffn),
+            static_cast<const __nv_bfloat16*>(w_pre_ffn2), (int)d, eps);
+    else
     post_attn_setup_kernel<<<rows, kNormThreads, sizeof(__half) * d, static_cast<cudaStream_t>(stream)>>>(
         static_cast<__half*>(hidden), static_cast<const __half*>(attn), static_cast<__half*>(dense_x),
         static_cast<__half*>(routed_x), static_cast<__half*>(router_x),
@@ -574,6 +770,12 @@ tf_status tf_layer_tail(tf_context* ctx, const void* h2, const void* h1, void* h
     if (d == 0 || d > 16384) return fail(ctx, TF_ERR_UNSUPPORTED_SHAPE, "%s: 0 < d <= 16384", name);
     if (rows == 0) return TF_OK;
     if (!h2 || !h1 || !hidden || !w_post_ffn2 || !w_post_ffn) return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
+    if (vec_rows_ok(d, {h2, h1, hidden, w_post_ffn1, w_post_ffn2, w_post_ffn}, {}))
+        layer_tail_vec_kernel<<<rows, vec_threads(d), 0, static_cast<cudaStream_t>(stream)>>>(
+            static_cast<const __half*>(h2), static_cast<const __half*>(h1), static_cast<__half*>(hidden),
+            static_cast<const __nv_bfloat16*>(w_post_ffn1), static_cast<const __nv_bfloat16*>(w_post_ffn2),
+            static_cast<const __nv_bfloat16*>(w_post_ffn), layer_scalar, (int)d, eps);
+    else
     layer_tail_kernel<<<rows, kNormThreads, sizeof(float) * d, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __half*>(h2), static_cast<const __half*>(h1), static_cast<__half*>(hidden),
         static_cast<const __nv_bfloat16*>(w_post_ffn1), static_cast<const __nv_bfloat16*>(w_post_ffn2),
