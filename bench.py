@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--no-stack", action="store_true", help="moe: skip the full decoder-stack sub-record")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="expert-parallel exchange at N > 1: peer-memory stores (default) or NCCL all-to-alls")
+    ap.add_argument("--overlap-shared", type=int, default=1,
+                    help="moe: run each layer's shared expert on a forked stream beside the routed path (1) or after it (0)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--workload", choices=["moe", "decode", "gemv", "batched", "prefill", "ep"], default="moe",
                     help="moe (default) = config-4 MoE decode step at batch 256/32/1 through 30 layers, experts "
@@ -835,12 +837,21 @@ def run_moe(a, rank, world, local_rank):
                                   torch.empty(E, 3, **i32), torch.empty(1, **i32), torch.empty(E, 4, **i32),
                                   torch.empty(1, **i32))
         launches = 0
+        side = torch.cuda.Stream(device=dev) if a.overlap_shared else None
 
         def step(xx):
             nonlocal launches
             launches = 0
             for l in range(L):
                 Lw, x = layers[l], xx[l]
+                if T and side is not None and not fused_b1:
+                    # the shared expert depends only on the layer input: it runs on a
+                    # forked stream while the router, the grouping and the exchange
+                    # (latency-bound, few SMs) run on the main one; joined at the
+                    # layer's end
+                    side.wait_stream(stream)
+                    shared.encode(x, Lw.shared_gate, Lw.shared_up, Lw.shared_down, sact, ys[l], T, stream=side)
+                    launches += 3
                 if fused_b1:
                     moe_decode_layer(Lw, x[0], x[0], h2[l][0], out_indices=idx[l][0], out_weights=wts[l][0],
                                      stream=stream, context=ctx, c_layer=c_layers[l])
@@ -858,7 +869,9 @@ def run_moe(a, rank, world, local_rank):
                     grouped.encode(Lw.experts, routes, x, act, part, T, TOPK, stream=stream)
                     PrefillMoE.encode_reduce_token_major(part, wts[l], h2[l], T, TOPK, D, stream=stream, context=ctx)
                     launches += 7
-                if T:
+                if T and side is not None:
+                    stream.wait_stream(side)
+                elif T:
                     shared.encode(x, Lw.shared_gate, Lw.shared_up, Lw.shared_down, sact, ys[l], T, stream=stream)
                     launches += 3
 
@@ -1066,7 +1079,8 @@ def run_moe(a, rank, world, local_rank):
                    "exchange": (f"{a.exchange} (fixed capacity, no host readback)" if world > 1 else "none"),
                    "l2": "weights per step (%.1f GB per GPU) exceed L2 (126 MB); no flush needed" %
                          (head["hbm_bytes_per_gpu"] / 1e9),
-                   "outputs": "routed h2 and shared y per layer, kept separate"},
+                   "outputs": "routed h2 and shared y per layer, kept separate",
+                   "shared_expert": "forked stream beside the routed path" if a.overlap_shared else "after the routed path"},
         "batches": {str(b): results[b] for b in batches},
         "tok_s": head["tok_s"],
         "e2e": {"value": head["tok_s_e2e"], "unit": "tok/s", "h2d_bytes_per_step": head["h2d_bytes_per_step"],
