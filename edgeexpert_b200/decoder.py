@@ -248,7 +248,7 @@ class Decoder:
     is allocated here once; `step` only enqueues work."""
 
     def __init__(self, weights: DecoderWeights, T: int, cache: KVCache, context: Context | None = None,
-                 device=None, ep_layers: list | None = None):
+                 device=None, ep_layers: list | None = None, overlap_shared: bool = True):
         """`ep_layers` (one ExpertParallelMoE per layer) routes the experts over
         the process group; the router, shared expert and attention stay local.
         T may be 0 on a rank that only serves experts."""
@@ -289,6 +289,8 @@ class Decoder:
             self.rpart = torch.empty(Ta * cfg.top_k, d, **f16)
         self.c_moe = [L.moe.as_c() for L in weights.layers]
         self.launches = 0
+        # the shared expert's stream (None: run it after the routed path)
+        self.side = torch.cuda.Stream(device=dev) if overlap_shared else None
 
     # int4 projection of T rows (row t of y at y + t*y_stride): the GEMV
     # engines for up to 8 tokens, the tcgen05 GEMM beyond
@@ -333,45 +335,57 @@ class Decoder:
                                    d, cfg.eps, stream=stream)
         self.launches += 1
 
+    def _shared(self, M, T, stream):
+        from .moe import SharedExpertRuntime
+        from .prefill import PrefillSharedExpert
+        if T == 1:
+            SharedExpertRuntime(4, self.ctx).encode(self.dense_x[0], M.shared_gate, M.shared_up, M.shared_down,
+                                                    self.h1[0], self.sact[0], stream=stream)
+            self.launches += 2
+        elif T:
+            PrefillSharedExpert(self.ctx).encode(self.dense_x, M.shared_gate, M.shared_up, M.shared_down, self.sact,
+                                                 self.h1, T, stream=stream)
+            self.launches += 2
+
     def _moe(self, i: int, stream):
-        """h1 = shared(dense_x), h2 = routed(routed_x) with the router on router_x."""
-        from .moe import SharedExpertRuntime, moe_decode_layer
-        from .prefill import PrefillGroupedRoutedMoE, PrefillMoE, PrefillRouter, PrefillSharedExpert, route_sort
+        """h1 = shared(dense_x), h2 = routed(routed_x) with the router on router_x.
+        The shared expert reads only dense_x, so it runs on a stream forked from
+        `stream` beside the routed path (which is latency-bound for most of its
+        length) and the two join before the layer tail."""
+        from .moe import moe_decode_layer
+        from .prefill import PrefillGroupedRoutedMoE, PrefillMoE, PrefillRouter, route_sort
         cfg, M, T, ctx = self.cfg, self.w.layers[i].moe, self.T, self.ctx
+        main = stream if stream is not None else torch.cuda.current_stream()
+        fork = T > 0 and self.side is not None
+        if fork:
+            self.side.wait_stream(main)
+            self._shared(M, T, self.side)
         if self.ep is not None:
             if T:
                 PrefillRouter(ctx).encode_gemma4_block(M.router_w, M.router_s, M.router_b, self.router_x, M.eff_scale,
                                                        M.per_expert_scale, self.idx, self.wts, T, cfg.num_experts,
-                                                       cfg.d, cfg.top_k, stream=stream)
-            self.ep[i].forward(self.routed_x[:T], self.idx[:T], self.wts[:T], self.h2[:T], stream=stream)
-            if T == 1:
-                SharedExpertRuntime(4, ctx).encode(self.dense_x[0], M.shared_gate, M.shared_up, M.shared_down,
-                                                   self.h1[0], self.sact[0], stream=stream)
-            elif T:
-                PrefillSharedExpert(ctx).encode(self.dense_x, M.shared_gate, M.shared_up, M.shared_down, self.sact,
-                                                self.h1, T, stream=stream)
-            self.launches += 13
-            return
-        if T == 1:
-            # the reference's shared expert runs on dense_x and the routed
-            # experts on routed_x: shared separately, then the fused routed layer
-            SharedExpertRuntime(4, ctx).encode(self.dense_x[0], M.shared_gate, M.shared_up, M.shared_down,
-                                               self.h1[0], self.sact[0], stream=stream)
+                                                       cfg.d, cfg.top_k, stream=main)
+            self.ep[i].forward(self.routed_x[:T], self.idx[:T], self.wts[:T], self.h2[:T], stream=main)
+            self.launches += 11
+        elif T == 1:
             moe_decode_layer(M, self.router_x[0], self.routed_x[0], self.h2[0], out_indices=self.idx[0],
-                             out_weights=self.wts[0], stream=stream, context=ctx, c_layer=self._routed_only(i))
-            self.launches += 5
-            return
-        PrefillRouter(ctx).encode_gemma4_block(M.router_w, M.router_s, M.router_b, self.router_x, M.eff_scale,
-                                               M.per_expert_scale, self.idx, self.wts, T, cfg.num_experts, cfg.d,
-                                               cfg.top_k, stream=stream)
-        route_sort(self.idx, self.wts, T, cfg.top_k, cfg.num_experts, 16, stream=stream, context=ctx, out=self.routes)
-        PrefillGroupedRoutedMoE(ctx).encode(M.experts, self.routes, self.routed_x, self.ract, self.rpart, T,
-                                            cfg.top_k, stream=stream)
-        PrefillMoE.encode_reduce_token_major(self.rpart, self.wts, self.h2, T, cfg.top_k, cfg.d, stream=stream,
-                                             context=ctx)
-        PrefillSharedExpert(ctx).encode(self.dense_x, M.shared_gate, M.shared_up, M.shared_down, self.sact, self.h1,
-                                        T, stream=stream)
-        self.launches += 10
+                             out_weights=self.wts[0], stream=main, context=ctx, c_layer=self._routed_only(i))
+            self.launches += 3
+        else:
+            PrefillRouter(ctx).encode_gemma4_block(M.router_w, M.router_s, M.router_b, self.router_x, M.eff_scale,
+                                                   M.per_expert_scale, self.idx, self.wts, T, cfg.num_experts, cfg.d,
+                                                   cfg.top_k, stream=main)
+            route_sort(self.idx, self.wts, T, cfg.top_k, cfg.num_experts, 16, stream=main, context=ctx,
+                       out=self.routes)
+            PrefillGroupedRoutedMoE(ctx).encode(M.experts, self.routes, self.routed_x, self.ract, self.rpart, T,
+                                                cfg.top_k, stream=main)
+            PrefillMoE.encode_reduce_token_major(self.rpart, self.wts, self.h2, T, cfg.top_k, cfg.d, stream=main,
+                                                 context=ctx)
+            self.launches += 8
+        if fork:
+            main.wait_stream(self.side)
+        else:
+            self._shared(M, T, main)
 
     def _routed_only(self, i: int):
         """The C layer struct with the shared expert switched off (rows = 0)."""
