@@ -44,7 +44,7 @@ constexpr int kGsStage = 2 * kGsBox;                // 4 groups x 240 rows (30 K
 constexpr int kGsMaxR = 7;
 constexpr int kGsThreads = 32 * (1 + kGsConsumers);
 constexpr int kGsMaxGroups = 256;
-constexpr size_t kGsSmemLimit = 232448;
+constexpr size_t kGsSmemLimit = 232448 - 1024;  // room for the static s_tok array
 constexpr uint32_t kGsSpin = 1u << 21;
 
 struct GsParams {
@@ -165,12 +165,15 @@ __device__ __forceinline__ float scale_at(const uint2& packed, int j) {
 // outside the subnormal range); rows ntok..nrows-1 are zero.  MODE 0 gathers
 // hidden rows by the pairs' tokens, MODE 1 reads the pass's act rows.
 __device__ __forceinline__ void stage_words_gather(const GsParams& p, uint32_t* xs, int ws, int p0, int ntok,
-                                                   int nrows, int ctid) {
+                                                   int nrows, int ctid, uint32_t* s_tok) {
     const int octets = p.K / 8;
     const int n = nrows * octets;
     const __half2 sixteenth = __float2half2_rn(0.0625f);
-    constexpr int U = 4;
+    constexpr int U = 12;  // 16 rows x 352 octets / 480 threads: every load of a restage in flight at once
     constexpr int NT = kGsConsumers * 32;
+    // the pass's token ids first (one load each), so no row load waits on a pair load
+    if (p.mode == 0 && ctid < ntok) s_tok[ctid] = p.pairs[p0 + ctid].token;
+    consumer_bar();
     for (int base = ctid; base < n; base += U * NT) {
         uint4 raw[U];
 #pragma unroll
@@ -181,7 +184,7 @@ __device__ __forceinline__ void stage_words_gather(const GsParams& p, uint32_t* 
                 const int tk = i / octets, o = i - tk * octets;
                 if (tk < ntok) {
                     if (p.mode == 0) {
-                        const uint32_t tok = p.pairs[p0 + tk].token;
+                        const uint32_t tok = s_tok[tk];
                         if (tok < (uint32_t)p.T)
                             raw[u] = __ldcg(reinterpret_cast<const uint4*>(p.x + (long long)tok * p.x_stride) + o);
                         else if (o == 0 && p.err)
@@ -211,21 +214,27 @@ __device__ __forceinline__ void stage_words_gather(const GsParams& p, uint32_t* 
     }
 }
 
-// Per (group, token) {-1024 * sum of the staged values, true sum}: one warp per
-// (token, group); odd pairs hold x/16, so the true sum is s + 15 * odd.
+// Per (token, group): {-1024 * sum(staged), sum(x)}; the odd pairs were staged
+// divided by 16, so sum(x) = sum(staged) + 15 * sum(staged odd pairs).  One
+// thread per item (32 staged words = eight 16-byte loads, started at a
+// thread-dependent chunk so a quarter-warp reads distinct banks).
 __device__ __forceinline__ void stage_xc(const uint32_t* xs, int ws, int ntok, int ngK, int TP, float2* xc, int ctid) {
-    const int warp = ctid >> 5, lane = ctid & 31;
-    for (int i = warp; i < ntok * ngK; i += kGsConsumers) {
+    for (int i = ctid; i < ntok * ngK; i += kGsConsumers * 32) {
         const int tk = i / ngK, G = i - tk * ngK;
-        const uint32_t w = xs[tk * ws + G * 32 + lane];
-        const __half2 h = *reinterpret_cast<const __half2*>(&w);
-        float s = __low2float(h) + __high2float(h);
-        float odd = (lane & 1) ? s : 0.f;
-        for (int off = 16; off; off >>= 1) {
-            s += __shfl_xor_sync(0xffffffffu, s, off);
-            odd += __shfl_xor_sync(0xffffffffu, odd, off);
+        const uint4* w = reinterpret_cast<const uint4*>(xs + tk * ws + G * 32);
+        float ev = 0.f, od = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const uint4 v = w[(k + i) & 7];
+            const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+            const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+            const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&v.z));
+            const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&v.w));
+            ev += (a.x + a.y) + (c.x + c.y);  // words 4q, 4q+2: even pairs
+            od += (b.x + b.y) + (d.x + d.y);  // words 4q+1, 4q+3: odd pairs (staged / 16)
         }
-        if (lane == 0) xc[G * TP + tk] = make_float2(-1024.f * s, s + 15.f * odd);
+        const float s = ev + od;
+        xc[G * TP + tk] = make_float2(-1024.f * s, s + 15.f * od);
     }
 }
 
@@ -239,6 +248,7 @@ __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __g
     float2* xc = reinterpret_cast<float2*>(sm + L.xc);
     GsBars& sh = *reinterpret_cast<GsBars*>(sm + L.bars);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    __shared__ uint32_t s_tok[32];  // the staged pass's token ids
     const int ngK = p.K >> 6, nst = (ngK + 3) >> 2, R = p.R, TP = p.TP;
     const int ws = x_words_stride(p.K);
     const int rows_out = p.mode == 0 ? p.F : p.D;  // output rows per expert
@@ -339,7 +349,7 @@ __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __g
             if (J.group != staged_group || J.pass != staged_pass) {
                 consumer_bar();  // every consumer is done with the previous token rows
                 if (ctid == 0) sh.stop = *reinterpret_cast<volatile int*>(&sh.abort_flag);
-                stage_words_gather(p, xs, ws, p0, ntok, nblk * 8, ctid);
+                stage_words_gather(p, xs, ws, p0, ntok, nblk * 8, ctid, s_tok);
                 consumer_bar();
                 stage_xc(xs, ws, nblk * 8, ngK, TP, xc, ctid);
                 consumer_bar();
@@ -378,10 +388,14 @@ __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __g
                         const uint2 wa = *reinterpret_cast<const uint2*>(sbase + offA + o);
                         const uint2 wb = *reinterpret_cast<const uint2*>(sbase + offB + o);
                         uint32_t pa0[4], pa1[4], pb0[4], pb1[4];
+#if defined(GS_VARIANT) && GS_VARIANT == 1
+                        for (int k = 0; k < 4; ++k) { pa0[k] = wa.x >> k; pa1[k] = wa.y >> k; pb0[k] = wb.x >> k; pb1[k] = wb.y >> k; }
+#else
                         dq4_folded(wa.x, pa0);
                         dq4_folded(wa.y, pa1);
                         dq4_folded(wb.x, pb0);
                         dq4_folded(wb.y, pb1);
+#endif
 #pragma unroll
                         for (int b = 0; b < 2; ++b) {
                             if (b < nblk) {
@@ -392,16 +406,26 @@ __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __g
                                 const float xs0 = xv.y, xs1 = xv.w;
                                 // the chain starts at -1024 * sum(staged x) and ends at the group's dot
                                 float c[4] = {xv.x, xv.z, xv.x, xv.z};
+#if defined(GS_VARIANT) && GS_VARIANT >= 2
+                                c[0] += __uint_as_float(pa0[0] ^ pb0[1] ^ x0.x ^ x1.w);
+                                c[1] += __uint_as_float(pa1[2] ^ pb1[3] ^ x0.z ^ x1.y);
+#else
                                 mma16816(c, pa0[0], pb0[0], pa0[1], pb0[1], x0.x, x0.y);
                                 mma16816(c, pa0[2], pb0[2], pa0[3], pb0[3], x0.z, x0.w);
                                 mma16816(c, pa1[0], pb1[0], pa1[1], pb1[1], x1.x, x1.y);
                                 mma16816(c, pa1[2], pb1[2], pa1[3], pb1[3], x1.z, x1.w);
+#endif
                                 const float sa = scale_at<ST>(scl[0], j), ba = scale_at<ST>(scl[1], j);
                                 const float sb = scale_at<ST>(scl[2], j), bb = scale_at<ST>(scl[3], j);
+#if defined(GS_VARIANT) && GS_VARIANT == 3
+                                acc[b][0] += c[0] + sa + ba;
+                                acc[b][1] += c[1] + sb + bb + xs0 + xs1;
+#else
                                 acc[b][0] = fmaf(sa, c[0], fmaf(ba, xs0, acc[b][0]));
                                 acc[b][1] = fmaf(sa, c[1], fmaf(ba, xs1, acc[b][1]));
                                 acc[b][2] = fmaf(sb, c[2], fmaf(bb, xs0, acc[b][2]));
                                 acc[b][3] = fmaf(sb, c[3], fmaf(bb, xs1, acc[b][3]));
+#endif
                             }
                         }
                     }
@@ -461,7 +485,10 @@ template <typename ST>
 tf_status launch_gs(tf_context* ctx, GsParams p, cudaStream_t s, const char* name) {
     // tokens per pass: 16 when the ring keeps at least 3 stages, else 8
     p.R = 0;
+    const char* tpe = getenv("TFCUDA_GS_TP");  // 8 or 16 forces the pass width (read per call)
+    const int tp_force = tpe ? atoi(tpe) : 0;
     for (int tp : {16, 8}) {
+        if (tp_force && tp != tp_force) continue;
         const GsLayout L0 = gs_layout(p.K, 0, tp);
         const long long left = (long long)kGsSmemLimit - (long long)L0.total;
         const int R = (int)std::min<long long>(kGsMaxR, left / kGsStage);
