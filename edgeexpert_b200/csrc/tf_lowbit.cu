@@ -73,29 +73,41 @@ __device__ __forceinline__ void lb_pair_codes(int P, int& lo, int& hi, float& in
 
 // Stage nvec activation vectors x[v * x_stride + k] (fp16, K = 64 * ngK):
 // xs[(v * ngK + G) * kLbPairStride + P] = pair words, xc[v * ngK + G] =
-// {1024 * sum(staged halves), sum(x)}.  One warp per (vector, group), lane
-// = pair.
+// {1024 * sum(staged halves), sum(x)}.  One thread per (vector, group): the
+// group's 64 halves in registers (eight 16-byte loads when aligned), its 32
+// pair words and both sums without cross-lane reductions.
 template <int BITS>
 __device__ void lb_stage(const __half* __restrict__ x, int x_stride, int nvec, int ngK, uint32_t* xs, float2* xc,
-                         int warp, int lane, int nwarps) {
-    int lo, hi;
-    float il, ih;
-    lb_pair_codes<BITS>(lane, lo, hi, il, ih);
-    for (int vg = warp; vg < nvec * ngK; vg += nwarps) {
+                         int tid, int nthreads) {
+    const bool vec = ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) && (nvec == 1 || (x_stride & 7) == 0);
+    for (int vg = tid; vg < nvec * ngK; vg += nthreads) {
         const int v = vg / ngK, G = vg - v * ngK;
         const __half* xg = x + (size_t)v * x_stride + 64 * G;
-        const __half xl = xg[lo], xh = xg[hi];
-        const __half a = __hmul(xl, __float2half_rn(il));
-        const __half b = __hmul(xh, __float2half_rn(ih));
-        xs[vg * kLbPairStride + lane] = (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
-        float cs = __half2float(a) + __half2float(b);
-        float sx = __half2float(xl) + __half2float(xh);
+        __half xv[64];
+        if (vec) {
 #pragma unroll
-        for (int off = 16; off; off >>= 1) {
-            cs += __shfl_xor_sync(0xffffffffu, cs, off);
-            sx += __shfl_xor_sync(0xffffffffu, sx, off);
+            for (int q = 0; q < 8; ++q) {
+                const uint4 r = __ldg(reinterpret_cast<const uint4*>(xg) + q);
+                memcpy(&xv[8 * q], &r, 16);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 64; ++k) xv[k] = xg[k];
         }
-        if (lane == 0) xc[vg] = make_float2(1024.0f * cs, sx);
+        uint32_t* w = xs + vg * kLbPairStride;
+        float cs = 0.f, sx = 0.f;
+#pragma unroll
+        for (int P = 0; P < 32; ++P) {
+            int lo, hi;
+            float il, ih;
+            lb_pair_codes<BITS>(P, lo, hi, il, ih);
+            const __half a = __hmul(xv[lo], __float2half_rn(il));
+            const __half b = __hmul(xv[hi], __float2half_rn(ih));
+            w[P] = (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+            cs += __half2float(a) + __half2float(b);
+            sx += __half2float(xv[lo]) + __half2float(xv[hi]);
+        }
+        xc[vg] = make_float2(1024.0f * cs, sx);
     }
     __syncthreads();
 }
@@ -356,7 +368,7 @@ __global__ void __launch_bounds__(kLbThreads, 2) lb_gemv_kernel(const __grid_con
     float2* xc = reinterpret_cast<float2*>(xs + (size_t)p.ntok * ngK * kLbPairStride);
     float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xc) + (size_t)p.ntok * ngK * 8);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    lb_stage<BITS>(p.x, p.x_stride, p.ntok, ngK, xs, xc, warp, lane, kLbWarps);
+    lb_stage<BITS>(p.x, p.x_stride, p.ntok, ngK, xs, xc, tid, kLbThreads);
 
     const int tilesM = (p.M + 15) >> 4, per = kLbWarps / p.ks;
     const int tile = blockIdx.x * per + warp / p.ks, kp = warp % p.ks;
@@ -443,7 +455,7 @@ __global__ void __launch_bounds__(kLbThreads, 2) lb_phase1_kernel(const __grid_c
     float2* xc = reinterpret_cast<float2*>(xs + (size_t)ngK * kLbPairStride);
     float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xc) + (size_t)ngK * 8);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    lb_stage<BITS>(p.x, 0, 1, ngK, xs, xc, warp, lane, kLbWarps);
+    lb_stage<BITS>(p.x, 0, 1, ngK, xs, xc, tid, kLbThreads);
 
     const int tilesF = (p.F + 7) >> 3, per = kLbWarps / p.ks;
     const int tile = blockIdx.x * per + warp / p.ks, kp = warp % p.ks;
@@ -490,7 +502,7 @@ __global__ void __launch_bounds__(kLbThreads, 2) lb_phase2_kernel(const __grid_c
     float2* xc = reinterpret_cast<float2*>(xs + (size_t)p.top_k * ngK * kLbPairStride);
     float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xc) + (size_t)p.top_k * ngK * 8);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    lb_stage<BITS>(p.x, p.F, p.top_k, ngK, xs, xc, warp, lane, kLbWarps);
+    lb_stage<BITS>(p.x, p.F, p.top_k, ngK, xs, xc, tid, kLbThreads);
 
     const int d0 = blockIdx.x * 16, g = lane >> 2;
     const int dA = d0 + g, dB = d0 + g + 8;

@@ -76,14 +76,27 @@ __global__ void __launch_bounds__(kRtThreads) prefill_router_kernel(
         }
     }
     __syncthreads();
-    for (int i = warp; i < kRtTok * ng; i += blockDim.x / 32) {
+    // per (token, group) sum of the staged hi + lo terms: one thread per item
+    // (eight 16-byte loads of each half, started at a thread-dependent chunk
+    // so a quarter-warp reads distinct banks), no shuffle chains
+    for (int i = tid; i < kRtTok * ng; i += blockDim.x) {
         const int t = i / ng, g = i - t * ng;
-        const uint32_t a = xs[(2 * t) * ws + g * 32 + lane], b = xs[(2 * t + 1) * ws + g * 32 + lane];
-        const __half2 ha = *reinterpret_cast<const __half2*>(&a);
-        const __half2 hb = *reinterpret_cast<const __half2*>(&b);
-        float s = (__low2float(ha) + __low2float(hb)) + (__high2float(ha) + __high2float(hb));
-        for (int off = 16; off; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-        if (lane == 0) xsum[t * ng + g] = s;
+        const uint4* ha = reinterpret_cast<const uint4*>(xs + (2 * t) * ws + g * 32);
+        const uint4* hb = reinterpret_cast<const uint4*>(xs + (2 * t + 1) * ws + g * 32);
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int q = (k + i) & 7;
+            const uint4 a = ha[q], b = hb[q];
+            const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&wa[j]));
+                const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&wb[j]));
+                s += (fa.x + fb.x) + (fa.y + fb.y);
+            }
+        }
+        xsum[t * ng + g] = s;
     }
     __syncthreads();
 
