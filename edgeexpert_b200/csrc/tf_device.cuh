@@ -252,8 +252,9 @@ __host__ __device__ constexpr int x_words_stride(int K) {
     return ((K / 2 + 31) / 32) * 32 + 4;
 }
 
-// Per-group sums from the staged octet-pair words: one warp per (token,
-// group); the 32 words of a group hold its 64 values, one word per lane.
+// Per-group sums from the staged octet-pair words: one thread per (token,
+// group), reading the group's 32 words (64 values) as eight 16-byte loads
+// started at a thread-dependent chunk (distinct banks within a quarter-warp).
 // With `fold` the odd pairs (words 1 and 3 of each octet) hold x/16 (see
 // stage_words); then  xsum = true sum of x  and  xcorr = 1024 * (sum of the
 // staged values), the exact offset the folded MMA adds.  Callers synchronise
@@ -261,21 +262,23 @@ __host__ __device__ constexpr int x_words_stride(int K) {
 __device__ __forceinline__ void stage_xsum_smem(const uint32_t* xs, int ws, int ntok, int K, float* xsum,
                                                 float* xcorr, bool fold, int tid, int nthreads) {
     const int ng = K / kGroup;
-    const int warp = tid >> 5, lane = tid & 31, nw = nthreads >> 5;
-    for (int i = warp; i < ntok * ng; i += nw) {
+    for (int i = tid; i < ntok * ng; i += nthreads) {
         const int t = i / ng, g = i - t * ng;
-        const uint32_t w = xs[t * ws + g * 32 + lane];
-        const __half2 h = *reinterpret_cast<const __half2*>(&w);
-        float s = __low2float(h) + __high2float(h);
-        float odd = (fold && (lane & 1)) ? s : 0.f;
-        for (int off = 16; off; off >>= 1) {
-            s += __shfl_xor_sync(0xffffffffu, s, off);
-            odd += __shfl_xor_sync(0xffffffffu, odd, off);
+        const uint4* w = reinterpret_cast<const uint4*>(xs + t * ws + g * 32);
+        float ev = 0.f, od = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const uint4 v = w[(k + i) & 7];
+            const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+            const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+            const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&v.z));
+            const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&v.w));
+            ev += (a.x + a.y) + (c.x + c.y);
+            od += (b.x + b.y) + (d.x + d.y);
         }
-        if (lane == 0) {
-            xsum[t * ng + g] = s + 15.f * odd;
-            if (fold) xcorr[t * ng + g] = 1024.f * s;
-        }
+        const float s = ev + od;
+        xsum[t * ng + g] = fold ? s + 15.f * od : s;
+        if (fold) xcorr[t * ng + g] = 1024.f * s;
     }
 }
 
