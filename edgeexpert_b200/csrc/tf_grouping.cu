@@ -69,27 +69,54 @@ __global__ void __launch_bounds__(kSortMaxExperts) route_plan_kernel(
         order[pos] = (uint32_t)e;
     }
     __syncthreads();
+    // position i (thread i) in sort order: exclusive scans of the counts and of
+    // the non-empty flags give each expert's first pair and its group index
+    // (block scan: warp inclusive scans, then the earlier warps' totals)
+    __shared__ uint32_t wsum[kSortMaxExperts / 32], wnz[kSortMaxExperts / 32];
+    __shared__ uint32_t s_ng;
+    const int lane = e & 31, wid = e >> 5;
+    const uint32_t x = e < E ? order[e] : 0u;
+    const uint32_t tx = e < E ? tot[x] : 0u, nz = tx ? 1u : 0u;
+    uint32_t ia = tx, in = nz;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t va = __shfl_up_sync(0xffffffffu, ia, o), vn = __shfl_up_sync(0xffffffffu, in, o);
+        if (lane >= o) {
+            ia += va;
+            in += vn;
+        }
+    }
+    if (lane == 31) {
+        wsum[wid] = ia;
+        wnz[wid] = in;
+    }
+    __syncthreads();
+    uint32_t pa = 0, pn = 0;
+    for (int w = 0; w < wid; ++w) {
+        pa += wsum[w];
+        pn += wnz[w];
+    }
+    const uint32_t acc = pa + ia - tx, g = pn + in - nz;  // exclusive
+    if (e < E) {
+        start[x] = acc;
+        offsets[x] = tx ? acc : 0xFFFFFFFFu;
+        counts[x] = tx;
+        if (tx) {
+            groups[g] = tf_moe_group{x, acc, tx};
+            gidx[g] = x;
+        }
+    }
+    if (e == (E > 0 ? E - 1 : 0)) s_ng = E > 0 ? g + nz : 0u;
+    __syncthreads();
+    const uint32_t ng = s_ng;
+    const uint32_t nt = (ng + (uint32_t)tile_e - 1) / (uint32_t)tile_e;
+    for (uint32_t j = (uint32_t)e; j < nt; j += blockDim.x) {
+        const uint32_t g0 = j * (uint32_t)tile_e, g1 = min(ng, g0 + (uint32_t)tile_e);
+        const uint32_t ps = start[gidx[g0]];
+        const uint32_t pe = start[gidx[g1 - 1]] + tot[gidx[g1 - 1]];
+        tiles[j] = tf_moe_tile{g0, g1 - g0, ps, pe - ps};
+    }
     if (e == 0) {
-        uint32_t acc = 0, ng = 0;
-        for (int i = 0; i < E; ++i) {
-            const uint32_t x = order[i];
-            start[x] = acc;
-            offsets[x] = tot[x] ? acc : 0xFFFFFFFFu;
-            counts[x] = tot[x];
-            if (tot[x]) {
-                groups[ng] = tf_moe_group{x, acc, tot[x]};
-                gidx[ng] = x;
-                ++ng;
-            }
-            acc += tot[x];
-        }
-        uint32_t nt = 0;
-        for (uint32_t g0 = 0; g0 < ng; g0 += (uint32_t)tile_e) {
-            const uint32_t g1 = min(ng, g0 + (uint32_t)tile_e);
-            const uint32_t ps = start[gidx[g0]];
-            const uint32_t pe = start[gidx[g1 - 1]] + tot[gidx[g1 - 1]];
-            tiles[nt++] = tf_moe_tile{g0, g1 - g0, ps, pe - ps};
-        }
         *n_groups = ng;
         *n_tiles = nt;
     }
