@@ -238,6 +238,46 @@ __device__ __forceinline__ void stage_xc(const uint32_t* xs, int ws, int ntok, i
     }
 }
 
+// One ring stage (4 groups of 64 codes) of a consumer warp: rows A and B of
+// the warp x NB blocks of 8 tokens.  (A FULL variant without the G < ngK test
+// spilled registers and ran slower.)
+template <typename ST, int NB>
+__device__ __forceinline__ void gs_stage(const uint8_t* sbase, int offA, int offB, const uint32_t* xs, int ws,
+                                         const float2* xc, int TP, int st, int ngK, int g, int t, const uint2 scl[4],
+                                         float acc[2][4]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int G = 4 * st + j;
+        if (G >= ngK) break;
+        const int o = ((((j * 2 + (t >> 1)) ^ g) & 7) << 4) + (t & 1) * 8;
+        const uint2 wa = *reinterpret_cast<const uint2*>(sbase + offA + o);
+        const uint2 wb = *reinterpret_cast<const uint2*>(sbase + offB + o);
+        uint32_t pa0[4], pa1[4], pb0[4], pb1[4];
+        dq4_folded(wa.x, pa0);
+        dq4_folded(wa.y, pa1);
+        dq4_folded(wb.x, pb0);
+        dq4_folded(wb.y, pb1);
+        const float sa = scale_at<ST>(scl[0], j), ba = scale_at<ST>(scl[1], j);
+        const float sb = scale_at<ST>(scl[2], j), bb = scale_at<ST>(scl[3], j);
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            const uint4* xp = reinterpret_cast<const uint4*>(xs + (b * 8 + g) * ws + (G * 8 + 2 * t) * 4);
+            const uint4 x0 = xp[0], x1 = xp[1];
+            const float4 xv = *reinterpret_cast<const float4*>(xc + G * TP + b * 8 + 2 * t);
+            // the chain starts at -1024 * sum(staged x) and ends at the group's dot
+            float c[4] = {xv.x, xv.z, xv.x, xv.z};
+            mma16816(c, pa0[0], pb0[0], pa0[1], pb0[1], x0.x, x0.y);
+            mma16816(c, pa0[2], pb0[2], pa0[3], pb0[3], x0.z, x0.w);
+            mma16816(c, pa1[0], pb1[0], pa1[1], pb1[1], x1.x, x1.y);
+            mma16816(c, pa1[2], pb1[2], pa1[3], pb1[3], x1.z, x1.w);
+            acc[b][0] = fmaf(sa, c[0], fmaf(ba, xv.y, acc[b][0]));
+            acc[b][1] = fmaf(sa, c[1], fmaf(ba, xv.w, acc[b][1]));
+            acc[b][2] = fmaf(sb, c[2], fmaf(bb, xv.y, acc[b][2]));
+            acc[b][3] = fmaf(sb, c[3], fmaf(bb, xv.w, acc[b][3]));
+        }
+    }
+}
+
 template <typename ST>
 __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __grid_constant__ GsParams p) {
     extern __shared__ uint8_t gs_raw[];
@@ -380,56 +420,11 @@ __global__ void __launch_bounds__(kGsThreads, 1) grouped_stream_kernel(const __g
                 if (st + 1 < nst) load_scales<ST>(sA, bA, sB, bB, 4 * (st + 1), ngK, vec, nscl);
                 if (!(ok = gs_wait(&sh.full[slot], ph, sh.abort_flag, p.err, __LINE__))) break;
                 const uint8_t* sbase = ring + slot * kGsStage;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int G = 4 * st + j;
-                    if (G < ngK) {
-                        const int o = ((((j * 2 + (t >> 1)) ^ g) & 7) << 4) + (t & 1) * 8;
-                        const uint2 wa = *reinterpret_cast<const uint2*>(sbase + offA + o);
-                        const uint2 wb = *reinterpret_cast<const uint2*>(sbase + offB + o);
-                        uint32_t pa0[4], pa1[4], pb0[4], pb1[4];
-#if defined(GS_VARIANT) && GS_VARIANT == 1
-                        for (int k = 0; k < 4; ++k) { pa0[k] = wa.x >> k; pa1[k] = wa.y >> k; pb0[k] = wb.x >> k; pb1[k] = wb.y >> k; }
-#else
-                        dq4_folded(wa.x, pa0);
-                        dq4_folded(wa.y, pa1);
-                        dq4_folded(wb.x, pb0);
-                        dq4_folded(wb.y, pb1);
-#endif
-#pragma unroll
-                        for (int b = 0; b < 2; ++b) {
-                            if (b < nblk) {
-                                const uint4* xp =
-                                    reinterpret_cast<const uint4*>(xs + (b * 8 + g) * ws + (G * 8 + 2 * t) * 4);
-                                const uint4 x0 = xp[0], x1 = xp[1];
-                                const float4 xv = *reinterpret_cast<const float4*>(xc + G * TP + b * 8 + 2 * t);
-                                const float xs0 = xv.y, xs1 = xv.w;
-                                // the chain starts at -1024 * sum(staged x) and ends at the group's dot
-                                float c[4] = {xv.x, xv.z, xv.x, xv.z};
-#if defined(GS_VARIANT) && GS_VARIANT >= 2
-                                c[0] += __uint_as_float(pa0[0] ^ pb0[1] ^ x0.x ^ x1.w);
-                                c[1] += __uint_as_float(pa1[2] ^ pb1[3] ^ x0.z ^ x1.y);
-#else
-                                mma16816(c, pa0[0], pb0[0], pa0[1], pb0[1], x0.x, x0.y);
-                                mma16816(c, pa0[2], pb0[2], pa0[3], pb0[3], x0.z, x0.w);
-                                mma16816(c, pa1[0], pb1[0], pa1[1], pb1[1], x1.x, x1.y);
-                                mma16816(c, pa1[2], pb1[2], pa1[3], pb1[3], x1.z, x1.w);
-#endif
-                                const float sa = scale_at<ST>(scl[0], j), ba = scale_at<ST>(scl[1], j);
-                                const float sb = scale_at<ST>(scl[2], j), bb = scale_at<ST>(scl[3], j);
-#if defined(GS_VARIANT) && GS_VARIANT == 3
-                                acc[b][0] += c[0] + sa + ba;
-                                acc[b][1] += c[1] + sb + bb + xs0 + xs1;
-#else
-                                acc[b][0] = fmaf(sa, c[0], fmaf(ba, xs0, acc[b][0]));
-                                acc[b][1] = fmaf(sa, c[1], fmaf(ba, xs1, acc[b][1]));
-                                acc[b][2] = fmaf(sb, c[2], fmaf(bb, xs0, acc[b][2]));
-                                acc[b][3] = fmaf(sb, c[3], fmaf(bb, xs1, acc[b][3]));
-#endif
-                            }
-                        }
-                    }
-                }
+                // the block count as a template argument: no per-group test of it
+                if (nblk == 2)
+                    gs_stage<ST, 2>(sbase, offA, offB, xs, ws, xc, TP, st, ngK, g, t, scl, acc);
+                else
+                    gs_stage<ST, 1>(sbase, offA, offB, xs, ws, xc, TP, st, ngK, g, t, scl, acc);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sh.empty[slot]);
                 if (++slot == R) {
