@@ -816,10 +816,17 @@ def run_moe(a, rank, world, local_rank):
         g2.manual_seed(99 + 7 * rank + B)
         xs = torch.randn(R, L, Tm, D, device=dev, generator=g2).to(torch.float16)
         x_in = torch.empty(L, Tm, D, dtype=torch.float16, device=dev)
-        idx = torch.empty(L, Tm, TOPK, dtype=torch.int32, device=dev)
-        wts = torch.empty(L, Tm, TOPK, dtype=torch.float16, device=dev)
-        h2 = torch.empty(L, Tm, D, dtype=torch.float16, device=dev)
-        ys = torch.empty(L, Tm, D, dtype=torch.float16, device=dev)
+        def io_set():  # one step's routing and outputs: (idx, wts, h2, ys)
+            return (torch.empty(L, Tm, TOPK, dtype=torch.int32, device=dev),
+                    torch.empty(L, Tm, TOPK, dtype=torch.float16, device=dev),
+                    torch.empty(L, Tm, D, dtype=torch.float16, device=dev),
+                    torch.empty(L, Tm, D, dtype=torch.float16, device=dev))
+
+        idx, wts, h2, ys = idx0, wts0, h20, ys0 = io_set()
+        # end-to-end steps alternate two input/output sets, so one step's copies
+        # overlap the neighbouring steps' kernels
+        x_e2e = [x_in, torch.empty(L, Tm, D, dtype=torch.float16, device=dev)]
+        io_e2e = [io_set(), io_set()]
         sact = torch.empty(Tm, FS, dtype=torch.float16, device=dev)
         fused_b1 = world == 1 and B == 1
         xch = None
@@ -839,9 +846,10 @@ def run_moe(a, rank, world, local_rank):
         launches = 0
         side = torch.cuda.Stream(device=dev) if a.overlap_shared else None
 
-        def step(xx):
+        def step(xx, io=None):
             nonlocal launches
             launches = 0
+            idx, wts, h2, ys = io if io is not None else (idx0, wts0, h20, ys0)
             for l in range(L):
                 Lw, x = layers[l], xx[l]
                 if T and side is not None and not fused_b1:
@@ -875,6 +883,9 @@ def run_moe(a, rank, world, local_rank):
                     shared.encode(x, Lw.shared_gate, Lw.shared_up, Lw.shared_down, sact, ys[l], T, stream=stream)
                     launches += 3
 
+        def slot_args(r):  # ring slots 0..R-1, then the two end-to-end sets
+            return (xs[r],) if r < R else (x_e2e[r - R], io_e2e[r - R])
+
         # eager warm-up (kernel attributes, NCCL communicators), then one graph per ring slot + x_in
         torch.cuda.synchronize()
         barrier()
@@ -885,10 +896,10 @@ def run_moe(a, rank, world, local_rank):
         graphs = []
         use_graph = True
         try:
-            for r in range(R + 1):
+            for r in range(R + 2):
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=stream):
-                    step(xs[r] if r < R else x_in)
+                    step(*slot_args(r))
                 graphs.append(g)
         except Exception as exc:  # noqa: BLE001 -- fall back to eager launches, reported in the line
             use_graph = False
@@ -902,7 +913,7 @@ def run_moe(a, rank, world, local_rank):
             if use_graph:
                 graphs[r].replay()
             else:
-                step(xs[r] if r < R else x_in)
+                step(*slot_args(r))
 
         with torch.cuda.stream(stream):
             for i in range(a.warmup):
@@ -926,28 +937,55 @@ def run_moe(a, rank, world, local_rank):
         if clk_all is None:
             clk_all = clk
 
-        # end to end: each step's inputs H2D from pinned memory, outputs (h2, ys, routing) D2H
+        # end to end: each step's inputs H2D from pinned memory, outputs (h2, ys, routing) D2H.
+        # The copies run on two copy streams (in, out) and the steps alternate two
+        # device sets, so step i's input copy and step i-1's output copy overlap the
+        # neighbouring steps' kernels; every copy is inside the timed region (the
+        # copy streams start after the start event, the end event waits for both).
         h_in = torch.empty(L, Tm, D, dtype=torch.float16, pin_memory=True)
         h_in.copy_(xs[0].cpu())
-        h_h2 = torch.empty(L, Tm, D, dtype=torch.float16, pin_memory=True)
-        h_ys = torch.empty(L, Tm, D, dtype=torch.float16, pin_memory=True)
-        h_idx = torch.empty(L, Tm, TOPK, dtype=torch.int32, pin_memory=True)
+        h_out = [(torch.empty(L, Tm, D, dtype=torch.float16, pin_memory=True),
+                  torch.empty(L, Tm, D, dtype=torch.float16, pin_memory=True),
+                  torch.empty(L, Tm, TOPK, dtype=torch.int32, pin_memory=True)) for _ in range(2)]
+        cin, cout = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+
+        def e2e_steps(n):
+            done = [None, None]  # per set: its last step's kernels finished
+            freed = [None, None]  # per set: its last output copy finished
+            cin.wait_stream(stream)
+            cout.wait_stream(stream)
+            for i in range(n):
+                k = i & 1
+                xin, (ei, _, eh2, eys) = x_e2e[k], io_e2e[k]
+                if done[k] is not None:
+                    cin.wait_event(done[k])  # step i-2 no longer reads this input set
+                with torch.cuda.stream(cin):
+                    xin.copy_(h_in, non_blocking=True)
+                stream.wait_stream(cin)
+                if freed[k] is not None:
+                    stream.wait_event(freed[k])  # step i-2's outputs are on the host
+                run(R + k)
+                done[k] = torch.cuda.Event()
+                done[k].record(stream)
+                cout.wait_event(done[k])
+                with torch.cuda.stream(cout):
+                    hh2, hys, hidx = h_out[k]
+                    hh2.copy_(eh2, non_blocking=True)
+                    hys.copy_(eys, non_blocking=True)
+                    hidx.copy_(ei, non_blocking=True)
+                    freed[k] = torch.cuda.Event()
+                    freed[k].record(cout)
+            stream.wait_stream(cout)
+            stream.wait_stream(cin)
+
         with torch.cuda.stream(stream):
-            for _ in range(a.warmup):
-                x_in.copy_(h_in, non_blocking=True)
-                run(R)
-                h_h2.copy_(h2, non_blocking=True)
+            e2e_steps(max(2, a.warmup))
         torch.cuda.synchronize()
         barrier()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
             f0.record(stream)
-            for _ in range(steps):
-                x_in.copy_(h_in, non_blocking=True)
-                run(R)
-                h_h2.copy_(h2, non_blocking=True)
-                h_ys.copy_(ys, non_blocking=True)
-                h_idx.copy_(idx, non_blocking=True)
+            e2e_steps(steps)
             f1.record(stream)
         torch.cuda.synchronize()
         barrier()
@@ -1084,7 +1122,8 @@ def run_moe(a, rank, world, local_rank):
         "batches": {str(b): results[b] for b in batches},
         "tok_s": head["tok_s"],
         "e2e": {"value": head["tok_s_e2e"], "unit": "tok/s", "h2d_bytes_per_step": head["h2d_bytes_per_step"],
-                "d2h_bytes_per_step": head["d2h_bytes_per_step"]},
+                "d2h_bytes_per_step": head["d2h_bytes_per_step"],
+                "copies": "pinned host buffers; in/out copy streams, two device sets alternating"},
         "roofline": ({"bound": "hbm", "kernel": head["dominant_kernel"]["kernel"],
                       "achieved": head["dominant_kernel"]["achieved_gbs"], "peak": peak, "peak_source": peak_src,
                       "unit": "GB/s", "frac": head["dominant_kernel"]["achieved_gbs"] / peak, "traffic": None,
