@@ -279,6 +279,185 @@ __global__ void __launch_bounds__(kAttnThreads) attention_partial_kernel(
     }
 }
 
+// Split-KV pass 1, streaming form (head_dim 64/128/256, at most 4 query
+// heads per KV head): CTA (chunk, kv head, token) of 4 warps; a position's K
+// and V rows are read by HD/8 lanes (8 dims each), so a warp covers 32/(HD/8)
+// positions per step and keeps U steps of K and V rows (2U 16-byte loads per
+// lane) in flight.  Each lane keeps an online softmax (m, d, o[8]) per query
+// head over its positions: scores and values are read in one pass, with no
+// score array in shared memory.  Lanes of other positions and the 4 warps
+// are merged at the end: M = max m, d = sum d e^(m - M), o = sum o e^(m - M).
+// The partial (m, d, o) goes to the same workspace rows as the two-pass form.
+template <int HD, int G>
+__global__ void __launch_bounds__(128, 4) attention_stream_kernel(
+    const __half* __restrict__ q, long long ldq, const __half* __restrict__ K, const __half* __restrict__ V,
+    long long ld_seq, int nq, int nkv, int seq_len, int kv_start, int chunk_len, int chunks, float scale,
+    float* __restrict__ md, float* __restrict__ po) {
+    constexpr int LPP = HD / 8;     // lanes per position
+    constexpr int PPW = 32 / LPP;   // positions per warp step
+    constexpr int NW = 4;
+    constexpr int U = 4;            // warp steps in flight
+    constexpr int STEP = NW * PPW;  // positions per CTA step
+    __shared__ float s_m[NW][G], s_d[NW][G];
+    __shared__ __align__(16) float s_o[NW][G][HD];
+    const int c = blockIdx.x, kvh = blockIdx.y, t = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int sub = lane / LPP, li = lane - sub * LPP;
+    const int p0 = kv_start + c * chunk_len;
+    const int np = max(0, min(seq_len, p0 + chunk_len) - p0);
+
+    float qf[G][8];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(q + (long long)t * ldq + (long long)(kvh * G + g) * HD + li * 8);
+        const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float2 f = __half22float2(h[u]);
+            qf[g][2 * u] = f.x * scale;
+            qf[g][2 * u + 1] = f.y * scale;
+        }
+    }
+    float m[G], d[G], acc[G][8];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        m[g] = -INFINITY;
+        d[g] = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[g][e] = 0.f;
+    }
+    const long long pstride = (long long)nkv * HD;
+    const __half* Kt = K + (long long)t * ld_seq + (long long)kvh * HD + li * 8 + (long long)p0 * pstride;
+    const __half* Vt = V + (long long)t * ld_seq + (long long)kvh * HD + li * 8 + (long long)p0 * pstride;
+
+    for (int base = warp * PPW; base < np; base += U * STEP) {  // warp-uniform bound
+        uint4 kr[U], vr[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int j = base + sub + u * STEP;
+            kr[u] = make_uint4(0u, 0u, 0u, 0u);
+            vr[u] = kr[u];
+            if (j < np) {
+                kr[u] = __ldcs(reinterpret_cast<const uint4*>(Kt + (long long)j * pstride));
+                vr[u] = __ldcs(reinterpret_cast<const uint4*>(Vt + (long long)j * pstride));
+            }
+        }
+        float s[U][G];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const __half2* kh = reinterpret_cast<const __half2*>(&kr[u]);
+            float kf[8];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = __half22float2(kh[e]);
+                kf[2 * e] = f.x;
+                kf[2 * e + 1] = f.y;
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float v = 0.f;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v = fmaf(qf[g][e], kf[e], v);
+                s[u][g] = v;
+            }
+        }
+#pragma unroll
+        for (int o = LPP / 2; o; o >>= 1)
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int g = 0; g < G; ++g) s[u][g] += __shfl_xor_sync(0xffffffffu, s[u][g], o);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (base + sub + u * STEP >= np)
+#pragma unroll
+                for (int g = 0; g < G; ++g) s[u][g] = -INFINITY;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float mn = m[g];
+#pragma unroll
+            for (int u = 0; u < U; ++u) mn = fmaxf(mn, s[u][g]);
+            if (mn == -INFINITY) continue;  // nothing valid yet for this lane
+            const float corr = __expf(m[g] - mn);  // 0 when m is still -inf
+            float p[U];
+            float dsum = 0.f;
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                p[u] = __expf(s[u][g] - mn);
+                dsum += p[u];
+            }
+            d[g] = fmaf(d[g], corr, dsum);
+            m[g] = mn;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[g][e] *= corr;
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const __half2* vh = reinterpret_cast<const __half2*>(&vr[u]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __half22float2(vh[e]);
+                    acc[g][2 * e] = fmaf(p[u], f.x, acc[g][2 * e]);
+                    acc[g][2 * e + 1] = fmaf(p[u], f.y, acc[g][2 * e + 1]);
+                }
+            }
+        }
+    }
+    // merge the warp's position slots (lanes li, li + LPP, ...)
+#pragma unroll
+    for (int o = LPP; o < 32; o <<= 1) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const float mo = __shfl_xor_sync(0xffffffffu, m[g], o);
+            const float dd = __shfl_xor_sync(0xffffffffu, d[g], o);
+            const float mn = fmaxf(m[g], mo);
+            const float a = mn == -INFINITY ? 0.f : __expf(m[g] - mn);
+            const float b = mn == -INFINITY ? 0.f : __expf(mo - mn);
+            d[g] = d[g] * a + dd * b;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float ov = __shfl_xor_sync(0xffffffffu, acc[g][e], o);
+                acc[g][e] = acc[g][e] * a + ov * b;
+            }
+            m[g] = mn;
+        }
+    }
+    if (sub == 0) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float4* r = reinterpret_cast<float4*>(&s_o[warp][g][li * 8]);
+            r[0] = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
+            r[1] = make_float4(acc[g][4], acc[g][5], acc[g][6], acc[g][7]);
+            if (li == 0) {
+                s_m[warp][g] = m[g];
+                s_d[warp][g] = d[g];
+            }
+        }
+    }
+    __syncthreads();
+    // merge the warps in warp order and write the chunk's partial rows
+    for (int i = threadIdx.x; i < G * HD; i += NW * 32) {
+        const int g = i / HD, e = i - g * HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) M = fmaxf(M, s_m[w][g]);
+        float D = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < NW; ++w) {
+                const float sc = __expf(s_m[w][g] - M);
+                D = fmaf(s_d[w][g], sc, D);
+                O = fmaf(s_o[w][g][e], sc, O);
+            }
+        }
+        const long long row = ((long long)t * nq + kvh * G + g) * chunks + c;
+        po[row * HD + e] = O;
+        if (e == 0) {
+            md[row * 2] = M;
+            md[row * 2 + 1] = D;
+        }
+    }
+}
+
 // Split-KV pass 2: one CTA per (query head, token) merges the chunks:
 // M = max m_c, D = sum d_c e^(m_c - M), out = half(sum o_c e^(m_c - M) / D).
 __global__ void __launch_bounds__(kAttnThreads) attention_combine_kernel(const float* __restrict__ md,
@@ -620,6 +799,36 @@ int attn_chunks(const tf_context* ctx, int T, int nkv, int seq_len) {
     return std::max(min_chunks, std::max(1, want));
 }
 
+// The streaming form runs head_dim 64/128/256 with at most 4 query heads per
+// KV head (TFCUDA_ATTN=split forces the two-pass form, read per call).
+bool attn_streams(int G, int hd) {
+    const char* e = getenv("TFCUDA_ATTN");
+    if (e && strcmp(e, "split") == 0) return false;
+    return G >= 1 && G <= 4 && (hd == 64 || hd == 128 || hd == 256);
+}
+
+// Chunks per (token, KV head) for the streaming form: the fewest whose CTAs
+// fill the resident slots (4 CTAs per SM) to at least 90 % in their last
+// wave, with at least 32 positions per chunk.  Independent of the live
+// length except through that cap, so it never grows when kv_start does.
+int attn_stream_chunks(const tf_context* ctx, int T, int nkv, int seq_len) {
+    if (seq_len <= 0) return 1;
+    const long long slots = 4LL * ctx->num_sms, pairs = (long long)T * nkv;
+    const int maxc = std::max(1, (seq_len + 31) / 32);
+    int best = 1;
+    double best_eff = 0.0;
+    for (int c = 1; c <= std::min(maxc, 1024); ++c) {
+        const long long n = pairs * c;
+        const double eff = (double)n / (double)(((n + slots - 1) / slots) * slots);
+        if (eff >= 0.9) return c;
+        if (eff > best_eff + 1e-9) {
+            best_eff = eff;
+            best = c;
+        }
+    }
+    return best;
+}
+
 size_t attn_smem(int G, int hd) {
     return sizeof(float) * ((size_t)G * hd + (size_t)G * kAttnMaxChunk + (size_t)kAttnWarps * G * 256);
 }
@@ -682,7 +891,10 @@ tf_status tf_qkv_epilogue(tf_context* ctx, void* q, uint32_t q_stride, void* k, 
 size_t tf_attention_workspace_bytes(const tf_context* ctx, uint32_t T, uint32_t head_dim, uint32_t num_q_heads,
                                     uint32_t num_kv_heads, uint32_t seq_len) {
     if (!ctx || num_kv_heads == 0) return 0;
-    const int chunks = attn_chunks(ctx, (int)std::max(1u, T), (int)num_kv_heads, (int)seq_len);
+    const int G = (int)(num_q_heads / num_kv_heads);
+    const int chunks = attn_streams(G, (int)head_dim)
+                           ? attn_stream_chunks(ctx, (int)std::max(1u, T), (int)num_kv_heads, (int)seq_len)
+                           : attn_chunks(ctx, (int)std::max(1u, T), (int)num_kv_heads, (int)seq_len);
     return sizeof(float) * (size_t)T * num_q_heads * chunks * (head_dim + 2);
 }
 
@@ -707,13 +919,38 @@ tf_status tf_attention_decode(tf_context* ctx, const void* q, uint32_t q_stride,
     if (!aligned16(k_cache) || !aligned16(v_cache) || (seq_stride * 2) % 16 || !aligned4(workspace))
         return fail(ctx, TF_ERR_MISALIGNED, "%s: caches 16-byte aligned, sequence stride a multiple of 8", name);
     const int live = (int)(seq_len - kv_start);
-    const int chunks = attn_chunks(ctx, (int)T, (int)num_kv_heads, live);
+    const int G = (int)(num_q_heads / num_kv_heads);
+    const bool streams = attn_streams(G, (int)head_dim) && aligned16(q) && q_stride % 8 == 0;
+    const int chunks = streams ? attn_stream_chunks(ctx, (int)T, (int)num_kv_heads, live)
+                               : attn_chunks(ctx, (int)T, (int)num_kv_heads, live);
     const int chunk_len = live > 0 ? (live + chunks - 1) / chunks : 1;
     const size_t need = sizeof(float) * (size_t)T * num_q_heads * chunks * (head_dim + 2);
     if (workspace_bytes < need)
         return fail(ctx, TF_ERR_INVALID_ARG, "%s: workspace of %zu bytes, %zu needed (tf_attention_workspace_bytes)",
                     name, workspace_bytes, need);
-    const int G = (int)(num_q_heads / num_kv_heads);
+    float* md = static_cast<float*>(workspace);
+    float* po = md + (size_t)T * num_q_heads * chunks * 2;
+    cudaStream_t cs = static_cast<cudaStream_t>(stream);
+    if (streams) {
+        const dim3 grid(chunks, num_kv_heads, T);
+        const __half* qh = static_cast<const __half*>(q);
+        const __half* kc = static_cast<const __half*>(k_cache);
+        const __half* vc = static_cast<const __half*>(v_cache);
+#define TF_ATTN_STREAM(HD, GG)                                                                                    \
+    if ((int)head_dim == HD && G == GG)                                                                            \
+        attention_stream_kernel<HD, GG><<<grid, 128, 0, cs>>>(qh, q_stride, kc, vc, (long long)seq_stride,         \
+                                                              (int)num_q_heads, (int)num_kv_heads, (int)seq_len, \
+                                                              (int)kv_start, chunk_len, chunks, scale, md, po);
+        TF_ATTN_STREAM(64, 1) TF_ATTN_STREAM(64, 2) TF_ATTN_STREAM(64, 3) TF_ATTN_STREAM(64, 4)
+        TF_ATTN_STREAM(128, 1) TF_ATTN_STREAM(128, 2) TF_ATTN_STREAM(128, 3) TF_ATTN_STREAM(128, 4)
+        TF_ATTN_STREAM(256, 1) TF_ATTN_STREAM(256, 2) TF_ATTN_STREAM(256, 3) TF_ATTN_STREAM(256, 4)
+#undef TF_ATTN_STREAM
+        s = cuda_check(ctx, cudaGetLastError(), name);
+        if (s) return s;
+        attention_combine_kernel<<<dim3(num_q_heads, T), kAttnThreads, sizeof(float) * chunks, cs>>>(
+            md, po, (int)head_dim, (int)num_q_heads, chunks, static_cast<__half*>(out), out_stride);
+        return cuda_check(ctx, cudaGetLastError(), name);
+    }
     const size_t smem = attn_smem(G, (int)head_dim);
     static bool configured[64] = {};
     if (!configured[ctx->device & 63]) {
@@ -722,9 +959,6 @@ tf_status tf_attention_decode(tf_context* ctx, const void* q, uint32_t q_stride,
         if (e != cudaSuccess) return cuda_check(ctx, e, name);
         configured[ctx->device & 63] = true;
     }
-    float* md = static_cast<float*>(workspace);
-    float* po = md + (size_t)T * num_q_heads * chunks * 2;
-    cudaStream_t cs = static_cast<cudaStream_t>(stream);
     attention_partial_kernel<<<dim3(chunks, num_kv_heads, T), kAttnThreads, smem, cs>>>(
         static_cast<const __half*>(q), q_stride, static_cast<const __half*>(k_cache),
         static_cast<const __half*>(v_cache), (long long)seq_stride, (int)head_dim, (int)num_q_heads,

@@ -67,7 +67,9 @@ def test_qkv_epilogue(cuda, T, position):
 
 @pytest.mark.parametrize("T,nq,nkv,hd,seq,start", [(1, 16, 8, 256, 4096, 0), (1, 16, 8, 256, 1, 0),
                                                    (2, 16, 8, 256, 300, 0), (3, 8, 1, 128, 77, 5),
-                                                   (1, 4, 4, 512, 513, 0), (1, 16, 2, 64, 1000, 0)])
+                                                   (1, 4, 4, 512, 513, 0), (1, 16, 2, 64, 1000, 0),
+                                                   (4, 16, 4, 128, 2000, 7), (2, 8, 8, 64, 333, 0),
+                                                   (3, 12, 4, 256, 901, 900), (8, 16, 8, 256, 4096, 0)])
 def test_attention_decode(cuda, T, nq, nkv, hd, seq, start):
     """Split-KV attention (config 4: 16 query / 8 KV heads of 256 at 4096
     context) against the oracle's two-pass softmax in double."""
