@@ -77,7 +77,8 @@ struct GsLayout {
 };
 
 // [ring: R stages][token rows: TP x x_words_stride(K) words][per group and
-// token {1024 * sum(staged x), sum(x)}: K/64 x TP float2][barriers]
+// token pair {-1024 * sum(staged x) of both, sum(x) of both}: K/64 x TP/2
+// float4, so the epilogue's two tokens are one packed FMA operand][barriers]
 __host__ __device__ inline GsLayout gs_layout(int K, int R, int TP) {
     const int ngK = K / 64;
     GsLayout L;
@@ -234,8 +235,22 @@ __device__ __forceinline__ void stage_xc(const uint32_t* xs, int ws, int ntok, i
             od += (b.x + b.y) + (d.x + d.y);  // words 4q+1, 4q+3: odd pairs (staged / 16)
         }
         const float s = ev + od;
-        xc[G * TP + tk] = make_float2(-1024.f * s, s + 15.f * od);
+        // a token pair's four floats: {-1024 * sum_even_tok, -1024 * sum_odd_tok, sum_x even, sum_x odd}
+        float* xf = reinterpret_cast<float*>(xc) + (size_t)(G * TP + (tk & ~1)) * 2 + (tk & 1);
+        xf[0] = -1024.f * s;
+        xf[2] = s + 15.f * od;
     }
+}
+
+// d = a * b + c on two fp32 lanes at once (one packed FMA, sm_100)
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
 }
 
 // One ring stage (4 groups of 64 codes) of a consumer warp: rows A and B of
@@ -259,21 +274,28 @@ __device__ __forceinline__ void gs_stage(const uint8_t* sbase, int offA, int off
         dq4_folded(wb.y, pb1);
         const float sa = scale_at<ST>(scl[0], j), ba = scale_at<ST>(scl[1], j);
         const float sb = scale_at<ST>(scl[2], j), bb = scale_at<ST>(scl[3], j);
+        const float2 sa2 = make_float2(sa, sa), ba2 = make_float2(ba, ba);
+        const float2 sb2 = make_float2(sb, sb), bb2 = make_float2(bb, bb);
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
             const uint4* xp = reinterpret_cast<const uint4*>(xs + (b * 8 + g) * ws + (G * 8 + 2 * t) * 4);
             const uint4 x0 = xp[0], x1 = xp[1];
             const float4 xv = *reinterpret_cast<const float4*>(xc + G * TP + b * 8 + 2 * t);
             // the chain starts at -1024 * sum(staged x) and ends at the group's dot
-            float c[4] = {xv.x, xv.z, xv.x, xv.z};
+            float c[4] = {xv.x, xv.y, xv.x, xv.y};
             mma16816(c, pa0[0], pb0[0], pa0[1], pb0[1], x0.x, x0.y);
             mma16816(c, pa0[2], pb0[2], pa0[3], pb0[3], x0.z, x0.w);
             mma16816(c, pa1[0], pb1[0], pa1[1], pb1[1], x1.x, x1.y);
             mma16816(c, pa1[2], pb1[2], pa1[3], pb1[3], x1.z, x1.w);
-            acc[b][0] = fmaf(sa, c[0], fmaf(ba, xv.y, acc[b][0]));
-            acc[b][1] = fmaf(sa, c[1], fmaf(ba, xv.w, acc[b][1]));
-            acc[b][2] = fmaf(sb, c[2], fmaf(bb, xv.y, acc[b][2]));
-            acc[b][3] = fmaf(sb, c[3], fmaf(bb, xv.w, acc[b][3]));
+            const float2 sx = make_float2(xv.z, xv.w);
+            float2 a0 = ffma2(ba2, sx, make_float2(acc[b][0], acc[b][1]));
+            float2 a1 = ffma2(bb2, sx, make_float2(acc[b][2], acc[b][3]));
+            a0 = ffma2(sa2, make_float2(c[0], c[1]), a0);
+            a1 = ffma2(sb2, make_float2(c[2], c[3]), a1);
+            acc[b][0] = a0.x;
+            acc[b][1] = a0.y;
+            acc[b][2] = a1.x;
+            acc[b][3] = a1.y;
         }
     }
 }
