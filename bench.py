@@ -57,12 +57,14 @@ def parse():
     ap.add_argument("--overlap-shared", type=int, default=1,
                     help="moe: run each layer's shared expert on a forked stream beside the routed path (1) or after it (0)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--workload", choices=["moe", "decode", "gemv", "batched", "prefill", "ep"], default="moe",
+    ap.add_argument("--workload", choices=["moe", "decode", "gemv", "batched", "prefill", "ep", "attention"],
+                    default="moe",
                     help="moe (default) = config-4 MoE decode step at batch 256/32/1 through 30 layers, experts "
                          "sharded over the GPUs (plus, on one GPU, the batch-1 roofline and the config-0 GEMV); "
                          "decode = config 1 (batch 1, GB/s); gemv = config 0 (int4 GEMV 1408x2816 streamed from "
                          "HBM); batched = config 2 (64 tokens); prefill = config 3 (4096 tokens); ep = one layer "
-                         "of the expert-parallel batch")
+                         "of the expert-parallel batch; attention = config-4 decode attention of one layer "
+                         "(--tokens sequences, default 32, over a 4096-token fp16 KV cache)")
     ap.add_argument("--matrices", type=int, default=256, help="gemv: distinct weight matrices per step")
     ap.add_argument("--tokens", type=int, default=0, help="override the chunk's token count (batched/prefill)")
     return ap.parse_args()
@@ -1285,6 +1287,134 @@ def run_decoder_stack(a, rank, world, local_rank, moe_layers, dev, ctx, stream, 
     return out
 
 
+# ------------------------------------------------------ decode attention ----
+def attention_cpu_sample(seconds: float, threads: int | None = None):
+    """The oracle's split-KV attention (double precision) over one sequence
+    of the config-4 layer (16 query / 8 KV heads of 256, 4096 positions),
+    repeated for ~`seconds`; one sequence at a time (the oracle is scalar).
+    Returns (sequences/s, threads, sample text)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import numpy as np
+
+    import oracle as O
+    rng = np.random.default_rng(5)
+    K = rng.standard_normal((CONTEXT, 8, 256)).astype(np.float16).view(np.uint16)
+    V = rng.standard_normal((CONTEXT, 8, 256)).astype(np.float16).view(np.uint16)
+    q = (rng.standard_normal((16, 256)) * 0.08).astype(np.float16).view(np.uint16)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.attention_decode(q, K, V, 256, 16, 8, CONTEXT, 0, 1.0)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return n / el, 1, f"{n} sequences of 4096 positions x 8 KV heads x 256 through the oracle in {el:.1f} s"
+
+
+def run_attention(a, rank, world, local_rank):
+    """Config 4's decode attention alone: `--tokens` sequences (default 32)
+    at position 4095 over a 4096-token fp16 KV cache, 16 query / 8 KV heads
+    of dim 256 (tf_attention_decode: the split-KV partial kernel and the
+    chunk merge).  value = KV-cache bytes read per second; one layer's cache
+    (1.07 GB at 32 sequences) exceeds L2, so no flush is needed.  Replicas
+    at N > 1 (attention does not shard across GPUs)."""
+    import torch
+    import torch.distributed as dist
+
+    from edgeexpert_b200._lib import Context
+    from edgeexpert_b200.decoder import Attention
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    ctx = Context.get(local_rank)
+    B = a.tokens or 32
+    nq, nkv, hd = 16, 8, 256
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(91 + rank)
+    K = torch.randn(B, CONTEXT, nkv, hd, device=dev, generator=gen, dtype=torch.float32).to(torch.float16)
+    V = torch.randn(B, CONTEXT, nkv, hd, device=dev, generator=gen, dtype=torch.float32).to(torch.float16)
+    q = (torch.randn(B, nq * hd, device=dev, generator=gen) * 0.08).to(torch.float16)
+    out = torch.empty(B, nq * hd, dtype=torch.float16, device=dev)
+    att = Attention(context=ctx)
+    ws = torch.empty(att.workspace_bytes(B, hd, nq, nkv, CONTEXT) // 4 + 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(s, qq, oo):
+        att.encode(qq, K, V, oo, hd, nq, nkv, B, CONTEXT, ws, scale=hd ** -0.5, seq_stride=CONTEXT * nkv * hd,
+                   stream=s)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, a.warmup)):
+            step(stream, q, out)
+    torch.cuda.synchronize()
+    barrier()
+    clk = ClockSampler(local_rank)
+    clk.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(a.steps):
+        step(stream, q, out)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+    # end to end: q from pinned host memory, the attention output back, every step
+    h_q = torch.empty_like(q, device="cpu").pin_memory()
+    h_q.copy_(q.cpu())
+    h_out = torch.empty_like(out, device="cpu").pin_memory()
+    q_in, out_d = torch.empty_like(q), torch.empty_like(out)
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        f0.record(stream)
+        for _ in range(a.steps):
+            q_in.copy_(h_q, non_blocking=True)
+            step(stream, q_in, out_d)
+            h_out.copy_(out_d, non_blocking=True)
+        f1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = max_over_ranks(f0.elapsed_time(f1) / a.steps)
+    ctx.check_device(stream)
+    kv = 2 * B * CONTEXT * nkv * hd * 2
+    per_gpu = (kv + 2 * q.numel() * 2) / (ms * 1e-3) / 1e9
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs", 6650.0)
+    src = "measured hbm_gbs" if "hbm_gbs" in peaks else "fallback 6.65 TB/s"
+    if rank != 0:
+        return
+    line = {
+        "metric": "decode attention KV-cache GB/s (config 4 layer)", "value": per_gpu * world, "unit": "GB/s",
+        "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16-kv/fp32-acc", "data": "synthetic N(0,1) cache",
+        "config": {"workload": f"config-4 decode attention, {B} sequences x {CONTEXT} positions, 16q/8kv x 256",
+                   "parallelism": f"replicas{world}", "l2": "1.07 GB of cache per step at 32 sequences exceeds L2"},
+        "e2e": {"value": (kv + 2 * q.numel() * 2) / (ms_e2e * 1e-3) / 1e9 * world, "unit": "GB/s",
+                "h2d_bytes_per_step": q.numel() * 2, "d2h_bytes_per_step": out.numel() * 2},
+        "roofline": {"bound": "hbm", "kernel": "attention_stream_kernel + attention_combine_kernel",
+                     "achieved": per_gpu, "peak": peak, "peak_source": src, "unit": "GB/s", "frac": per_gpu / peak,
+                     "traffic": None, "bytes_per_launch": kv, "us_per_launch": ms * 1e3},
+        "gpu_launches": 2 * a.steps, "clocks": clocks,
+    }
+    if not a.no_cpu_baseline:
+        u, thr, txt = attention_cpu_sample(min(a.cpu_seconds, 10.0))
+        line["cpu_baseline"] = {"value": u * (kv / B) / 1e9, "unit": "GB/s", "cores": thr, "kind": "port",
+                                "sample": txt, "cpu_model": cpu_model()}
+    print(json.dumps(line), flush=True)
+
+
 # ------------------------------------------------------ chunk workloads ----
 CHUNK_TOKENS = {"batched": 64, "prefill": 4096}
 
@@ -1513,7 +1643,7 @@ def run_chunk(a, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
-DEFAULT_STEPS = {"moe": 50, "decode": 400, "gemv": 3000, "batched": 1000, "prefill": 300, "ep": 200}
+DEFAULT_STEPS = {"moe": 50, "decode": 400, "gemv": 3000, "batched": 1000, "prefill": 300, "ep": 200, "attention": 200}
 
 
 def main():
@@ -1541,6 +1671,8 @@ def main():
         run_gemv(a, rank, world, local_rank)
     elif a.workload == "ep":
         run_ep(a, rank, world, local_rank)
+    elif a.workload == "attention":
+        run_attention(a, rank, world, local_rank)
     else:
         run_chunk(a, rank, world, local_rank)
     if world > 1:
