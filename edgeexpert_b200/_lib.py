@@ -128,6 +128,8 @@ _PROTOS = {
                                   C.POINTER(AffineMatrix), _P, _P, _U32, _U32, _I, _P], _I),
     "tf_moe_grouped_routed": ([_P, _P, _U64, _U32, C.POINTER(ExpertOffsets), _P, _P, _P, _P, _U32, _P, _P, _U32,
                                _U32, _U32, _U32, _I, _P], _I),
+    "tf_moe_grouped_routed_expected": ([_P, _P, _U64, _U32, C.POINTER(ExpertOffsets), _P, _P, _P, _P, _U32, _P, _P,
+                                        _U32, _U32, _U32, _U32, _U32, _I, _P], _I),
     "tf_moe_reduce_token_major": ([_P, _P, _P, _P, _U32, _U32, _U32, _P], _I),
     "tf_rmsnorm": ([_P, _P, _U32, _P, _P, _U32, _U32, _U32, C.c_float, _P], _I),
     "tf_qkv_epilogue": ([_P, _P, _U32, _P, _P, _U64, _P, _P, _U32, _U32, _U32, _U32, _U32, C.c_float, _U32,

@@ -322,7 +322,13 @@ __global__ void ep_reduce_p2p_kernel(const float* __restrict__ back, const uint3
     }
 }
 
-constexpr int kEpCombineBlocks = 8;  // combine CTAs per sender (the reduce waits for this many)
+// Combine CTAs per sender (the sender's reduce waits for this many signals
+// from every owner): about two 16-byte items per thread, 8 to 128 CTAs.  A
+// function of the shape only, so every rank derives the same count.
+int ep_combine_blocks(uint32_t capacity, uint32_t d) {
+    const long long items = (long long)capacity * (d / 8);
+    return (int)std::max<long long>(8, std::min<long long>(128, (items + 511) / 512));
+}
 
 int grid_for(const tf_context* ctx, long long n) {
     return (int)std::max<long long>(1, std::min<long long>((n + 255) / 256, (long long)ctx->num_sms * 8));
@@ -498,7 +504,7 @@ tf_status tf_ep_combine_p2p(tf_context* ctx, const void* route_partials, const v
     if (!route_partials || !expert_ids || !weights || !peer_back || !peer_flags || !my_flags)
         return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
     if (!aligned16(route_partials)) return fail(ctx, TF_ERR_MISALIGNED, "%s: partials 16-byte aligned", name);
-    ep_combine_p2p_kernel<<<dim3(kEpCombineBlocks, world), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+    ep_combine_p2p_kernel<<<dim3(ep_combine_blocks(capacity, d), world), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __half*>(route_partials), static_cast<const uint32_t*>(expert_ids),
         static_cast<const __half*>(weights), (int)capacity, (int)top_k, (int)d, (int)rank,
         static_cast<float* const*>(peer_back), static_cast<uint32_t* const*>(peer_flags),
@@ -521,7 +527,7 @@ tf_status tf_ep_return_reduce_p2p(tf_context* ctx, const void* back, const void*
     const long long n = std::max<long long>(1, (long long)T * (d / 4));
     ep_reduce_p2p_kernel<<<grid_for(ctx, n), 256, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const float*>(back), static_cast<const uint32_t*>(my_flags), (int)world, (int)capacity, (int)T,
-        (int)d, kEpCombineBlocks, static_cast<__half*>(h2), (long long)h2_stride, ctx->d_err);
+        (int)d, ep_combine_blocks(capacity, d), static_cast<__half*>(h2), (long long)h2_stride, ctx->d_err);
     return cuda_check(ctx, cudaGetLastError(), name);
 }
 

@@ -1093,6 +1093,17 @@ tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64_t expe
                                 const void* n_groups, const void* hidden, uint32_t hidden_stride, void* act_scratch,
                                 void* route_partials, uint32_t t, uint32_t d, uint32_t f, uint32_t top_k,
                                 tf_scale_type st, void* stream) {
+    return tf_moe_grouped_routed_expected(ctx, pool, expert_stride, num_experts, off, sorted_pairs, groups, n_groups,
+                                          hidden, hidden_stride, act_scratch, route_partials, t, d, f, top_k, 0, st,
+                                          stream);
+}
+
+tf_status tf_moe_grouped_routed_expected(tf_context* ctx, const void* pool, uint64_t expert_stride,
+                                         uint32_t num_experts, const tf_expert_offsets* off, const void* sorted_pairs,
+                                         const void* groups, const void* n_groups, const void* hidden,
+                                         uint32_t hidden_stride, void* act_scratch, void* route_partials, uint32_t t,
+                                         uint32_t d, uint32_t f, uint32_t top_k, uint32_t expected_pairs,
+                                         tf_scale_type st, void* stream) {
     if (!ctx) return TF_ERR_INVALID_ARG;
     const char* name = "tf_moe_grouped_routed";
     if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, TF_ERR_CUDA, "cudaSetDevice failed");
@@ -1112,12 +1123,15 @@ tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64_t expe
         return fail(ctx, TF_ERR_MISALIGNED, "%s: activation pointers", name);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const uint32_t P = t * top_k;
+    // the pairs the groups are expected to hold: all t * top_k unless the
+    // caller knows better (expert parallelism: most slots are other ranks')
+    const uint32_t P_est = expected_pairs ? std::min(expected_pairs, P) : P;
     const uint8_t* pb = static_cast<const uint8_t*>(pool);
     // Few tokens per expert (batched decode): the streaming engine reads each
     // hit expert's weights once with up to 8 tokens per MMA column block; many
     // (prefill): the tcgen05 GEMMs.  TFCUDA_GROUPED=gemv|gemm forces one.
     const char* env = getenv("TFCUDA_GROUPED");
-    bool gemv = (uint64_t)P <= 24ull * num_experts;  // measured crossover with the tcgen05 GEMMs
+    bool gemv = (uint64_t)P_est <= 24ull * num_experts;  // measured crossover with the tcgen05 GEMMs
     bool engine = false;
     if (env && env[0] == 'g' && env[1] == 'e' && env[2] == 'm') gemv = env[3] == 'v';
     if (env && env[0] == 'e' && env[1] == 'n') gemv = engine = true;

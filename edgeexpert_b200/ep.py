@@ -74,6 +74,9 @@ class EPBuffers:
     ret: torch.Tensor       # fp32  [world*capacity, d]
     back: torch.Tensor      # fp32  [world*capacity, d]
     routes: object          # DeviceRoutes of the received rows
+    # local pairs the grouped experts should expect: each sender's tokens
+    # spread their K slots over every rank, so capacity * K (not rows * K)
+    expected_pairs: int = 0
 
 
 class CudaOps:
@@ -102,7 +105,7 @@ class CudaOps:
                          torch.empty(n, d, dtype=torch.float16, device=device),
                          torch.empty(rows, d, dtype=torch.float32, device=device),
                          torch.empty(rows, d, dtype=torch.float32, device=device),
-                         routes)
+                         routes, capacity * K)
 
     def dispatch_pack(self, hidden, expert_ids, weights, T, K, E, per_rank, world, capacity, send, stream=None):
         d = hidden.shape[1]
@@ -120,7 +123,8 @@ class CudaOps:
         d = pool.d
         route_sort(buf.ids, buf.w, rows, K, pool.num_experts, 16, stream=stream, context=self.ctx, out=buf.routes)
         PrefillGroupedRoutedMoE(self.ctx).encode(pool, buf.routes, recv, buf.act, buf.part, rows, K,
-                                                 hidden_stride=row_bytes(d) // 2, stream=stream)
+                                                 hidden_stride=row_bytes(d) // 2, stream=stream,
+                                                 expected_pairs=buf.expected_pairs)
         st = lib().tf_ep_expert_combine(self.ctx.handle, ptr(buf.part), ptr(buf.ids), ptr(buf.w), rows, K, d,
                                         ptr(buf.ret), stream_ptr(stream))
         self.ctx.check(st, "tf_ep_expert_combine")
@@ -253,7 +257,8 @@ class ExpertParallelMoE:
         from .prefill import PrefillGroupedRoutedMoE, route_sort
         route_sort(b.ids, b.w, rows, K, self.pool.num_experts, 16, stream=stream, context=ctx, out=b.routes)
         PrefillGroupedRoutedMoE(ctx).encode(self.pool, b.routes, x.recv, b.act, b.part, rows, K,
-                                            hidden_stride=row_bytes(d) // 2, stream=stream)
+                                            hidden_stride=row_bytes(d) // 2, stream=stream,
+                                            expected_pairs=b.expected_pairs)
         ctx.check(lib().tf_ep_combine_p2p(ctx.handle, ptr(b.part), ptr(b.ids), ptr(b.w), self.world, self.rank,
                                           self.capacity, K, d, ptr(x.peer_back), ptr(x.peer_flags),
                                           C.c_void_p(x.flags), sp), "tf_ep_combine_p2p")

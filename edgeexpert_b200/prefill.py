@@ -208,12 +208,13 @@ class PrefillGroupedRoutedMoE:
         self.ctx = context or Context.get(torch.cuda.current_device())
 
     def encode(self, experts, routes: "DeviceRoutes", hidden, act_scratch, route_partials, t: int, top_k: int,
-               hidden_stride: int = 0, stream=None):
-        from .quant import scale_type_of
-        st = lib().tf_moe_grouped_routed(
+               hidden_stride: int = 0, stream=None, expected_pairs: int = 0):
+        """`expected_pairs` (0: t * top_k) is the caller's estimate of the
+        pairs the groups hold; it only selects the kernel."""
+        st = lib().tf_moe_grouped_routed_expected(
             self.ctx.handle, ptr(experts.blob), experts.stride, experts.num_experts, C.byref(experts.offsets),
             ptr(routes.sorted_pairs), ptr(routes.groups), ptr(routes.n_groups), ptr(hidden), hidden_stride,
-            ptr(act_scratch), ptr(route_partials), t, experts.d, experts.f, top_k,
+            ptr(act_scratch), ptr(route_partials), t, experts.d, experts.f, top_k, expected_pairs,
             0 if experts.scale_dtype == _bf16() else 1, stream_ptr(stream))
         self.ctx.check(st, "PrefillGroupedRoutedMoE.encodeStreamedBatched")
 

@@ -350,6 +350,21 @@ TF_API tf_status tf_moe_grouped_routed(tf_context* ctx, const void* pool, uint64
                                        void* route_partials, uint32_t T, uint32_t d, uint32_t f, uint32_t top_k,
                                        tf_scale_type st, void* stream);
 
+/* tf_moe_grouped_routed with the caller's estimate of the pairs the groups
+ * hold (0: all T*top_k).  The estimate only picks the kernel (the grouped
+ * ring-streamed kernel up to 24 pairs per expert, the tcgen05 GEMMs above);
+ * results are the same either way.  For rows whose slots mostly belong to
+ * other ranks (expert parallelism: tf_ep_dispatch_unpack* marks them
+ * UINT32_MAX), T*top_k overstates the work by the number of ranks.  No
+ * reference counterpart beyond tf_moe_grouped_routed's. */
+TF_API tf_status tf_moe_grouped_routed_expected(tf_context* ctx, const void* pool, uint64_t expert_stride,
+                                                uint32_t num_experts, const tf_expert_offsets* offsets,
+                                                const void* sorted_pairs, const void* groups, const void* n_groups,
+                                                const void* hidden, uint32_t hidden_stride, void* act_scratch,
+                                                void* route_partials, uint32_t T, uint32_t d, uint32_t f,
+                                                uint32_t top_k, uint32_t expected_pairs, tf_scale_type st,
+                                                void* stream);
+
 /* PrefillMoE.encodeReduceTokenMajor (Sources/TurboFieldfare/Kernels/Prefill/MoE/PrefillMoE.swift:11-40;
  * prefill.metal:575-596): h2[t][i] = half(sum_r fma(w[t][r], partial[t*top_k+r][i])), rank order.
  * routing_weights fp16[T][top_k]; partials and h2 16-byte aligned, d % 8 == 0. */

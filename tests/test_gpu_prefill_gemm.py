@@ -195,6 +195,30 @@ def test_grouped_routed_and_reduce(cuda, T, K, E, D, F, st, path, monkeypatch):
     assert np.array_equal(f16(h2).reshape(-1), h2_ref)
 
 
+@pytest.mark.parametrize("expected", [0, 1024, 100000])
+def test_grouped_routed_expected_pairs(cuda, expected, monkeypatch):
+    """tf_moe_grouped_routed_expected: the pair estimate only picks the kernel
+    (T*K = 2048 pairs over 64 experts selects the tcgen05 GEMMs; an estimate
+    of 1024, as expert parallelism over 2 GPUs passes, the grouped
+    ring-streamed kernel; an estimate above T*K is clamped to it), and every
+    choice matches the oracle."""
+    monkeypatch.delenv("TFCUDA_GROUPED", raising=False)
+    T, K, E, D, F, st = 256, 8, 64, 2816, 704, 0
+    ex = Experts(E, D, F, st, f"g-{E}-{D}-{F}-{st}")
+    idx, w = skewed_routing(T, K, E, T + E)
+    X = O.seed_tree(T, f"gx-{D}").normal_f16(T * D).reshape(T, D)
+    pairs = PrefillRouter.make_token_expert_pairs(idx, w, T, K)
+    ref = O.group_pairs(pairs, T, K, E, 16)
+    part_ref = O.grouped_routed(ex.host.reshape(-1), ex.lay.stride, ex.off, ref["sorted"], X, D, D, F, K, T, st)
+    routes = route_sort(dev(idx.view(np.int32)), dev(w), T, K, E, 16)
+    act = torch.empty(T * K, F, dtype=torch.float16, device="cuda")
+    part = torch.empty(T * K, D, dtype=torch.float16, device="cuda")
+    PrefillGroupedRoutedMoE().encode(ex.pool(), routes, dev(X, torch.float16), act, part, T, K,
+                                     expected_pairs=expected)
+    torch.cuda.synchronize()
+    assert O.rel_error(O.f16_to_f32(f16(part)), O.f16_to_f32(part_ref)) < FP16_TOL
+
+
 @pytest.mark.parametrize("path", ["gemm", "gemv", "engine"])
 def test_grouped_routed_empty_routes(cuda, path, monkeypatch):
     """A route table with no groups runs no tile; T = 0 touches nothing."""
