@@ -174,57 +174,61 @@ __device__ __forceinline__ bool ep_wait_count(const uint32_t* cnt, uint32_t want
     return true;
 }
 
-// Dispatch: CTA (owner r, slot t) writes its row straight into rank r's
-// receive buffer at [my_rank][t], then signals recv_cnt[my_rank] on rank r.
-// The slot-0 CTA of each owner first resets this rank's back_cnt[r] (rank r
-// cannot answer before that CTA's signal arrives).
-__global__ void ep_dispatch_p2p_kernel(const __half* __restrict__ x, long long ldx, const uint32_t* __restrict__ ids,
-                                       const __half* __restrict__ w, int T, int K, int E, int per_rank, int cap, int d,
-                                       int my_rank, uint8_t* const* __restrict__ peer_recv,
-                                       uint32_t* const* __restrict__ peer_flags, uint32_t* my_flags, int world,
-                                       uint32_t* err) {
-    const int slot = blockIdx.x;
-    const int r = slot / cap, t = slot - r * cap;
-    const size_t row_bytes = (size_t)d * 2 + sizeof(tf_ep_row_header);
-    uint8_t* row = peer_recv[r] + ((size_t)my_rank * cap + t) * row_bytes;
-    __shared__ int s_n;
-    if (threadIdx.x == 0) {
-        if (t == 0) my_flags[(world + r) * kEpFlagStride] = 0u;  // back_cnt[r]
-        tf_ep_row_header h;
-        uint32_t n = 0;
-        for (int k = 0; k < 8; ++k) {
-            h.local_expert[k] = 0xFFFFFFFFu;
-            h.weight_bits[k] = 0;
-        }
-        if (t < T) {
-            for (int k = 0; k < K; ++k) {
-                const uint32_t e = ids[(size_t)t * K + k];
-                if (e >= (uint32_t)E) {
-                    if (err) atomicOr(err, kErrBadExpert);
-                    continue;
-                }
-                if ((int)(e / (uint32_t)per_rank) == r) {
-                    h.local_expert[k] = e - (uint32_t)(r * per_rank);
-                    h.weight_bits[k] = __half_as_ushort(w[(size_t)t * K + k]);
-                    ++n;
-                }
+// Dispatch: warp w of CTA (block b, owner r) takes slot t = 8b + w and writes
+// the token's row straight into rank r's receive buffer at [my_rank][t]
+// (lane k < top_k maps routing slot k; the header's fields are one lane
+// each); the CTA then signals recv_cnt[my_rank] on rank r by its slot count,
+// so rank r waits for cap.  CTA 0 of each owner first resets this rank's
+// back_cnt[r] (rank r cannot answer before that CTA's signal arrives).
+constexpr int kEpDispatchWarps = 8;
+__global__ void __launch_bounds__(32 * kEpDispatchWarps) ep_dispatch_p2p_kernel(
+    const __half* __restrict__ x, long long ldx, const uint32_t* __restrict__ ids, const __half* __restrict__ w,
+    int T, int K, int E, int per_rank, int cap, int d, int my_rank, uint8_t* const* __restrict__ peer_recv,
+    uint32_t* const* __restrict__ peer_flags, uint32_t* my_flags, int world, uint32_t* err) {
+    const int r = blockIdx.y;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * kEpDispatchWarps + warp;
+    if (blockIdx.x == 0 && threadIdx.x == 0) my_flags[(world + r) * kEpFlagStride] = 0u;  // back_cnt[r]
+    if (t < cap) {
+        const size_t row_bytes = (size_t)d * 2 + sizeof(tf_ep_row_header);
+        uint8_t* row = peer_recv[r] + ((size_t)my_rank * cap + t) * row_bytes;
+        uint32_t local = 0xFFFFFFFFu;
+        uint16_t wbits = 0;
+        if (t < T && lane < K) {
+            const uint32_t e = ids[(size_t)t * K + lane];
+            if (e >= (uint32_t)E) {
+                if (err) atomicOr(err, kErrBadExpert);
+            } else if ((int)(e / (uint32_t)per_rank) == r) {
+                local = e - (uint32_t)(r * per_rank);
+                wbits = __half_as_ushort(w[(size_t)t * K + lane]);
             }
         }
-        h.n_valid = n;
-        h.src_token = (uint32_t)t;
-        h.reserved[0] = h.reserved[1] = 0;
-        *reinterpret_cast<tf_ep_row_header*>(row + (size_t)d * 2) = h;
-        s_n = (int)n;
-    }
-    __syncthreads();
-    if (s_n) {
-        const uint4* src = reinterpret_cast<const uint4*>(x + (long long)t * ldx);
-        uint4* dst = reinterpret_cast<uint4*>(row);
-        for (int c = threadIdx.x; c < d / 8; c += blockDim.x) dst[c] = __ldg(src + c);
+        const uint32_t n = (uint32_t)__popc(__ballot_sync(0xffffffffu, local != 0xFFFFFFFFu));
+        tf_ep_row_header* h = reinterpret_cast<tf_ep_row_header*>(row + (size_t)d * 2);
+        if (lane < 8) {
+            h->local_expert[lane] = local;
+            h->weight_bits[lane] = wbits;
+        } else if (lane == 8) {
+            h->n_valid = n;
+        } else if (lane == 9) {
+            h->src_token = (uint32_t)t;
+        } else if (lane < 12) {
+            h->reserved[lane - 10] = 0;
+        }
+        if (n) {
+            const uint4* src = reinterpret_cast<const uint4*>(x + (long long)t * ldx);
+            uint4* dst = reinterpret_cast<uint4*>(row);
+            for (int c = lane; c < d / 8; c += 32) dst[c] = __ldg(src + c);
+        }
     }
     __threadfence_system();
     __syncthreads();
-    if (threadIdx.x == 0) ep_signal(peer_flags[r] + (size_t)my_rank * kEpFlagStride);  // recv_cnt[my_rank] on r
+    if (threadIdx.x == 0) {
+        const int nslots = min(kEpDispatchWarps, cap - (int)blockIdx.x * kEpDispatchWarps);
+        asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(peer_flags[r] + (size_t)my_rank * kEpFlagStride),
+                     "r"((uint32_t)nslots)
+                     : "memory");  // recv_cnt[my_rank] on r
+    }
 }
 
 // Owner side: wait until every sender's cap rows have landed, then the
@@ -469,7 +473,8 @@ tf_status tf_ep_dispatch_p2p(tf_context* ctx, const void* hidden, uint32_t hidde
         return fail(ctx, TF_ERR_INVALID_ARG, "%s: null pointer", name);
     if (T && (!aligned16(hidden) || !aligned4(expert_ids) || !aligned2(weights)))
         return fail(ctx, TF_ERR_MISALIGNED, "%s: hidden 16-byte aligned", name);
-    ep_dispatch_p2p_kernel<<<world * capacity, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+    const dim3 dgrid((capacity + kEpDispatchWarps - 1) / kEpDispatchWarps, world);
+    ep_dispatch_p2p_kernel<<<dgrid, 32 * kEpDispatchWarps, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const __half*>(hidden), hidden_stride, static_cast<const uint32_t*>(expert_ids),
         static_cast<const __half*>(weights), (int)T, (int)top_k, (int)num_experts, (int)experts_per_rank,
         (int)capacity, (int)d, (int)rank, static_cast<uint8_t* const*>(peer_recv),
