@@ -1107,6 +1107,11 @@ def run_moe(a, rank, world, local_rank):
             cpu["sample"] += f"; tok/s = layer-tokens/s / {L} layers"
     if rank != 0:
         return
+    # ncu DRAM bytes of the grouped gate/up + down pair per layer (one GPU, batch 256, all 128 experts hit)
+    gs_traffic = None
+    gs_tr = ROOT / "profiles" / "grouped_stream_traffic.json"
+    if world == 1 and head.get("tokens") == 256 and gs_tr.exists():
+        gs_traffic = json.loads(gs_tr.read_text()).get("bytes_per_launch")
     line = {
         "metric": METRIC, "value": head["tok_s"], "unit": "tok/s", "n_gpus": world, "steps": a.steps,
         "warmup": a.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True, "scaling": "strong",
@@ -1128,8 +1133,8 @@ def run_moe(a, rank, world, local_rank):
                 "copies": "pinned host buffers; in/out copy streams, two device sets alternating"},
         "roofline": ({"bound": "hbm", "kernel": head["dominant_kernel"]["kernel"],
                       "achieved": head["dominant_kernel"]["achieved_gbs"], "peak": peak, "peak_source": peak_src,
-                      "unit": "GB/s", "frac": head["dominant_kernel"]["achieved_gbs"] / peak, "traffic": None,
-                      "bytes_per_launch": head["dominant_kernel"]["bytes_per_layer"],
+                      "unit": "GB/s", "frac": head["dominant_kernel"]["achieved_gbs"] / peak,
+                      "traffic": gs_traffic, "bytes_per_launch": head["dominant_kernel"]["bytes_per_layer"],
                       "us_per_launch": head["dominant_kernel"]["us_per_layer"]}
                      if head.get("dominant_kernel") else None),
         "roofline_step": {"bound": "hbm", "kernel": "whole step per GPU (all kernels)",
@@ -1405,7 +1410,9 @@ def run_attention(a, rank, world, local_rank):
                 "h2d_bytes_per_step": q.numel() * 2, "d2h_bytes_per_step": out.numel() * 2},
         "roofline": {"bound": "hbm", "kernel": "attention_stream_kernel + attention_combine_kernel",
                      "achieved": per_gpu, "peak": peak, "peak_source": src, "unit": "GB/s", "frac": per_gpu / peak,
-                     "traffic": None, "bytes_per_launch": kv, "us_per_launch": ms * 1e3},
+                     "traffic": (1074024000 + 5156864) * B // 32 if B == 32 else None,
+                     "traffic_source": "profiles/attention_stream_kernel_ncu.md (32 sequences)",
+                     "bytes_per_launch": kv, "us_per_launch": ms * 1e3},
         "gpu_launches": 2 * a.steps, "clocks": clocks,
     }
     if not a.no_cpu_baseline:
