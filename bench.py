@@ -90,6 +90,12 @@ class ClockSampler:
                  "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # nvidia-smi takes a few hundred ms to start: wait (up to 3 s) for its first
+            # sample, so even a short timed region is covered
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 3.0 and self.proc.poll() is None:
+                time.sleep(0.01)
+            self.lines.clear()  # that sample predates the timed region; later ones arrive every 20 ms
         except (OSError, FileNotFoundError):
             self.proc = None
 
