@@ -1656,7 +1656,7 @@ def run_chunk(a, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
-DEFAULT_STEPS = {"moe": 50, "decode": 400, "gemv": 3000, "batched": 1000, "prefill": 300, "ep": 200, "attention": 200}
+DEFAULT_STEPS = {"moe": 50, "decode": 400, "gemv": 3000, "batched": 1000, "prefill": 300, "ep": 200, "attention": 2000}
 
 
 def main():
