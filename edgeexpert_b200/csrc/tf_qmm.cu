@@ -846,7 +846,11 @@ bool use_small_tiles(const tf_context* ctx, const QmmParams& p, bool pair) {
     bool small = p.small_tiles != 0;
     if (p.mode == kDensePlain || p.mode == kDenseGateUp) {
         const int fpt = (p.mode == kDenseGateUp ? kTM / 2 : kTM) * (pair ? 2 : 1);
-        small = p.T <= kTN && (long long)((p.nfeat + fpt - 1) / fpt) < ctx->num_sms / (pair ? 2 : 1);
+        // one 64-token tile; above that one 256-token tile, whose few feature
+        // tiles then split K over the idle SMs (T = 256 shared expert: 64-token
+        // tiles took 4 tiles x 44 k-blocks per CTA, 256-token tiles with a
+        // 4-way split 11 k-blocks; the batch-256 step 10.24 -> 9.83 ms)
+        small = p.T <= 64 && (long long)((p.nfeat + fpt - 1) / fpt) < ctx->num_sms / (pair ? 2 : 1);
     }
     const char* tn = getenv("TFCUDA_QMM_TN");
     if (tn) small = atoi(tn) == 64;
